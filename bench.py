@@ -1,0 +1,401 @@
+#!/usr/bin/env python3
+"""Decode benchmark of the B200 cirrus-s-1a path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (one "step"): one tau=1 decode step of one sequence at 32K context
+(cache holds 32767 tokens, the step appends the 32768th) with the benchmark
+shapes (d 768, vocab 32000, 9 GDN + 3 SWA self layers, 6 cross layers,
+12 q / 4 kv heads of 64, window 2048, indexer 4 x 64, top-k 512), random
+NVFP4 weights (seed 0) and a synthetic cache (bf16 K/V ~ N(0, 1), E4M3
+indexer keys of N(0, 1), GDN state ~ N(0, 0.1)).  Each step restores the
+position to 32767, so every timed step does exactly the 32K-context work.
+L2 is flushed (512 MB write) between timed steps, outside the timed region.
+
+One JSON line on rank 0:
+  value        tokens/s of all ranks, device-timed (CUDA events) graph replay
+  e2e          the same through the public DecodeGraph API with the token id
+               copied in from pinned host memory and the argmax token copied
+               back every step
+  roofline     the NVFP4 weight stream (every projection of a step, M = 1)
+               timed as its own CUDA graph: algorithmic bytes / time vs the
+               measured HBM copy bandwidth
+  step_roofline  the whole step's algorithmic bytes / step time
+  cpu_baseline the oracle restatement of the reference forward on the host
+               cores (rank 0, N = 1, a bounded number of 32K-context steps)
+
+``--impl reference`` times only that CPU restatement (rank 0) and prints its
+own line.  Multi-GPU: one process per GPU under torchrun; every rank decodes
+its own sequence (no collective on the data path), the timing is the max over
+ranks and ``value`` sums the ranks' tokens.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s (batch 1, τ=1, 32K ctx) per B200 + HBM GB/s vs 8 TB/s; box tok/s 1/2/4/8"
+PUBLISHED_TOK_S = 1815.0  # reference: decode tok/s at 32K, tau=1 (GB10, measured stream + roofline remainder)
+CTX = 32768
+FLUSH_BYTES = 512 << 20
+
+
+def _peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi samples of one GPU during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id, self.rows, self.proc = gpu_id, [], None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu_id}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) == 7:
+                self.rows.append(parts)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[3:]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def step_bytes(cfg, weight_bytes: float, ctx: int) -> dict:
+    """Algorithmic bytes of one tau=1 batch-1 decode step at context ``ctx``."""
+    H, dk, dv = cfg.gdn_heads, cfg.gdn_head_dim_k, cfg.gdn_head_dim_v
+    kinds = cfg.self_layer_kinds
+    n_gdn, n_swa = kinds.count("gdn"), kinds.count("swa")
+    C = 2 * H * dk + H * dv
+    kv_row = cfg.n_kv_heads * cfg.head_dim * 2  # bf16
+    return {
+        "weights": weight_bytes,
+        "gdn_state_rw": 2 * n_gdn * H * dk * dv * 4,
+        "conv_state_rw": 2 * n_gdn * (cfg.gdn_conv_size - 1) * C * 4,
+        "swa_kv": n_swa * min(ctx, cfg.swa_window) * 2 * kv_row,
+        "indexer_keys": ctx * cfg.indexer_dim,
+        "topk_kv_gather": min(ctx, cfg.sparse_topk + 1) * 2 * kv_row,
+    }
+
+
+def fill_cache(cache, ctx: int, seed: int) -> None:
+    import torch
+
+    g = torch.Generator(device=cache.kv_k.device).manual_seed(seed)
+    cache.gdn_state.normal_(0.0, 0.1, generator=g)
+    cache.gdn_conv.normal_(0.0, 1.0, generator=g)
+    for t in (cache.swa_k, cache.swa_v):
+        t.copy_(torch.randn(t.shape, generator=g, device=t.device).to(torch.bfloat16))
+    for t in (cache.kv_k, cache.kv_v):
+        t[:, :ctx].copy_(torch.randn(t[:, :ctx].shape, generator=g, device=t.device).to(torch.bfloat16))
+    di = cache.model.cfg.indexer_dim
+    ik = torch.randn((cache.batch, ctx, di), generator=g, device=cache.kv_ik.device).to(torch.float8_e4m3fn)
+    cache.kv_ik[:, :ctx, :di].copy_(ik.view(torch.uint8))
+    cache.pos_dev.fill_(ctx - 1)
+    cache.pos_host = [ctx - 1] * cache.batch
+
+
+def weight_stream_graph(eng):
+    """CUDA graph of one M=1 GEMV per projection matrix of the model (the
+    reference's "decode-step weight stream", configs[1])."""
+    import ctypes as C
+
+    import torch
+
+    from cirrus_s_1a_b200 import _lib
+    from cirrus_s_1a_b200.engine import PackedMatrix
+
+    mats = [m for m in eng.model._keep if isinstance(m, PackedMatrix)]
+    dev = eng.device
+    kmax = max(m.k for m in mats)
+    x = torch.randn(1, kmax, device=dev)
+    y = torch.empty(max(m.rows for m in mats), device=dev)
+    structs = [m.struct() for m in mats]
+    L = _lib.lib()
+    side = torch.cuda.Stream(dev)
+
+    def run(st):
+        for s in structs:
+            _lib.check(L.cb_gemv_nvfp4(C.byref(s), x.data_ptr(), s.k, 1, y.data_ptr(), s.rows, s.rows, st), "gemv")
+
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        run(side.cuda_stream)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            run(side.cuda_stream)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    real = sum(m.real_bytes for m in mats)
+    return g, len(structs), real
+
+
+def cpu_baseline(cfg, sd, cache, ctx: int, budget_s: float, max_steps: int) -> dict:
+    """Oracle (the reference forward restated on the CPU) decode steps at ``ctx``."""
+    import torch
+
+    from oracle import model as om
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    p = om.quantized_params(sd)
+    ref = cache.to_reference()
+    oc = om.OracleCache(ref["layers"], ref["shared"], ref["pos"])
+    ids = torch.tensor([[17]])
+    om.forward(p, cfg, ids, cache=oc, n_logits=1, casts=om.B200)  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while n < max_steps and (n == 0 or time.perf_counter() - t0 < budget_s):
+        om.forward(p, cfg, ids, cache=oc, n_logits=1, casts=om.B200)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{n} oracle decode steps (batch 1, tau=1) at ctx {ctx}, torch CPU fp32, "
+                      f"{threads} threads, {dt:.1f} s"}
+
+
+def run_reference(args, rank: int) -> None:
+    if rank != 0:
+        return
+    import torch
+
+    from cirrus_s_1a_b200 import synthetic
+    from cirrus_s_1a_b200.config import baseline_config
+    from oracle import model as om
+
+    cfg = baseline_config()
+    sd = synthetic.random_state_dict(cfg, seed=0)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    p = om.quantized_params(sd)
+    # synthetic 32K cache built directly in the reference Cache layout (CPU)
+    g = torch.Generator().manual_seed(1)
+    H, dk, dv, KC = cfg.gdn_heads, cfg.gdn_head_dim_k, cfg.gdn_head_dim_v, cfg.gdn_conv_size
+    C = 2 * H * dk + H * dv
+    n = CTX - 1
+    layers = []
+    for kind in cfg.self_layer_kinds:
+        if kind == "gdn":
+            layers.append({"conv": torch.randn(1, KC - 1, C, generator=g), "S": torch.randn(1, H, dk, dv, generator=g) * 0.1})
+        else:
+            shp = (1, cfg.swa_window, cfg.n_kv_heads, cfg.head_dim)
+            layers.append({"k": torch.randn(shp, generator=g).bfloat16().float(),
+                           "v": torch.randn(shp, generator=g).bfloat16().float()})
+    shp = (1, n, cfg.n_kv_heads, cfg.head_dim)
+    shared = {"k": torch.randn(shp, generator=g).bfloat16().float(), "v": torch.randn(shp, generator=g).bfloat16().float(),
+              "ik": torch.randn(1, n, cfg.indexer_dim, generator=g).to(torch.float8_e4m3fn).float()}
+    oc = om.OracleCache(layers, shared, n)
+    ids = torch.tensor([[17]])
+    for _ in range(args.warmup):
+        om.forward(p, cfg, ids, cache=oc, n_logits=1, casts=om.B200)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        om.forward(p, cfg, ids, cache=oc, n_logits=1, casts=om.B200)
+        times.append(time.perf_counter() - t0)
+    tot = sum(times)
+    value = args.steps / tot
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": value / PUBLISHED_TOK_S, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "cirrus-s-1a decode step, batch 1, tau=1, ctx 32768 (benchmark shapes, "
+                                   "random NVFP4 fake-quantised weights seed 0, synthetic cache)",
+                       "batch": 1, "ctx": CTX},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                             "sample": f"{args.steps} oracle decode steps at ctx {CTX} (torch CPU fp32, "
+                                       f"{threads} threads)"},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--cpu-budget-s", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch
+
+    from cirrus_s_1a_b200 import _lib, synthetic
+    from cirrus_s_1a_b200.config import baseline_config
+    from cirrus_s_1a_b200.engine import CirrusB200, DecodeGraph
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=dev)
+    cfg = baseline_config()
+    sd = synthetic.random_state_dict(cfg, seed=0)
+    eng = CirrusB200(cfg, sd, device=dev, max_ctx=CTX + 64)
+    cache = eng.new_cache(1)
+    fill_cache(cache, CTX, seed=1 + rank)
+
+    L = _lib.lib()
+    n0 = L.cb_launch_count()
+    graph = DecodeGraph(eng, cache, T=1, n_logits=1, want_logits=False)
+    launches_per_step = (L.cb_launch_count() - n0) // 2  # warm-up launch + captured launch
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    tok = torch.tensor([[17]], dtype=torch.int64)
+
+    def reset():
+        cache.pos_dev.fill_(CTX - 1)
+        cache.pos_host = [CTX - 1]
+        flush.random_(0, 255)
+
+    # ------------------------------------------------ device-timed steps
+    graph.ids.copy_(tok)
+    for _ in range(args.warmup):
+        reset()
+        graph.replay()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    gpu_uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    sampler = ClockSampler(gpu_uuid if gpu_uuid.startswith("GPU-") else f"GPU-{gpu_uuid}")
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    for i in range(args.steps):
+        reset()
+        torch.cuda.nvtx.range_push("cb_step")
+        evs[i][0].record(stream)
+        graph.replay()
+        evs[i][1].record(stream)
+        torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    if world > 1:
+        torch.distributed.barrier()
+    t_steps = [a.elapsed_time(b) for a, b in evs]
+    t_total_ms = sum(t_steps)
+
+    # ------------------------------------------------ end to end (public API)
+    ids_host = torch.tensor([[17]], dtype=torch.int64).pin_memory()
+    out_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+    e2e_ms = []
+    for i in range(args.warmup + args.steps):
+        reset()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        graph.ids.copy_(ids_host, non_blocking=True)
+        graph.replay()
+        out_host.copy_(graph.argmax.view(-1), non_blocking=True)
+        b.record(stream)
+        b.synchronize()
+        ids_host[0, 0] = int(out_host[0])  # the next step consumes the token just produced
+        if i >= args.warmup:
+            e2e_ms.append(a.elapsed_time(b))
+    e2e_total = sum(e2e_ms)
+
+    # ------------------------------------------------ weight stream roofline
+    wgraph, n_mats, wbytes = weight_stream_graph(eng)
+    w_ms = []
+    for i in range(args.warmup + args.steps):
+        flush.random_(0, 255)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        wgraph.replay()
+        b.record(stream)
+        b.synchronize()
+        if i >= args.warmup:
+            w_ms.append(a.elapsed_time(b))
+
+    tot = torch.tensor([t_total_ms, e2e_total], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(tot, op=torch.distributed.ReduceOp.MAX)
+    t_total_ms, e2e_total = float(tot[0]), float(tot[1])
+    peaks = _peaks()
+    w_avg_s = statistics.mean(w_ms) * 1e-3
+    sb = step_bytes(cfg, float(eng.model.weight_real_bytes), CTX)
+    step_total = sum(sb.values())
+    ms_step = t_total_ms / args.steps
+    value = world * args.steps / (t_total_ms * 1e-3)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": value / PUBLISHED_TOK_S, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "cirrus-s-1a decode step, batch 1, tau=1, ctx 32768 (benchmark shapes, random "
+                               "NVFP4 weights seed 0, synthetic cache), one CUDA graph per step",
+                   "batch_per_gpu": 1, "ctx": CTX, "weights": "nvfp4 (e2m1 + e4m3/16 + f32)",
+                   "kv": "bf16", "indexer_keys": "e4m3", "l2": "flushed between timed steps (512 MB write)",
+                   "parallelism": f"replicas x{world} (independent sequences)"},
+        "roofline": {"bound": "hbm", "kernel": f"gemv_nvfp4 weight stream ({n_mats} launches, M=1)",
+                     "achieved": wbytes / w_avg_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": wbytes / w_avg_s / 1e9 / peaks["hbm_gbs"], "traffic": None,
+                     "bytes": wbytes, "us": w_avg_s * 1e6, "peak_source": peaks["source"]},
+        "step_roofline": {"bound": "hbm", "bytes": step_total, "parts": sb,
+                          "achieved": step_total / (ms_step * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                          "frac": step_total / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"]},
+        "e2e": {"value": world * args.steps / (e2e_total * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                "d2h_bytes_per_step": 4, "ms_per_step": e2e_total / args.steps},
+        "gpu_launches": launches_per_step * args.steps,
+        "launches_per_step": launches_per_step,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, sd, cache, CTX, args.cpu_budget_s, 50)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph, wgraph
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,123 @@
+"""ctypes binding of ``libcirrus_b200.so`` (the C ABI of ``include/cirrus_b200.h``).
+
+The library is loaded from this package directory only.  Importing this
+module never builds anything; a missing library is an error, never a
+fallback: there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libcirrus_b200.so")
+
+CB_MAX_SELF = 32
+CB_MAX_CROSS = 16
+CB_MAX_T = 8
+CB_TILE_ROWS = 16
+CB_SWA_EXTRA = 16
+CB_LAYER_GDN, CB_LAYER_SWA = 0, 1
+
+STATUS = {0: "ok", 1: "invalid argument", 2: "shape not supported", 3: "CUDA launch failed",
+          4: "workspace too small", 5: "context full (position >= max_ctx)", 6: "token id outside the vocabulary"}
+
+EXPORTS = ("cb_abi_version", "cb_status_string", "cb_nvfp4_quantize", "cb_nvfp4_pack_tiles", "cb_gemv_nvfp4",
+           "cb_embed", "cb_argmax", "cb_gdn_step", "cb_indexer_topk", "cb_workspace_bytes", "cb_forward",
+           "cb_read_status", "cb_clear_status", "cb_launch_count")
+
+P = C.c_void_p
+I32 = C.c_int32
+
+
+class CbMatrix(C.Structure):
+    _fields_ = [("tiles", P), ("tile_scale", P), ("rows", I32), ("k", I32)]
+
+
+class CbSelfLayer(C.Structure):
+    _fields_ = [("kind", I32), ("slot", I32), ("norm1", P), ("norm2", P), ("in_proj", CbMatrix),
+                ("o_proj", CbMatrix), ("gate_up", CbMatrix), ("down", CbMatrix), ("conv_w", P), ("A_log", P),
+                ("dt_bias", P), ("o_norm", P), ("q_norm", P), ("k_norm", P)]
+
+
+class CbCrossLayer(C.Structure):
+    _fields_ = [("norm1", P), ("norm2", P), ("q_gate", CbMatrix), ("o_proj", CbMatrix), ("gate_up", CbMatrix),
+                ("down", CbMatrix), ("q_norm", P)]
+
+
+class CbModel(C.Structure):
+    _fields_ = [
+        ("d_model", I32), ("vocab_size", I32), ("n_self_layers", I32), ("n_cross_layers", I32),
+        ("gdn_heads", I32), ("gdn_dk", I32), ("gdn_dv", I32), ("conv_size", I32),
+        ("n_q_heads", I32), ("n_kv_heads", I32), ("head_dim", I32), ("rot_dim", I32),
+        ("swa_window", I32), ("sparse_topk", I32),
+        ("indexer_heads", I32), ("indexer_dim", I32), ("ffn_hidden", I32),
+        ("norm_eps", C.c_float),
+        ("inv_freq", P),
+        ("gdn_off_gate", I32), ("gdn_off_a", I32), ("gdn_off_b", I32),
+        ("swa_off_kv", I32), ("swa_off_gate", I32),
+        ("sh_off_ik", I32), ("sh_off_iq", I32), ("sh_off_iw", I32),
+        ("cr_off_gate", I32),
+        ("self_layers", CbSelfLayer * CB_MAX_SELF),
+        ("shared_norm", P), ("shared_k_norm", P), ("shared_proj", CbMatrix),
+        ("cross_layers", CbCrossLayer * CB_MAX_CROSS),
+        ("final_norm", P), ("lm_head", CbMatrix),
+    ]
+
+
+class CbCache(C.Structure):
+    _fields_ = [("batch", I32), ("max_ctx", I32), ("swa_slots", I32), ("n_gdn", I32), ("n_swa", I32),
+                ("pos", P), ("gdn_state", P), ("gdn_conv", P), ("swa_k", P), ("swa_v", P), ("kv_k", P),
+                ("kv_v", P), ("kv_ik", P)]
+
+
+class CbError(RuntimeError):
+    pass
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """The loaded library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise CbError(f"{LIB_PATH} is missing: build it with `python -m cirrus_s_1a_b200.build` "
+                          "(there is no CPU fallback)")
+        L = C.CDLL(LIB_PATH)
+        L.cb_abi_version.restype = C.c_int
+        L.cb_status_string.restype = C.c_char_p
+        L.cb_status_string.argtypes = [C.c_int]
+        L.cb_nvfp4_quantize.argtypes = [P, I32, I32, C.c_float, P, P, P]
+        L.cb_nvfp4_pack_tiles.argtypes = [P, P, I32, I32, P, P]
+        L.cb_gemv_nvfp4.argtypes = [C.POINTER(CbMatrix), P, I32, I32, P, I32, I32, P]
+        L.cb_embed.argtypes = [C.POINTER(CbMatrix), P, I32, P, P, P]
+        L.cb_argmax.argtypes = [P, I32, I32, I32, P, P]
+        L.cb_gdn_step.argtypes = [C.POINTER(CbModel), I32, P, I32, I32, I32, P, C.c_int64, P, C.c_int64, P, I32, P]
+        L.cb_indexer_topk.argtypes = [P, P, I32, P, I32, I32, I32, P, P, I32, I32, P, P, P, P]
+        L.cb_workspace_bytes.restype = C.c_size_t
+        L.cb_workspace_bytes.argtypes = [C.POINTER(CbModel), I32, I32, I32]
+        L.cb_forward.argtypes = [C.POINTER(CbModel), C.POINTER(CbCache), P, C.c_size_t, P, I32, I32, P, P, P, P]
+        L.cb_read_status.argtypes = [P, C.POINTER(I32), P]
+        L.cb_clear_status.argtypes = [P, P]
+        L.cb_launch_count.restype = C.c_int64
+        L.cb_launch_count.argtypes = []
+        for name in EXPORTS:
+            if name not in ("cb_status_string", "cb_workspace_bytes", "cb_launch_count"):
+                getattr(L, name).restype = C.c_int
+        if L.cb_abi_version() != 1:
+            raise CbError("libcirrus_b200.so ABI version mismatch")
+        _lib = L
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise CbError(f"{what}: {STATUS.get(rc, 'error')} (code {rc})")
+
+
+def ptr(t) -> int | None:
+    """Device pointer of a tensor (None for None)."""
+    return None if t is None else t.data_ptr()

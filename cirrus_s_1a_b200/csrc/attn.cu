@@ -1,0 +1,324 @@
+// Attention kernels of the decode step.
+//
+//  head_prep   q/k RMSNorm + partial interleaved RoPE, bf16 K/V cache append,
+//              E4M3 indexer-key append        (layers.py:227-235, 265-279)
+//  swa_attn    sliding-window attention over the ring, split over key ranges
+//  swa_combine merges the splits, applies the sigmoid head gate (layers.py:243)
+//  cross_attn  cross-decoder attention over the selected shared-KV rows
+//              (layers.py:325-331) with the q norm/RoPE and head gate fused in
+#include <algorithm>
+
+#include "attn.cuh"
+#include "common.cuh"
+
+namespace cb {
+
+// ------------------------------------------------------------- head prep
+__global__ void __launch_bounds__(256) head_prep_kernel(HeadPrepParams p) {
+  const int r = blockIdx.x, b = r / p.T, t = r % p.T;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int position = p.pos[b] + p.c0 + t;
+  // a position outside the cache (context full, or a corrupted pos) writes nothing
+  const bool linear_full = position < 0 || (!p.ring && position >= p.slots);
+  if (linear_full && threadIdx.x == 0) set_status(p.status, CB_ERR_CTX_FULL);
+  const int slot = position < 0 ? 0 : (p.ring ? position % p.slots : position);
+  const float* row = p.proj + (int64_t)r * p.ldp;
+  const int items = p.Hq + 2 * p.Hkv + (p.Di > 0 ? 1 : 0);
+  const int npairs = p.hd / 2;
+  for (int it = warp; it < items; it += 8) {
+    if (it < p.Hq + p.Hkv) {
+      const bool is_q = it < p.Hq;
+      const int hh = is_q ? it : it - p.Hq;
+      const float* x = row + (is_q ? p.off_q : p.off_k) + hh * p.hd;
+      const float* nw = is_q ? p.q_norm : p.k_norm;
+      float ss = 0.0f;
+      for (int j = lane; j < npairs; j += 32) ss += x[2 * j] * x[2 * j] + x[2 * j + 1] * x[2 * j + 1];
+      ss = warp_sum(ss);
+      const float rn = rsqrtf(ss / (float)p.hd + p.eps);
+      for (int j = lane; j < npairs; j += 32) {
+        float x1 = x[2 * j] * rn * nw[2 * j];
+        float x2 = x[2 * j + 1] * rn * nw[2 * j + 1];
+        if (j < p.rot2) rope_pair(x1, x2, position, p.inv_freq[j]);
+        if (is_q) {
+          float* q = p.qout + (int64_t)r * p.ldq + hh * p.hd;
+          q[2 * j] = x1;
+          q[2 * j + 1] = x2;
+        } else if (!linear_full) {
+          uint16_t* k = p.kdst + (int64_t)b * p.seq_stride + ((int64_t)slot * p.Hkv + hh) * p.hd;
+          k[2 * j] = f32_to_bf16(x1);
+          k[2 * j + 1] = f32_to_bf16(x2);
+        }
+      }
+    } else if (it < p.Hq + 2 * p.Hkv) {
+      if (linear_full) continue;
+      const int hh = it - p.Hq - p.Hkv;
+      const float* x = row + p.off_v + hh * p.hd;
+      uint16_t* v = p.vdst + (int64_t)b * p.seq_stride + ((int64_t)slot * p.Hkv + hh) * p.hd;
+      for (int d = lane; d < p.hd; d += 32) v[d] = f32_to_bf16(x[d]);
+    } else {
+      if (linear_full) continue;
+      const float* x = row + p.off_ik;
+      uint8_t* ik = p.ikdst + (int64_t)b * p.ik_seq_stride + (int64_t)slot * p.Di;
+      for (int d = lane; d < p.Di; d += 32) ik[d] = f32_to_e4m3(x[d]);
+    }
+  }
+}
+
+int launch_head_prep(const HeadPrepParams& p, int rows, cudaStream_t st) {
+  if (p.hd % 2 || p.hd > 256) return CB_ERR_SHAPE;
+  head_prep_kernel<<<rows, 256, 0, st>>>(p);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
+
+// ------------------------------------------------------------------ SWA
+constexpr int kSwaThreads = 128;
+
+__global__ void __launch_bounds__(kSwaThreads) swa_attn_kernel(SwaParams p) {
+  const int s = blockIdx.x, g = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  const int hd = p.hd, G = p.Hq / p.Hkv, L = p.split_len;
+  extern __shared__ __align__(16) float sm[];
+  float* Ks = sm;                            // [L][hd + 1]
+  float* Vs = Ks + L * (hd + 1);             // [L][hd]
+  float* qsh = Vs + L * hd;                  // [hd]
+  float* es = qsh + hd;                      // [L]
+  float* ored = es + L;                      // [kSwaThreads]
+  __shared__ float red[33];
+
+  const int p0 = p.pos[b] + p.c0;
+  const int lo = max(0, p0 - p.window + 1), last = p0 + p.T - 1;
+  const int ks = lo + s * L, ke = min(ks + L, last + 1);
+  const int n = ke - ks;
+
+  auto part_ptr = [&](int t, int qh) {
+    return p.part + ((((int64_t)b * p.T + t) * p.Hq + qh) * p.n_splits + s) * (hd + 2);
+  };
+  if (n <= 0) {
+    for (int t = 0; t < p.T; ++t)
+      for (int j = 0; j < G; ++j) {
+        float* pp = part_ptr(t, g * G + j);
+        for (int d = tid; d < hd + 2; d += kSwaThreads) pp[d] = d == 0 ? -INFINITY : 0.0f;
+      }
+    return;
+  }
+  const uint16_t* kr = p.kring + (int64_t)b * p.seq_stride;
+  const uint16_t* vr = p.vring + (int64_t)b * p.seq_stride;
+  for (int i = tid; i < n * hd; i += kSwaThreads) {
+    const int key = i / hd, d = i - key * hd;
+    const int64_t off = ((int64_t)((ks + key) % p.slots) * p.Hkv + g) * hd + d;
+    Ks[key * (hd + 1) + d] = bf16_to_f32(kr[off]);
+    Vs[key * hd + d] = bf16_to_f32(vr[off]);
+  }
+  __syncthreads();
+
+  for (int t = 0; t < p.T; ++t) {
+    const int pt = p0 + t;
+    for (int j = 0; j < G; ++j) {
+      const int qh = g * G + j;
+      const float* qrow = p.q + ((int64_t)b * p.T + t) * p.ldq + qh * hd;
+      for (int d = tid; d < hd; d += kSwaThreads) qsh[d] = qrow[d];
+      __syncthreads();
+      float sc = -INFINITY;
+      if (tid < n) {
+        const int kp = ks + tid;
+        if (kp <= pt && kp > pt - p.window) {
+          float acc = 0.0f;
+          const float* kk = Ks + tid * (hd + 1);
+          for (int d = 0; d < hd; ++d) acc = fmaf(qsh[d], kk[d], acc);
+          sc = acc * p.scale;
+        }
+      }
+      const float m = block_max(sc, red);
+      float* pp = part_ptr(t, qh);
+      if (m == -INFINITY) {
+        for (int d = tid; d < hd + 2; d += kSwaThreads) pp[d] = d == 0 ? -INFINITY : 0.0f;
+        __syncthreads();
+        continue;
+      }
+      const float e = sc == -INFINITY ? 0.0f : expf(sc - m);
+      if (tid < L) es[tid] = e;
+      const float l = block_sum(e, red);
+      // o[d] = sum_i e_i V[i][d]; kSwaThreads / hd groups of keys
+      const int groups = kSwaThreads / hd;
+      float o = 0.0f;
+      const int d = tid % hd, grp = tid / hd;
+      if (grp < groups)
+        for (int i = grp; i < n; i += groups) o = fmaf(es[i], Vs[i * hd + d], o);
+      ored[tid] = o;
+      __syncthreads();
+      if (tid < hd) {
+        float acc = 0.0f;
+        for (int q2 = 0; q2 < groups; ++q2) acc += ored[q2 * hd + tid];
+        pp[2 + tid] = acc;
+      }
+      if (tid == 0) {
+        pp[0] = m;
+        pp[1] = l;
+      }
+      __syncthreads();
+    }
+  }
+}
+
+__global__ void swa_combine_kernel(SwaParams p) {
+  const int r = blockIdx.x;
+  const int hd = p.hd;
+  for (int i = threadIdx.x; i < p.Hq * hd; i += blockDim.x) {
+    const int qh = i / hd, d = i - qh * hd;
+    const float* base = p.part + ((int64_t)r * p.Hq + qh) * p.n_splits * (hd + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < p.n_splits; ++s) M = fmaxf(M, base[s * (hd + 2)]);
+    float L = 0.0f, O = 0.0f;
+    for (int s = 0; s < p.n_splits; ++s) {
+      const float ms = base[s * (hd + 2)];
+      if (ms == -INFINITY) continue;
+      const float w = expf(ms - M);
+      L += base[s * (hd + 2) + 1] * w;
+      O += base[s * (hd + 2) + 2 + d] * w;
+    }
+    const float gate = sigmoid(p.gate[(int64_t)r * p.ldg + qh]);
+    p.out[(int64_t)r * p.ldo + qh * hd + d] = (O / L) * gate;
+  }
+}
+
+int launch_swa(const SwaParams& p, int batch, cudaStream_t st) {
+  if (p.hd > kSwaThreads || kSwaThreads % p.hd || p.split_len != kSwaSplit) return CB_ERR_SHAPE;
+  const size_t smem = sizeof(float) * ((size_t)p.split_len * (2 * p.hd + 1) + p.hd + p.split_len + kSwaThreads);
+  static bool set = false;
+  if (!set) {
+    cudaFuncSetAttribute(swa_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    set = true;
+  }
+  swa_attn_kernel<<<dim3(p.n_splits, p.Hkv, batch), kSwaThreads, smem, st>>>(p);
+  count_launch();
+  if (cudaGetLastError() != cudaSuccess) return CB_ERR_CUDA;
+  swa_combine_kernel<<<batch * p.T, std::min(1024, p.Hq * p.hd), 0, st>>>(p);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
+
+// ---------------------------------------------------------- cross attention
+constexpr int kCrossThreads = 256;
+constexpr int kCrossChunk = 256;
+constexpr int kCrossMaxG = 8;
+
+__global__ void __launch_bounds__(kCrossThreads) cross_attn_kernel(CrossParams p) {
+  const int g = blockIdx.x, r = blockIdx.y, tid = threadIdx.x;
+  const int hd = p.hd, G = p.Hq / p.Hkv;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int b = r / p.nq, j0 = r % p.nq;
+  const int position = p.pos[b] + p.c0 + p.t_off + j0;
+  extern __shared__ __align__(16) float sm[];
+  float* qs = sm;                          // [G][hd]
+  float* es = qs + G * hd;                 // [G][kCrossChunk]
+  __shared__ int keys[kCrossChunk];
+  __shared__ float red[33];
+  __shared__ float mrun[kCrossMaxG], lrun[kCrossMaxG], corr[kCrossMaxG];
+
+  // q: RMSNorm (q_norm) + RoPE per head of this KV group
+  const float* row = p.proj + (int64_t)r * p.ldp;
+  for (int j = warp; j < G; j += kCrossThreads / 32) {
+    const float* x = row + (g * G + j) * hd;
+    float ss = 0.0f;
+    for (int d = lane; d < hd; d += 32) ss += x[d] * x[d];
+    ss = warp_sum(ss);
+    const float rn = rsqrtf(ss / (float)hd + p.eps);
+    for (int jj = lane; jj < hd / 2; jj += 32) {
+      float x1 = x[2 * jj] * rn * p.q_norm[2 * jj];
+      float x2 = x[2 * jj + 1] * rn * p.q_norm[2 * jj + 1];
+      if (jj < p.rot2) rope_pair(x1, x2, position, p.inv_freq[jj]);
+      qs[j * hd + 2 * jj] = x1;
+      qs[j * hd + 2 * jj + 1] = x2;
+    }
+  }
+  if (tid < G) {
+    mrun[tid] = -INFINITY;
+    lrun[tid] = 0.0f;
+  }
+  const bool dense = p.sel_idx == nullptr;
+  const int n = dense ? max(0, min(position + 1, p.max_ctx)) : min(p.sel_cnt[r], p.sel_ld);
+  const uint16_t* kb = p.kk + (int64_t)b * p.seq_stride;
+  const uint16_t* vb = p.vv + (int64_t)b * p.seq_stride;
+  // each thread accumulates up to two (head, dim) outputs
+  float o_acc[2] = {0.0f, 0.0f};
+  __syncthreads();
+
+  for (int c = 0; c < n; c += kCrossChunk) {
+    const int cn = min(kCrossChunk, n - c);
+    if (tid < cn) keys[tid] = dense ? c + tid : p.sel_idx[(int64_t)r * p.sel_ld + c + tid];
+    __syncthreads();
+    // scores for this chunk
+    for (int i = tid; i < cn; i += kCrossThreads) {
+      const uint16_t* kr = kb + ((int64_t)keys[i] * p.Hkv + g) * hd;
+      float acc[kCrossMaxG];
+#pragma unroll
+      for (int j = 0; j < kCrossMaxG; ++j) acc[j] = 0.0f;
+      for (int d = 0; d < hd; d += 8) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(kr + d);
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+        float kf[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          kf[2 * e] = bf16_to_f32(w[e]);
+          kf[2 * e + 1] = bf16_to_f32(w[e] >> 16);
+        }
+#pragma unroll
+        for (int j = 0; j < kCrossMaxG; ++j)
+          if (j < G)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[j] = fmaf(qs[j * hd + d + e], kf[e], acc[j]);
+      }
+      for (int j = 0; j < G; ++j) es[j * kCrossChunk + i] = acc[j] * p.scale;
+    }
+    __syncthreads();
+    // running max / sum per head
+    for (int j = 0; j < G; ++j) {
+      const float v = tid < cn ? es[j * kCrossChunk + tid] : -INFINITY;
+      const float cm = block_max(v, red);
+      const float mnew = fmaxf(mrun[j], cm);
+      const float e = tid < cn ? expf(v - mnew) : 0.0f;
+      if (tid < cn) es[j * kCrossChunk + tid] = e;
+      const float cs = block_sum(e, red);
+      if (tid == 0) {
+        corr[j] = mrun[j] == -INFINITY ? 0.0f : expf(mrun[j] - mnew);
+        lrun[j] = lrun[j] * corr[j] + cs;
+        mrun[j] = mnew;
+      }
+      __syncthreads();
+    }
+    // o[j][d] += sum_i e[j][i] * V[key_i][g][d]
+#pragma unroll
+    for (int q2 = 0; q2 < 2; ++q2) {
+      const int idx = tid + q2 * kCrossThreads;
+      if (idx < G * hd) {
+        const int j = idx / hd, d = idx - j * hd;
+        float acc = o_acc[q2] * corr[j];
+        const float* ej = es + j * kCrossChunk;
+        for (int i = 0; i < cn; ++i) acc = fmaf(ej[i], bf16_to_f32(vb[((int64_t)keys[i] * p.Hkv + g) * hd + d]), acc);
+        o_acc[q2] = acc;
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int q2 = 0; q2 < 2; ++q2) {
+    const int idx = tid + q2 * kCrossThreads;
+    if (idx < G * hd) {
+      const int j = idx / hd, d = idx - j * hd;
+      const int qh = g * G + j;
+      const float gate = sigmoid(row[p.off_gate + qh]);
+      p.out[(int64_t)r * p.ldo + qh * hd + d] = (o_acc[q2] / lrun[j]) * gate;
+    }
+  }
+}
+
+int launch_cross(const CrossParams& p, int rows, cudaStream_t st) {
+  const int G = p.Hq / p.Hkv;
+  if (G > kCrossMaxG || G * p.hd > 2 * kCrossThreads || p.hd % 8) return CB_ERR_SHAPE;
+  const size_t smem = sizeof(float) * ((size_t)G * p.hd + (size_t)G * kCrossChunk);
+  cross_attn_kernel<<<dim3(p.Hkv, rows), kCrossThreads, smem, st>>>(p);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
+
+}  // namespace cb

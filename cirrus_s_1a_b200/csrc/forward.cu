@@ -1,0 +1,426 @@
+// cb_forward: one CirrusModel.forward (cirrus/model/model.py:99-176) for a
+// batch of sequences, as a fixed sequence of launches on one stream.
+//
+// Per chunk of <= CB_MAX_T tokens per sequence:
+//   embed -> 12 x [in-proj GEMV (norm1 fused) -> GDN step | SWA prep + attention
+//              -> o-proj GEMV (+residual) -> gate_up GEMV (norm2 fused)
+//              -> down GEMV (SwiGLU fused, +residual)]
+//   -> shared projection GEMV (norm fused) -> K/V/indexer-key append
+//   -> (rows that need logits) indexer scores + top-k
+//   -> 6 x [q|gate GEMV -> sparse attention -> o-proj -> FFN] -> final norm + LM head
+// Dynamic values (positions) are read on the device, so the whole sequence
+// can be captured once in a CUDA graph and replayed every step.
+#include <algorithm>
+#include <atomic>
+#include <cstring>
+
+#include "attn.cuh"
+#include "common.cuh"
+#include "gdn.cuh"
+#include "nvfp4.cuh"
+
+namespace cb {
+
+static std::atomic<long long> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+struct Workspace {
+  int32_t* status;
+  float* h;
+  float* proj;
+  float* attn;
+  float* gu;
+  float* qbuf;
+  float* part;
+  float* xc;
+  float* cproj;
+  float* scores;
+  int32_t* sel_idx;
+  int32_t* sel_cnt;
+  float* logits;
+  int32_t* amax;
+  size_t bytes;
+  int ldp, att_ld, cr_ld, n_splits, sel_ld;
+};
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static int swa_splits(const CbModel& m) { return ceil_div(m.swa_window + CB_MAX_T, kSwaSplit); }
+
+static Workspace carve(const CbModel& m, int batch, int T, int max_ctx, char* base) {
+  Workspace w{};
+  const int R = batch * std::min(std::max(T, 1), CB_MAX_T);
+  int ldp = m.shared_proj.rows;
+  for (int i = 0; i < m.n_self_layers; ++i) ldp = std::max(ldp, m.self_layers[i].in_proj.rows);
+  w.ldp = ldp;
+  w.att_ld = std::max(m.gdn_heads * m.gdn_dv, m.n_q_heads * m.head_dim);
+  w.cr_ld = m.n_cross_layers > 0 ? m.cross_layers[0].q_gate.rows : 16;
+  w.n_splits = swa_splits(m);
+  w.sel_ld = std::max(m.sparse_topk, 1) + 1;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += align256(bytes);
+    return base ? base + o : nullptr;
+  };
+  w.status = (int32_t*)take(256);
+  w.h = (float*)take(sizeof(float) * R * m.d_model);
+  w.proj = (float*)take(sizeof(float) * R * ldp);
+  w.attn = (float*)take(sizeof(float) * R * w.att_ld);
+  w.gu = (float*)take(sizeof(float) * R * 2 * m.ffn_hidden);
+  w.qbuf = (float*)take(sizeof(float) * R * m.n_q_heads * m.head_dim);
+  w.part = (float*)take(sizeof(float) * R * m.n_q_heads * w.n_splits * (m.head_dim + 2));
+  w.xc = (float*)take(sizeof(float) * R * m.d_model);
+  w.cproj = (float*)take(sizeof(float) * R * w.cr_ld);
+  w.scores = (float*)take(m.sparse_topk > 0 ? sizeof(float) * R * (size_t)max_ctx : 0);
+  w.sel_idx = (int32_t*)take(m.sparse_topk > 0 ? sizeof(int32_t) * R * (size_t)w.sel_ld : 0);
+  w.sel_cnt = (int32_t*)take(sizeof(int32_t) * R);
+  w.logits = (float*)take(sizeof(float) * R * (size_t)m.vocab_size);
+  w.amax = (int32_t*)take(sizeof(int32_t) * R);
+  w.bytes = off;
+  return w;
+}
+
+__global__ void gather_rows_kernel(const float* __restrict__ src, int src_T, int t_off, int nq, int cols,
+                                   float* __restrict__ dst) {
+  const int r = blockIdx.x, b = r / nq, j = r % nq;
+  const float* s = src + ((int64_t)b * src_T + t_off + j) * cols;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) dst[(int64_t)r * cols + c] = s[c];
+}
+
+template <typename Tv>
+__global__ void scatter_rows_kernel(const Tv* __restrict__ src, int cols, int nqc, int nq, int off, Tv* __restrict__ dst) {
+  const int r = blockIdx.x, b = r / nqc, j = r % nqc;
+  Tv* d = dst + ((int64_t)b * nq + off + j) * cols;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) d[c] = src[(int64_t)r * cols + c];
+}
+
+__global__ void advance_pos_kernel(int32_t* pos, int batch, int T) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < batch) pos[b] += T;
+}
+
+#define CB_TRY(x)               \
+  do {                          \
+    const int rc_ = (x);        \
+    if (rc_ != CB_OK) return rc_; \
+  } while (0)
+
+static int gemv(const CbMatrix& W, const float* x, int ldx, int m_rows, const float* norm_w, float eps, int pre, int epi,
+                float* y, int ldy, int rows_out, cudaStream_t st) {
+  GemvParams p{};
+  p.tiles = W.tiles;
+  p.tile_scale = W.tile_scale;
+  p.rows = W.rows;
+  p.K = W.k;
+  p.x = x;
+  p.ldx = ldx;
+  p.m_rows = m_rows;
+  p.norm_w = norm_w;
+  p.eps = eps;
+  p.y = y;
+  p.ldy = ldy;
+  p.rows_out = rows_out;
+  return launch_gemv(p, pre, epi, st);
+}
+
+static int ffn(const CbMatrix& gate_up, const CbMatrix& down, const float* norm2, const CbModel& m, float* x, int rows,
+               const Workspace& w, cudaStream_t st) {
+  const int d = m.d_model, F2 = 2 * m.ffn_hidden;
+  CB_TRY(gemv(gate_up, x, d, rows, norm2, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.gu, F2, F2, st));
+  return gemv(down, w.gu, F2, rows, nullptr, 0.f, PRE_SWIGLU, EPI_ADD, x, d, d, st);
+}
+
+static int validate(const CbModel& m, const CbCache& c) {
+  if (m.n_self_layers <= 0 || m.n_self_layers > CB_MAX_SELF || m.n_cross_layers <= 0 ||
+      m.n_cross_layers > CB_MAX_CROSS || m.d_model <= 0 || m.d_model % 16 || m.vocab_size <= 0)
+    return CB_ERR_ARG;
+  if (m.n_q_heads % m.n_kv_heads || m.head_dim % 8 || m.rot_dim > m.head_dim) return CB_ERR_SHAPE;
+  if (!c.pos || !c.kv_k || !c.kv_v || (m.sparse_topk > 0 && !c.kv_ik) || c.batch <= 0 || c.max_ctx <= 0)
+    return CB_ERR_ARG;
+  if (c.swa_slots < m.swa_window + CB_SWA_EXTRA) return CB_ERR_SHAPE;
+  if (!m.lm_head.tiles || !m.shared_proj.tiles || !m.inv_freq) return CB_ERR_ARG;
+  return CB_OK;
+}
+
+}  // namespace cb
+
+using namespace cb;
+
+extern "C" int cb_abi_version(void) { return CB_ABI_VERSION; }
+
+extern "C" int64_t cb_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+extern "C" const char* cb_status_string(int code) {
+  switch (code) {
+    case CB_OK: return "ok";
+    case CB_ERR_ARG: return "invalid argument";
+    case CB_ERR_SHAPE: return "shape not supported";
+    case CB_ERR_CUDA: return "CUDA launch failed";
+    case CB_ERR_WORKSPACE: return "workspace too small";
+    case CB_ERR_CTX_FULL: return "context full (position >= max_ctx)";
+    case CB_ERR_TOKEN: return "token id outside the vocabulary";
+    default: return "unknown status";
+  }
+}
+
+extern "C" size_t cb_workspace_bytes(const CbModel* m, int32_t batch, int32_t T, int32_t max_ctx) {
+  if (!m || batch <= 0 || max_ctx <= 0) return 0;
+  return carve(*m, batch, T, max_ctx, nullptr).bytes;
+}
+
+extern "C" int cb_read_status(const void* workspace, int32_t* status, void* stream) {
+  if (!workspace || !status) return CB_ERR_ARG;
+  if (cudaMemcpyAsync(status, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost, (cudaStream_t)stream) !=
+      cudaSuccess)
+    return CB_ERR_CUDA;
+  return cudaStreamSynchronize((cudaStream_t)stream) == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
+
+extern "C" int cb_clear_status(void* workspace, void* stream) {
+  if (!workspace) return CB_ERR_ARG;
+  return cudaMemsetAsync(workspace, 0, sizeof(int32_t), (cudaStream_t)stream) == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
+
+extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace, size_t workspace_bytes,
+                          const int64_t* ids, int32_t T, int32_t n_logits, float* logits, float* hidden,
+                          int32_t* argmax, void* stream) {
+  if (!mp || !cp || !workspace || !ids || T <= 0) return CB_ERR_ARG;
+  const CbModel& m = *mp;
+  const CbCache& c = *cp;
+  CB_TRY(validate(m, c));
+  const int B = c.batch;
+  const Workspace w = carve(m, B, T, c.max_ctx, (char*)workspace);
+  if (workspace_bytes < w.bytes) return CB_ERR_WORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int d = m.d_model;
+  const int nq = (n_logits <= 0 || n_logits > T) ? T : n_logits;
+  const int Tc = std::min(T, CB_MAX_T);
+  const int H = m.gdn_heads, C = 2 * H * m.gdn_dk + H * m.gdn_dv;
+  const int64_t gdn_S_layer = (int64_t)H * m.gdn_dk * m.gdn_dv;
+  const int64_t gdn_conv_layer = (int64_t)(m.conv_size - 1) * C;
+  const int64_t swa_layer = (int64_t)c.swa_slots * m.n_kv_heads * m.head_dim;
+  const int64_t kv_seq = (int64_t)c.max_ctx * m.n_kv_heads * m.head_dim;
+
+  for (int c0 = 0; c0 < T; c0 += Tc) {
+    const int tc = std::min(Tc, T - c0);
+    const int R = B * tc;
+    CB_TRY(launch_embed(m.lm_head, m.vocab_size, ids, T, B, tc, c0, w.h, w.status, st));
+
+    // ------------------------------------------------------ self-decoder
+    for (int i = 0; i < m.n_self_layers; ++i) {
+      const CbSelfLayer& L = m.self_layers[i];
+      const int ldp = L.in_proj.rows;
+      CB_TRY(gemv(L.in_proj, w.h, d, R, L.norm1, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.proj, ldp, ldp, st));
+      if (L.kind == CB_LAYER_GDN) {
+        GdnParams g{};
+        g.proj = w.proj;
+        g.ldp = ldp;
+        g.off_gate = m.gdn_off_gate;
+        g.off_a = m.gdn_off_a;
+        g.off_b = m.gdn_off_b;
+        g.conv_w = L.conv_w;
+        g.A_log = L.A_log;
+        g.dt_bias = L.dt_bias;
+        g.o_norm = L.o_norm;
+        g.state = c.gdn_state + (int64_t)L.slot * gdn_S_layer;
+        g.state_stride = (int64_t)c.n_gdn * gdn_S_layer;
+        g.conv = c.gdn_conv + (int64_t)L.slot * gdn_conv_layer;
+        g.conv_stride = (int64_t)c.n_gdn * gdn_conv_layer;
+        g.out = w.attn;
+        g.ldo = w.att_ld;
+        g.batch = B;
+        g.T = tc;
+        g.H = H;
+        g.Dk = m.gdn_dk;
+        g.Dv = m.gdn_dv;
+        g.C = C;
+        g.KC = m.conv_size;
+        g.eps = m.norm_eps;
+        g.scale = 1.0f / sqrtf((float)m.gdn_dk);
+        CB_TRY(launch_gdn_step(g, st));
+      } else {
+        HeadPrepParams hp{};
+        hp.proj = w.proj;
+        hp.ldp = ldp;
+        hp.T = tc;
+        hp.c0 = c0;
+        hp.pos = c.pos;
+        hp.Hq = m.n_q_heads;
+        hp.Hkv = m.n_kv_heads;
+        hp.hd = m.head_dim;
+        hp.rot2 = m.rot_dim / 2;
+        hp.off_q = 0;
+        hp.off_k = m.swa_off_kv;
+        hp.off_v = m.swa_off_kv + m.n_kv_heads * m.head_dim;
+        hp.q_norm = L.q_norm;
+        hp.k_norm = L.k_norm;
+        hp.inv_freq = m.inv_freq;
+        hp.eps = m.norm_eps;
+        hp.qout = w.qbuf;
+        hp.ldq = m.n_q_heads * m.head_dim;
+        hp.kdst = c.swa_k + (int64_t)L.slot * swa_layer;
+        hp.vdst = c.swa_v + (int64_t)L.slot * swa_layer;
+        hp.seq_stride = (int64_t)c.n_swa * swa_layer;
+        hp.slots = c.swa_slots;
+        hp.ring = true;
+        hp.status = w.status;
+        CB_TRY(launch_head_prep(hp, R, st));
+        SwaParams sp{};
+        sp.q = w.qbuf;
+        sp.ldq = hp.ldq;
+        sp.kring = hp.kdst;
+        sp.vring = hp.vdst;
+        sp.seq_stride = hp.seq_stride;
+        sp.slots = c.swa_slots;
+        sp.pos = c.pos;
+        sp.T = tc;
+        sp.c0 = c0;
+        sp.Hq = m.n_q_heads;
+        sp.Hkv = m.n_kv_heads;
+        sp.hd = m.head_dim;
+        sp.window = m.swa_window;
+        sp.split_len = kSwaSplit;
+        sp.n_splits = w.n_splits;
+        sp.scale = 1.0f / sqrtf((float)m.head_dim);
+        sp.part = w.part;
+        sp.gate = w.proj + m.swa_off_gate;
+        sp.ldg = ldp;
+        sp.out = w.attn;
+        sp.ldo = w.att_ld;
+        CB_TRY(launch_swa(sp, B, st));
+      }
+      CB_TRY(gemv(L.o_proj, w.attn, w.att_ld, R, nullptr, 0.f, PRE_NONE, EPI_ADD, w.h, d, d, st));
+      CB_TRY(ffn(L.gate_up, L.down, L.norm2, m, w.h, R, w, st));
+    }
+
+    // ------------------------------------------------ shared KV (YOCO)
+    const int lds = m.shared_proj.rows;
+    CB_TRY(gemv(m.shared_proj, w.h, d, R, m.shared_norm, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.proj, lds, lds, st));
+    {
+      HeadPrepParams hp{};
+      hp.proj = w.proj;
+      hp.ldp = lds;
+      hp.T = tc;
+      hp.c0 = c0;
+      hp.pos = c.pos;
+      hp.Hq = 0;
+      hp.Hkv = m.n_kv_heads;
+      hp.hd = m.head_dim;
+      hp.rot2 = m.rot_dim / 2;
+      hp.off_k = 0;
+      hp.off_v = m.n_kv_heads * m.head_dim;
+      hp.k_norm = m.shared_k_norm;
+      hp.inv_freq = m.inv_freq;
+      hp.eps = m.norm_eps;
+      hp.kdst = c.kv_k;
+      hp.vdst = c.kv_v;
+      hp.seq_stride = kv_seq;
+      hp.slots = c.max_ctx;
+      hp.ring = false;
+      if (m.sparse_topk > 0) {
+        hp.off_ik = m.sh_off_ik;
+        hp.Di = m.indexer_dim;
+        hp.ikdst = c.kv_ik;
+        hp.ik_seq_stride = (int64_t)c.max_ctx * m.indexer_dim;
+      }
+      hp.status = w.status;
+      CB_TRY(launch_head_prep(hp, R, st));
+    }
+
+    // --------------------------------------------------- cross-decoder
+    const int nqc = std::max(0, std::min(tc, c0 + tc - (T - nq)));
+    if (nqc == 0) continue;
+    const int RQ = B * nqc, t_off = tc - nqc;
+    gather_rows_kernel<<<RQ, 256, 0, st>>>(w.h, tc, t_off, nqc, d, w.xc);
+    count_launch();
+    if (cudaGetLastError() != cudaSuccess) return CB_ERR_CUDA;
+    if (m.sparse_topk > 0) {
+      IndexerParams ip{};
+      ip.iq = w.proj + m.sh_off_iq;
+      ip.iw = w.proj + m.sh_off_iw;
+      ip.ld_q = lds;
+      ip.iq_T = tc;
+      ip.iq_off = t_off;
+      ip.ik = c.kv_ik;
+      ip.ik_seq_stride = (int64_t)c.max_ctx * m.indexer_dim;
+      ip.Hi = m.indexer_heads;
+      ip.Di = m.indexer_dim;
+      ip.max_ctx = c.max_ctx;
+      ip.pos = c.pos;
+      ip.c0 = c0;
+      ip.t_off = t_off;
+      ip.nq = nqc;
+      ip.rows = RQ;
+      ip.k = m.sparse_topk;
+      ip.scores = w.scores;
+      ip.sel_idx = w.sel_idx;
+      ip.sel_ld = w.sel_ld;
+      ip.sel_cnt = w.sel_cnt;
+      CB_TRY(launch_indexer_topk(ip, st));
+    }
+    for (int j = 0; j < m.n_cross_layers; ++j) {
+      const CbCrossLayer& L = m.cross_layers[j];
+      const int ldc = L.q_gate.rows;
+      CB_TRY(gemv(L.q_gate, w.xc, d, RQ, L.norm1, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.cproj, ldc, ldc, st));
+      CrossParams cpp{};
+      cpp.proj = w.cproj;
+      cpp.ldp = ldc;
+      cpp.off_gate = m.cr_off_gate;
+      cpp.q_norm = L.q_norm;
+      cpp.inv_freq = m.inv_freq;
+      cpp.rot2 = m.rot_dim / 2;
+      cpp.eps = m.norm_eps;
+      cpp.scale = 1.0f / sqrtf((float)m.head_dim);
+      cpp.pos = c.pos;
+      cpp.c0 = c0;
+      cpp.t_off = t_off;
+      cpp.nq = nqc;
+      cpp.kk = c.kv_k;
+      cpp.vv = c.kv_v;
+      cpp.seq_stride = kv_seq;
+      cpp.Hq = m.n_q_heads;
+      cpp.Hkv = m.n_kv_heads;
+      cpp.hd = m.head_dim;
+      cpp.sel_idx = m.sparse_topk > 0 ? w.sel_idx : nullptr;
+      cpp.sel_cnt = w.sel_cnt;
+      cpp.sel_ld = w.sel_ld;
+      cpp.max_ctx = c.max_ctx;
+      cpp.out = w.attn;
+      cpp.ldo = w.att_ld;
+      CB_TRY(launch_cross(cpp, RQ, st));
+      CB_TRY(gemv(L.o_proj, w.attn, w.att_ld, RQ, nullptr, 0.f, PRE_NONE, EPI_ADD, w.xc, d, d, st));
+      CB_TRY(ffn(L.gate_up, L.down, L.norm2, m, w.xc, RQ, w, st));
+    }
+
+    // --------------------------------------------------- LM head + outputs
+    const int V = m.vocab_size;
+    const int out_off = c0 + t_off - (T - nq);  // first logits row of this chunk, per sequence
+    const bool direct = (tc == T) && logits != nullptr;
+    float* lg = direct ? logits : w.logits;
+    CB_TRY(gemv(m.lm_head, w.xc, d, RQ, m.final_norm, m.norm_eps, PRE_RMSNORM, EPI_STORE, lg, V, V, st));
+    if (logits && !direct) {
+      scatter_rows_kernel<float><<<RQ, 256, 0, st>>>(lg, V, nqc, nq, out_off, logits);
+      count_launch();
+      if (cudaGetLastError() != cudaSuccess) return CB_ERR_CUDA;
+    }
+    if (argmax) {
+      if (tc == T) {
+        CB_TRY(launch_argmax(lg, RQ, V, V, argmax, st));
+      } else {
+        CB_TRY(launch_argmax(lg, RQ, V, V, w.amax, st));
+        scatter_rows_kernel<int32_t><<<RQ, 32, 0, st>>>(w.amax, 1, nqc, nq, out_off, argmax);
+        count_launch();
+        if (cudaGetLastError() != cudaSuccess) return CB_ERR_CUDA;
+      }
+    }
+    if (hidden) {
+      scatter_rows_kernel<float><<<RQ, 256, 0, st>>>(w.xc, d, nqc, nq, out_off, hidden);
+      count_launch();
+      if (cudaGetLastError() != cudaSuccess) return CB_ERR_CUDA;
+    }
+  }
+  advance_pos_kernel<<<ceil_div(B, 128), 128, 0, st>>>(c.pos, B, T);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}

@@ -1,0 +1,208 @@
+/*
+ * cirrus_b200.h -- C ABI of the B200 (sm_100a) decode path of cirrus-s-1a.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), launches work on that stream only, allocates nothing,
+ * never synchronises the device and never throws.  Each returns CB_OK or a
+ * CB_ERR_* code for a host-side argument error (nothing is launched then).
+ * Errors found on the device (context full, bad token id) are written to the
+ * status word of the workspace (cb_forward) and read with cb_read_status.
+ *
+ * Reference interfaces these replace (paths inside the reference project):
+ *   cb_forward            CirrusModel.forward            cirrus/model/model.py:99-176
+ *   cb_nvfp4_quantize     (no quantiser in the reference; the NVFP4 format is
+ *                          cirrus/perf/bench_kernels.cu:141-145)
+ *   cb_nvfp4_pack_tiles   pack_nvfp4_mma / pack_nvfp4_v3  scripts/bench_spark.py:369-391, 639-660
+ *   cb_gemv_nvfp4         nvfp4_gemv                     cirrus/perf/bench_kernels.cu:202-227
+ *                         (and every nn.Linear of the model, layers.py)
+ *   cb_gdn_step           GatedDeltaNet.forward          cirrus/model/layers.py:151-174
+ *   cb_indexer_topk       indexer_scores + topk_mask     cirrus/model/layers.py:282-309
+ *   cb_embed              nn.Embedding (tied to lm_head) cirrus/model/model.py:124, 75-77
+ *   cb_argmax             logits.argmax                  cirrus/model/generate.py:33, 74
+ */
+#ifndef CIRRUS_B200_H
+#define CIRRUS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CB_ABI_VERSION 1
+#define CB_MAX_SELF 32   /* self-decoder layers */
+#define CB_MAX_CROSS 16  /* cross-decoder layers */
+#define CB_MAX_T 8       /* tokens per sequence per launch chunk (1 + draft) */
+#define CB_TILE_ROWS 16  /* rows per NVFP4 weight tile */
+#define CB_SWA_EXTRA 16  /* SWA ring slots beyond the window */
+
+enum {
+  CB_OK = 0,
+  CB_ERR_ARG = 1,         /* null pointer or bad size */
+  CB_ERR_SHAPE = 2,       /* shape not supported by the kernels */
+  CB_ERR_CUDA = 3,        /* a launch failed (cudaGetLastError) */
+  CB_ERR_WORKSPACE = 4,   /* workspace smaller than cb_workspace_bytes */
+  CB_ERR_CTX_FULL = 5,    /* device status: a position reached max_ctx */
+  CB_ERR_TOKEN = 6        /* device status: token id outside the vocabulary */
+};
+
+enum { CB_LAYER_GDN = 0, CB_LAYER_SWA = 1 };
+
+/* One NVFP4 weight matrix in tile layout: ceil(rows/16) tiles, each tile is
+ * 16 rows of E2M1 codes (K/2 bytes per row, low nibble = even k) followed by
+ * the 16 rows of E4M3 block scales (K/16 bytes per row): 9*K bytes a tile.
+ * Several matrices that read the same input are concatenated row-wise, each
+ * padded to a multiple of 16 rows; tile_scale holds the float32 tensor scale
+ * of every tile. */
+typedef struct CbMatrix {
+  const uint8_t* tiles;
+  const float* tile_scale;
+  int32_t rows;         /* rows including padding (multiple of 16) */
+  int32_t k;            /* multiple of 16 */
+} CbMatrix;
+
+typedef struct CbSelfLayer {
+  int32_t kind;         /* CB_LAYER_GDN or CB_LAYER_SWA */
+  int32_t slot;         /* index among the GDN layers, or among the SWA layers */
+  const float* norm1;   /* [d_model] */
+  const float* norm2;   /* [d_model] */
+  CbMatrix in_proj;     /* GDN: qkv | gate | ab ;  SWA: q | kv | gate */
+  CbMatrix o_proj;
+  CbMatrix gate_up;     /* [2*ffn_hidden rows] gate rows first, then up rows */
+  CbMatrix down;
+  const float* conv_w;  /* GDN [C, conv_size], C = 2*H*dk + H*dv */
+  const float* A_log;   /* GDN [H] */
+  const float* dt_bias; /* GDN [H] */
+  const float* o_norm;  /* GDN [dv] */
+  const float* q_norm;  /* SWA [head_dim] */
+  const float* k_norm;  /* SWA [head_dim] */
+} CbSelfLayer;
+
+typedef struct CbCrossLayer {
+  const float* norm1;
+  const float* norm2;
+  CbMatrix q_gate;      /* q | gate */
+  CbMatrix o_proj;
+  CbMatrix gate_up;
+  CbMatrix down;
+  const float* q_norm;  /* [head_dim] */
+} CbCrossLayer;
+
+typedef struct CbModel {
+  int32_t d_model, vocab_size, n_self_layers, n_cross_layers;
+  int32_t gdn_heads, gdn_dk, gdn_dv, conv_size;
+  int32_t n_q_heads, n_kv_heads, head_dim, rot_dim;
+  int32_t swa_window, sparse_topk;            /* sparse_topk 0 = dense cross attention */
+  int32_t indexer_heads, indexer_dim, ffn_hidden;
+  float norm_eps;
+  const float* inv_freq;                      /* [rot_dim/2], as layers.py:69 computes it */
+  /* column offsets inside the concatenated projection outputs (each segment
+   * starts on a multiple of 16) */
+  int32_t gdn_off_gate, gdn_off_a, gdn_off_b;  /* q at 0, k at H*dk, v at 2*H*dk */
+  int32_t swa_off_kv, swa_off_gate;            /* q at 0; k at off_kv, v at off_kv + kv_dim */
+  int32_t sh_off_ik, sh_off_iq, sh_off_iw;     /* k at 0, v at kv_dim */
+  int32_t cr_off_gate;                         /* q at 0 */
+  CbSelfLayer self_layers[CB_MAX_SELF];
+  const float* shared_norm;
+  const float* shared_k_norm;
+  CbMatrix shared_proj;                        /* kv | idx_k | idx_q | idx_w */
+  CbCrossLayer cross_layers[CB_MAX_CROSS];
+  const float* final_norm;
+  CbMatrix lm_head;                            /* tied with the embedding */
+} CbModel;
+
+/* Decode state of `batch` independent sequences (the reference Cache,
+ * model.py:41-51).  pos[b] = tokens already in the cache.  SWA keys live in a
+ * ring of swa_slots = swa_window + CB_SWA_EXTRA rows, slot = position % swa_slots;
+ * the shared KV rows are indexed by position.  Rows at positions >= pos[b]
+ * are scratch: a forward that is later discarded may write them. */
+typedef struct CbCache {
+  int32_t batch, max_ctx, swa_slots, n_gdn, n_swa;
+  int32_t* pos;        /* device [batch] */
+  float* gdn_state;    /* [batch][n_gdn][H][dk][dv] float32 (S[k][v], layers.py:120) */
+  float* gdn_conv;     /* [batch][n_gdn][conv_size-1][C] float32 */
+  uint16_t* swa_k;     /* bf16 [batch][n_swa][swa_slots][n_kv_heads][head_dim] */
+  uint16_t* swa_v;
+  uint16_t* kv_k;      /* bf16 [batch][max_ctx][n_kv_heads][head_dim] */
+  uint16_t* kv_v;
+  uint8_t* kv_ik;      /* E4M3 [batch][max_ctx][indexer_dim] */
+} CbCache;
+
+int cb_abi_version(void);
+const char* cb_status_string(int code);
+
+/* ---------------------------------------------------------------- NVFP4 */
+/* w float32 [n, k] (k % 16 == 0) -> standard NVFP4: codes [n, k/2] (low nibble
+ * = even k), scales E4M3 [n, k/16].  Block scale = absmax(w/tensor_scale)/6
+ * rounded to E4M3 (nearest-even, saturating); codes = E2M1 nearest-even of
+ * (w/tensor_scale)/scale, saturating; zero scale -> zero codes. */
+int cb_nvfp4_quantize(const float* w, int32_t n, int32_t k, float tensor_scale, uint8_t* codes,
+                      uint8_t* scales, void* stream);
+
+/* standard NVFP4 [n, k] -> ceil(n/16) tiles (see CbMatrix); pad rows are zero. */
+int cb_nvfp4_pack_tiles(const uint8_t* codes, const uint8_t* scales, int32_t n, int32_t k, uint8_t* tiles,
+                        void* stream);
+
+/* y[m, :rows_out] = x[m, :k] @ dequant(W)^T for m < m_rows (rows_out <= W.rows);
+ * x row stride ldx, y row stride ldy (elements).  Any m_rows >= 1. */
+int cb_gemv_nvfp4(const CbMatrix* w, const float* x, int32_t ldx, int32_t m_rows, float* y, int32_t ldy,
+                  int32_t rows_out, void* stream);
+
+/* h[r, :] = dequant(lm_head row ids[r]) for r < n_rows (float32 [n_rows, d]). */
+int cb_embed(const CbMatrix* table, const int64_t* ids, int32_t n_rows, float* h, int32_t* status, void* stream);
+
+/* out[r] = first index of the maximum of x[r, :n] for r < rows. */
+int cb_argmax(const float* x, int32_t rows, int32_t n, int32_t ld, int32_t* out, void* stream);
+
+/* ------------------------------------------------------------ GDN step */
+/* One Gated DeltaNet mixer step for T tokens of `batch` sequences, from the
+ * in_proj output (qkv | gate | ab, row = b*T + t, row stride ldp) to the
+ * gated, normalised output [batch*T, H*dv]: short conv with its rolling
+ * cache, L2-norm of q and k, decay g = -exp(A_log)*softplus(a + dt_bias),
+ * beta = sigmoid(b), the exact recurrence on S (updated in place), o_norm and
+ * the silu(gate) product.  state/conv point at this layer's slot of sequence
+ * 0; state_stride / conv_stride are the element strides between sequences. */
+int cb_gdn_step(const CbModel* m, int32_t layer, const float* proj, int32_t ldp, int32_t batch, int32_t T,
+                float* state, int64_t state_stride, float* conv, int64_t conv_stride, float* out, int32_t ldo,
+                void* stream);
+
+/* -------------------------------------------------- indexer + top-k */
+/* For each of `rows` query rows: scores over keys 0..qpos[r] of sequence
+ * seq[r] (s = sum_h iw_h * relu(iq_h . ik_s), one fixed float32 order), then
+ * the stable top-k of layers.py:291-309 (most recent key wins ties, the
+ * query's own key always kept, all keys kept when qpos+1 <= k).
+ * iq [rows][Hi*Di] (stride ld_q), iw [rows][Hi] (stride ld_q), ik E4M3
+ * [batch][max_ctx][Di].  scores: scratch [rows][max_ctx] float32.
+ * sel_idx [rows][k+1] ascending key indices, sel_cnt [rows]. */
+int cb_indexer_topk(const float* iq, const float* iw, int32_t ld_q, const uint8_t* ik, int32_t max_ctx,
+                    int32_t Hi, int32_t Di, const int32_t* seq, const int32_t* qpos, int32_t rows, int32_t k,
+                    float* scores, int32_t* sel_idx, int32_t* sel_cnt, void* stream);
+
+/* ------------------------------------------------------- whole forward */
+/* Workspace bytes cb_forward needs for `batch` sequences and up to T tokens
+ * per sequence (T is clamped to CB_MAX_T: longer inputs run in chunks). */
+size_t cb_workspace_bytes(const CbModel* m, int32_t batch, int32_t T, int32_t max_ctx);
+
+/* CirrusModel.forward(input_ids[batch, T], cache, n_logits) for a batch of
+ * sequences sharing T: embeds, runs the self-decoder (updating GDN / conv /
+ * SWA state), appends T shared-KV rows per sequence, runs the cross-decoder
+ * and LM head for the last n_logits positions (n_logits <= 0 means T), and
+ * advances cache->pos by T on the device.  ids: device int64 [batch, T].
+ * Outputs (any may be NULL): logits [batch][n][vocab], hidden [batch][n][d]
+ * (pre-final-norm), argmax [batch][n].  Launch-only: capturable in a CUDA graph. */
+int cb_forward(const CbModel* m, const CbCache* c, void* workspace, size_t workspace_bytes, const int64_t* ids,
+               int32_t T, int32_t n_logits, float* logits, float* hidden, int32_t* argmax, void* stream);
+
+/* Copy the workspace's device status word into *status (synchronises on the stream). */
+int cb_read_status(const void* workspace, int32_t* status, void* stream);
+/* Clear the status word (stream-ordered). */
+int cb_clear_status(void* workspace, void* stream);
+
+/* Number of kernels this library has launched in this process (all entry points). */
+int64_t cb_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CIRRUS_B200_H */

@@ -65,10 +65,22 @@ def e4m3_encode(x: np.ndarray) -> np.ndarray:
     return np.where(np.signbit(x), code | 0x80, code).astype(np.uint8)
 
 
-def e2m1_encode(x: np.ndarray) -> np.ndarray:
-    """float32 -> E2M1 code (0..15), round-to-nearest-even, saturating to +-6."""
+def e2m1_encode_table(x: np.ndarray) -> np.ndarray:
+    """float32 -> E2M1 code (0..15), round-to-nearest-even, saturating to +-6 (table search)."""
     x = np.asarray(x, dtype=np.float32).astype(np.float64)
     code = _rne_to_table(np.abs(x), E2M1_MAG.astype(np.float64)).astype(np.uint8)
+    return np.where(np.signbit(x), code | 0x8, code).astype(np.uint8)
+
+
+def e2m1_encode(x: np.ndarray) -> np.ndarray:
+    """Same result as ``e2m1_encode_table`` for non-NaN input, by counting the
+    rounding boundaries below |x|: a boundary that is a tie belongs to the
+    even code (0.25 -> 0, 0.75 -> 1.0, 1.25 -> 1.0, 1.75 -> 2.0, 2.5 -> 2.0,
+    3.5 -> 4.0, 5.0 -> 4.0)."""
+    x = np.asarray(x, dtype=np.float32)
+    a = np.abs(x)
+    code = ((a > 0.25).astype(np.uint8) + (a >= 0.75) + (a > 1.25) + (a >= 1.75) + (a > 2.5) + (a >= 3.5)
+            + (a > 5.0)).astype(np.uint8)
     return np.where(np.signbit(x), code | 0x8, code).astype(np.uint8)
 
 

@@ -1,0 +1,170 @@
+"""End-to-end parity of the B200 forward (``CirrusB200``, through ``cb_forward``)
+against the oracle's restatement of ``CirrusModel.forward`` on the same
+NVFP4-quantised weights, with the B200 storage casts (bf16 K/V, E4M3 indexer
+keys).  Tolerance: logits within 1e-2 relative / 2e-2 absolute; greedy tokens
+identical except where the oracle's own top-2 logit margin is below 2e-2
+(a documented near-tie)."""
+
+from dataclasses import replace
+
+import pytest
+import torch
+
+from oracle import model as om
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-2, 2e-2
+
+
+def _setup(cfg, seed=0, max_ctx=512):
+    from cirrus_s_1a_b200 import synthetic
+    from cirrus_s_1a_b200.engine import CirrusB200
+
+    sd = synthetic.random_state_dict(cfg, seed=seed, norm_jitter=0.1)
+    eng = CirrusB200(cfg, sd, max_ctx=max_ctx)
+    return eng, om.quantized_params(sd)
+
+
+def _cfgs():
+    from cirrus_s_1a_b200.config import baseline_config, get_config
+
+    return {"debug": get_config("cirrus-s-1a-debug"), "debug_dense": replace(get_config("cirrus-s-1a-debug"),
+                                                                            sparse_topk=None),
+            "baseline": baseline_config()}
+
+
+def _close(a, b, what):
+    a, b = a.float().cpu(), b.float().cpu()
+    err = (a - b).abs().max().item()
+    torch.testing.assert_close(a, b, rtol=RTOL, atol=ATOL, msg=lambda m: f"{what}: max abs err {err}\n{m}")
+
+
+@pytest.mark.parametrize("name,prompt_len,steps", [("debug", 20, 12), ("debug_dense", 13, 6), ("baseline", 70, 6)])
+def test_prefill_decode_verify_match_oracle(name, prompt_len, steps):
+    from cirrus_s_1a_b200 import synthetic
+
+    cfg = _cfgs()[name]
+    eng, p = _setup(cfg, seed=1)
+    prompt = synthetic.random_prompt(prompt_len, cfg.vocab_size, seed=2)
+    ids = torch.tensor([prompt])
+    o_ref = om.forward(p, cfg, ids, use_cache=True, n_logits=1, casts=om.B200)
+    o = eng(ids, use_cache=True, n_logits=1)
+    _close(o.logits, o_ref.logits, "prefill logits")
+    _close(o.hidden, o_ref.hidden, "prefill hidden")
+    cache, cref = o.cache, o_ref.cache
+    for s in range(steps):
+        tok = int(o_ref.logits[0, -1].argmax())
+        o_ref = om.forward(p, cfg, torch.tensor([[tok]]), cache=cref, n_logits=1, casts=om.B200)
+        o = eng(torch.tensor([[tok]]), cache=cache, n_logits=1)
+        cref, cache = o_ref.cache, o.cache
+        _close(o.logits, o_ref.logits, f"step {s} logits")
+    # verify-style forward of 5 tokens with logits for all of them
+    draft = prompt[3:8]
+    o_ref = om.forward(p, cfg, torch.tensor([draft]), cache=cref, n_logits=5, casts=om.B200)
+    o = eng(torch.tensor([draft]), cache=cache, n_logits=5)
+    _close(o.logits, o_ref.logits, "verify logits")
+    # cache contents against the oracle's cache
+    exp = cache.to_reference()
+    assert exp["pos"] == o_ref.cache.pos
+    for i, (a, b) in enumerate(zip(exp["layers"], o_ref.cache.layers)):
+        for key in a:
+            torch.testing.assert_close(a[key], b[key].float(), rtol=2e-2, atol=2e-2, msg=f"layer {i} {key}")
+    for key in exp["shared"]:
+        torch.testing.assert_close(exp["shared"][key], o_ref.cache.shared[key].float(), rtol=5e-2, atol=5e-2,
+                                   msg=f"shared {key}")
+    assert eng.read_status(cache) == 0
+
+
+def test_long_prompt_chunks_and_full_logits():
+    cfg = _cfgs()["debug"]
+    eng, p = _setup(cfg, seed=4)
+    ids = torch.randint(0, cfg.vocab_size, (1, 19), generator=torch.Generator().manual_seed(3))
+    o = eng(ids, use_cache=True)  # all 19 positions' logits, 3 chunks of <= 8
+    o_ref = om.forward(p, cfg, ids, use_cache=True, casts=om.B200)
+    _close(o.logits, o_ref.logits, "full logits")
+    o = eng(ids, use_cache=True, n_logits=11)
+    _close(o.logits, o_ref.logits[:, -11:], "last 11 logits")
+
+
+def test_batched_sequences_match_individual_runs():
+    from cirrus_s_1a_b200 import synthetic
+
+    cfg = _cfgs()["baseline"]
+    eng, p = _setup(cfg, seed=5)
+    prompts = [synthetic.random_prompt(24, cfg.vocab_size, seed=s) for s in (10, 11, 12)]
+    o = eng(torch.tensor(prompts), use_cache=True, n_logits=2)
+    cache = o.cache
+    refs = [om.forward(p, cfg, torch.tensor([pr]), use_cache=True, n_logits=2, casts=om.B200) for pr in prompts]
+    for b in range(3):
+        _close(o.logits[b], refs[b].logits[0], f"seq {b} prefill")
+    for s in range(3):
+        toks = [int(r.logits[0, -1].argmax()) for r in refs]
+        refs = [om.forward(p, cfg, torch.tensor([[t]]), cache=r.cache, n_logits=1, casts=om.B200)
+                for t, r in zip(toks, refs)]
+        o = eng(torch.tensor([[t] for t in toks]), cache=cache, n_logits=1)
+        for b in range(3):
+            _close(o.logits[b], refs[b].logits[0], f"seq {b} step {s}")
+
+
+def _tokens_agree(gpu, ref_tokens, margins):
+    for i, (a, b) in enumerate(zip(gpu, ref_tokens)):
+        if a != b:
+            assert margins[i] < ATOL, f"token {i}: {a} != {b} with oracle margin {margins[i]}"
+            return i
+    return len(gpu)
+
+
+def test_greedy_speculative_and_oracle_agree():
+    from cirrus_s_1a_b200 import generate as G
+
+    cfg = _cfgs()["debug"]
+    eng, p = _setup(cfg, seed=6)
+    g = torch.Generator().manual_seed(8)
+    base = torch.randint(0, cfg.vocab_size, (12,), generator=g).tolist()
+    prompt = base + torch.randint(0, cfg.vocab_size, (5,), generator=g).tolist() + base[:4]
+    ref, s_ref = G.greedy(eng, prompt, 30)
+    spec, s_spec = G.speculative_greedy(eng, prompt, 30, use_mtp=False)
+    assert spec == ref
+    assert s_spec.steps <= s_ref.steps
+    # oracle greedy with margins
+    o = om.forward(p, cfg, torch.tensor([prompt]), use_cache=True, n_logits=1, casts=om.B200)
+    toks, margins = [], []
+    for _ in range(30):
+        lg = o.logits[0, -1]
+        top2 = lg.topk(2).values
+        margins.append(float(top2[0] - top2[1]))
+        toks.append(int(lg.argmax()))
+        o = om.forward(p, cfg, torch.tensor([[toks[-1]]]), cache=o.cache, n_logits=1, casts=om.B200)
+    _tokens_agree(ref, toks, margins)
+
+
+def test_graph_replay_matches_eager():
+    from cirrus_s_1a_b200.engine import DecodeGraph
+
+    cfg = _cfgs()["baseline"]
+    eng, _ = _setup(cfg, seed=9)
+    prompt = torch.randint(0, cfg.vocab_size, (1, 33), generator=torch.Generator().manual_seed(1))
+    o1 = eng(prompt, use_cache=True, n_logits=1)
+    o2 = eng(prompt, use_cache=True, n_logits=1)
+    c1, c2 = o1.cache, o2.cache
+    graph = DecodeGraph(eng, c2, T=1, n_logits=1)
+    tok = int(o1.logits[0, -1].argmax())
+    for _ in range(5):
+        e = eng(torch.tensor([[tok]]), cache=c1, n_logits=1)
+        graph.step(torch.tensor([[tok]]))
+        torch.cuda.synchronize()
+        assert torch.equal(graph.logits, e.logits)
+        assert int(graph.argmax[0, 0]) == int(e.logits[0, -1].argmax())
+        tok = int(e.logits[0, -1].argmax())
+    assert c1.pos == c2.pos
+
+
+def test_context_full_is_rejected_on_host():
+    from cirrus_s_1a_b200._lib import CbError
+
+    cfg = _cfgs()["debug"]
+    eng, _ = _setup(cfg, seed=0, max_ctx=16)
+    o = eng(torch.zeros(1, 10, dtype=torch.long), use_cache=True, n_logits=1)
+    with pytest.raises(CbError):
+        eng(torch.zeros(1, 7, dtype=torch.long), cache=o.cache, n_logits=1)

@@ -39,6 +39,14 @@ def test_e2m1_ties_and_saturation():
     assert vals.tolist() == [0.0, 1.0, 1.0, 2.0, 2.0, 4.0, 4.0, 6.0, -0.0, -4.0, 0.5, -0.5, 6.0]
 
 
+def test_e2m1_threshold_encoder_equals_table_rne():
+    rng = np.random.default_rng(1)
+    x = np.concatenate([rng.normal(0, 2, 100000), rng.uniform(-8, 8, 100000),
+                        np.float32([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0, 6.5, -0.0, 0.0])]).astype(np.float32)
+    x = np.concatenate([x, np.nextafter(x, np.float32(np.inf)), np.nextafter(x, np.float32(-np.inf))])
+    assert np.array_equal(nvfp4.e2m1_encode(x), nvfp4.e2m1_encode_table(x))
+
+
 def test_dequant_matches_reference_benchmark_dequant():
     g = golden("nvfp4_ref.pt")
     ours = nvfp4.dequantize(g["codes"].numpy(), g["scales"].numpy())
