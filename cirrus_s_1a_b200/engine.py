@@ -212,7 +212,7 @@ class DeviceCache:
             self.swa_v = torch.zeros_like(self.swa_k)
             self.kv_k = torch.zeros(batch, max_ctx, kvh, hd, dtype=torch.bfloat16, device=dev)
             self.kv_v = torch.zeros_like(self.kv_k)
-            self.kv_ik = torch.zeros(batch, max_ctx, max(cfg.indexer_dim, 16), dtype=torch.uint8, device=dev)
+            self.kv_ik = torch.zeros(batch, max_ctx, max(cfg.indexer_dim, 1), dtype=torch.uint8, device=dev)
             self.pos_host = [0] * batch
         else:
             self.pos_dev = _share.pos_dev.clone()
@@ -264,7 +264,7 @@ class DeviceCache:
                 si += 1
         shared = {"k": self.kv_k[b, :pos].float().cpu()[None], "v": self.kv_v[b, :pos].float().cpu()[None]}
         if cfg.sparse_topk is not None:
-            raw = self.kv_ik[b, :pos, :cfg.indexer_dim].contiguous().cpu()
+            raw = self.kv_ik[b, :pos].contiguous().cpu()
             shared["ik"] = raw.view(torch.float8_e4m3fn).float()[None]
         return {"layers": layers, "shared": shared, "pos": pos}
 

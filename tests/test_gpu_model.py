@@ -70,9 +70,15 @@ def test_prefill_decode_verify_match_oracle(name, prompt_len, steps):
     for i, (a, b) in enumerate(zip(exp["layers"], o_ref.cache.layers)):
         for key in a:
             torch.testing.assert_close(a[key], b[key].float(), rtol=2e-2, atol=2e-2, msg=f"layer {i} {key}")
-    for key in exp["shared"]:
+    for key in ("k", "v"):
         torch.testing.assert_close(exp["shared"][key], o_ref.cache.shared[key].float(), rtol=5e-2, atol=5e-2,
                                    msg=f"shared {key}")
+    if "ik" in exp["shared"]:
+        # E4M3 keys: a last-bit difference before rounding can move a key by one E4M3 step
+        # (<= 1/8 relative, 2^-9 absolute near zero); nearly all keys must be identical
+        a, b = exp["shared"]["ik"], o_ref.cache.shared["ik"].float()
+        assert ((a - b).abs() <= b.abs() / 8 + 2.0**-9).all()
+        assert (a == b).float().mean() > 0.97
     assert eng.read_status(cache) == 0
 
 
