@@ -21,11 +21,13 @@ CB_SWA_EXTRA = 16
 CB_LAYER_GDN, CB_LAYER_SWA = 0, 1
 
 STATUS = {0: "ok", 1: "invalid argument", 2: "shape not supported", 3: "CUDA launch failed",
-          4: "workspace too small", 5: "context full (position >= max_ctx)", 6: "token id outside the vocabulary"}
+          4: "workspace too small", 5: "context full (position >= max_ctx)", 6: "token id outside the vocabulary",
+          7: "rows * max_ctx exceeds the static scratch of cb_indexer_topk_noalloc"}
+CB_NOALLOC_MAX_SCORES = 1 << 20
 
 EXPORTS = ("cb_abi_version", "cb_status_string", "cb_nvfp4_quantize", "cb_nvfp4_pack_tiles", "cb_gemv_nvfp4",
            "cb_embed", "cb_argmax", "cb_gdn_step", "cb_indexer_topk", "cb_workspace_bytes", "cb_forward",
-           "cb_read_status", "cb_clear_status", "cb_launch_count")
+           "cb_read_status", "cb_clear_status", "cb_launch_count", "cb_indexer_topk_noalloc")
 
 P = C.c_void_p
 I32 = C.c_int32
@@ -97,6 +99,7 @@ def lib() -> C.CDLL:
         L.cb_argmax.argtypes = [P, I32, I32, I32, P, P]
         L.cb_gdn_step.argtypes = [C.POINTER(CbModel), I32, P, I32, I32, I32, P, C.c_int64, P, C.c_int64, P, I32, P]
         L.cb_indexer_topk.argtypes = [P, P, I32, P, I32, I32, I32, P, P, I32, I32, P, P, P, P]
+        L.cb_indexer_topk_noalloc.argtypes = [P, P, I32, P, I32, I32, I32, P, P, I32, I32, P, P, P]
         L.cb_workspace_bytes.restype = C.c_size_t
         L.cb_workspace_bytes.argtypes = [C.POINTER(CbModel), I32, I32, I32]
         L.cb_forward.argtypes = [C.POINTER(CbModel), C.POINTER(CbCache), P, C.c_size_t, P, I32, I32, P, P, P, P]

@@ -160,6 +160,7 @@ extern "C" const char* cb_status_string(int code) {
     case CB_ERR_WORKSPACE: return "workspace too small";
     case CB_ERR_CTX_FULL: return "context full (position >= max_ctx)";
     case CB_ERR_TOKEN: return "token id outside the vocabulary";
+    case CB_ERR_TOO_LARGE: return "rows * max_ctx exceeds the static scratch of cb_indexer_topk_noalloc";
     default: return "unknown status";
   }
 }

@@ -12,6 +12,7 @@
 // order-preserving 32-bit key of each score; the ties at that score are then
 // taken from the highest index down.
 #include <algorithm>
+#include <mutex>
 
 #include "attn.cuh"
 #include "common.cuh"
@@ -248,6 +249,65 @@ extern "C" int cb_indexer_topk(const float* iq, const float* iw, int32_t ld_q, c
   p.rows = rows;
   p.k = k;
   p.scores = scores;
+  p.sel_idx = sel_idx;
+  p.sel_ld = k + 1;
+  p.sel_cnt = sel_cnt;
+  return launch_indexer_topk(p, (cudaStream_t)stream);
+}
+
+// ------------------------------------------------ no-allocation variant
+// Score scratch owned by the library for cb_indexer_topk_noalloc, for callers
+// that cannot allocate device memory.  In host code the name of this array is
+// only a host-side stand-in, never a device address: the device address is
+// looked up per device with cudaGetSymbolAddress (with that device current)
+// and passed to the kernels.
+static __device__ __align__(256) float g_noalloc_scores[CB_NOALLOC_MAX_SCORES];
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+float* g_noalloc_addr[kNoAllocMaxDevices] = {};
+
+// Device address of g_noalloc_scores on the current device (looked up once per device).
+int noalloc_scratch(float** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CB_ERR_CUDA;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return CB_ERR_ARG;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* addr = nullptr;
+    if (cudaGetSymbolAddress(&addr, g_noalloc_scores) != cudaSuccess || addr == nullptr) return CB_ERR_CUDA;
+    g_noalloc_addr[dev] = static_cast<float*>(addr);
+  }
+  *out = g_noalloc_addr[dev];
+  return CB_OK;
+}
+}  // namespace
+
+extern "C" int cb_indexer_topk_noalloc(const float* iq, const float* iw, int32_t ld_q, const uint8_t* ik,
+                                       int32_t max_ctx, int32_t Hi, int32_t Di, const int32_t* seq,
+                                       const int32_t* qpos, int32_t rows, int32_t k, int32_t* sel_idx,
+                                       int32_t* sel_cnt, void* stream) {
+  if (!iq || !iw || !ik || !seq || !qpos || !sel_idx || !sel_cnt || rows <= 0 || k <= 0 || max_ctx <= 0)
+    return CB_ERR_ARG;
+  if ((int64_t)rows * max_ctx > (int64_t)CB_NOALLOC_MAX_SCORES) return CB_ERR_TOO_LARGE;
+  float* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != CB_OK) return rc;
+  IndexerParams p{};
+  p.iq = iq;
+  p.iw = iw;
+  p.ld_q = ld_q;
+  p.ik = ik;
+  p.ik_seq_stride = (int64_t)max_ctx * Di;
+  p.Hi = Hi;
+  p.Di = Di;
+  p.max_ctx = max_ctx;
+  p.seq_arr = seq;
+  p.qpos_arr = qpos;
+  p.rows = rows;
+  p.k = k;
+  p.scores = scratch;
   p.sel_idx = sel_idx;
   p.sel_ld = k + 1;
   p.sel_cnt = sel_cnt;

@@ -44,7 +44,8 @@ enum {
   CB_ERR_CUDA = 3,        /* a launch failed (cudaGetLastError) */
   CB_ERR_WORKSPACE = 4,   /* workspace smaller than cb_workspace_bytes */
   CB_ERR_CTX_FULL = 5,    /* device status: a position reached max_ctx */
-  CB_ERR_TOKEN = 6        /* device status: token id outside the vocabulary */
+  CB_ERR_TOKEN = 6,       /* device status: token id outside the vocabulary */
+  CB_ERR_TOO_LARGE = 7    /* request larger than the static scratch of cb_indexer_topk_noalloc */
 };
 
 enum { CB_LAYER_GDN = 0, CB_LAYER_SWA = 1 };
@@ -178,6 +179,28 @@ int cb_gdn_step(const CbModel* m, int32_t layer, const float* proj, int32_t ldp,
 int cb_indexer_topk(const float* iq, const float* iw, int32_t ld_q, const uint8_t* ik, int32_t max_ctx,
                     int32_t Hi, int32_t Di, const int32_t* seq, const int32_t* qpos, int32_t rows, int32_t k,
                     float* scores, int32_t* sel_idx, int32_t* sel_cnt, void* stream);
+
+/* cb_indexer_topk for callers that cannot allocate device memory when they
+ * call: for example a serving process whose memory planner hands out every
+ * device byte at start-up and forbids allocation afterwards, or a binding in
+ * another language that receives only the input and output buffers from its
+ * host runtime and has no device allocator to call.  No counterpart in the
+ * reference: it is cb_indexer_topk with the `scores` scratch taken from a
+ * static array inside the library (CB_NOALLOC_MAX_SCORES float32 values =
+ * 4 MiB per GPU that loads the library, held until the process exits), so the
+ * caller passes only inputs and outputs and nothing is allocated.
+ *   - rows * max_ctx must be <= CB_NOALLOC_MAX_SCORES, else CB_ERR_TOO_LARGE and
+ *     nothing is launched (e.g. 8 query rows at 128K context, 32 at 32K);
+ *   - the first call on each device looks the array up on that device (make
+ *     that first call before any stream capture on the device);
+ *   - every call on a device shares the one array and it keeps the last call's
+ *     scores; nothing in it needs to start at zero (each call writes every
+ *     score it reads), but calls that overlap on the GPU (other streams, or
+ *     other threads' streams) race on it and must be serialised by the caller. */
+#define CB_NOALLOC_MAX_SCORES (1 << 20)
+int cb_indexer_topk_noalloc(const float* iq, const float* iw, int32_t ld_q, const uint8_t* ik, int32_t max_ctx,
+                            int32_t Hi, int32_t Di, const int32_t* seq, const int32_t* qpos, int32_t rows,
+                            int32_t k, int32_t* sel_idx, int32_t* sel_cnt, void* stream);
 
 /* ------------------------------------------------------- whole forward */
 /* Workspace bytes cb_forward needs for `batch` sequences and up to T tokens
