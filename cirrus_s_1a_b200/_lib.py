@@ -22,7 +22,9 @@ CB_LAYER_GDN, CB_LAYER_SWA = 0, 1
 
 STATUS = {0: "ok", 1: "invalid argument", 2: "shape not supported", 3: "CUDA launch failed",
           4: "workspace too small", 5: "context full (position >= max_ctx)", 6: "token id outside the vocabulary",
-          7: "rows * max_ctx exceeds the static scratch of cb_indexer_topk_noalloc"}
+          7: "rows * max_ctx exceeds the static scratch of cb_indexer_topk_noalloc",
+          8: "a bounded wait in the persistent kernel timed out"}
+CB_PATH_AUTO, CB_PATH_MULTI_KERNEL = 0, 1
 CB_NOALLOC_MAX_SCORES = 1 << 20
 
 EXPORTS = ("cb_abi_version", "cb_status_string", "cb_nvfp4_quantize", "cb_nvfp4_pack_tiles", "cb_gemv_nvfp4",
@@ -56,6 +58,7 @@ class CbModel(C.Structure):
         ("swa_window", I32), ("sparse_topk", I32),
         ("indexer_heads", I32), ("indexer_dim", I32), ("ffn_hidden", I32),
         ("norm_eps", C.c_float),
+        ("forward_path", I32),
         ("inv_freq", P),
         ("gdn_off_gate", I32), ("gdn_off_a", I32), ("gdn_off_b", I32),
         ("swa_off_kv", I32), ("swa_off_gate", I32),
@@ -110,7 +113,7 @@ def lib() -> C.CDLL:
         for name in EXPORTS:
             if name not in ("cb_status_string", "cb_workspace_bytes", "cb_launch_count"):
                 getattr(L, name).restype = C.c_int
-        if L.cb_abi_version() != 1:
+        if L.cb_abi_version() != 2:
             raise CbError("libcirrus_b200.so ABI version mismatch")
         _lib = L
     return _lib

@@ -17,6 +17,7 @@
 #include "attn.cuh"
 #include "common.cuh"
 #include "gdn.cuh"
+#include "mk.cuh"
 #include "nvfp4.cuh"
 
 namespace cb {
@@ -39,13 +40,26 @@ struct Workspace {
   int32_t* sel_cnt;
   float* logits;
   int32_t* amax;
+  // persistent kernel
+  float* part2;
+  unsigned* hist;
+  int32_t* hi_list;
+  int32_t* hi_cnt;
+  unsigned long long* cand;
+  int32_t* cand_cnt;
+  unsigned* arrive;
+  unsigned long long* amax64;
+  unsigned* sync;     // [0] barrier counter, [32] abort flag
   size_t bytes;
-  int ldp, att_ld, cr_ld, n_splits, sel_ld;
+  int ldp, att_ld, cr_ld, n_splits, sel_ld, cross_splits;
 };
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 static int swa_splits(const CbModel& m) { return ceil_div(m.swa_window + CB_MAX_T, kSwaSplit); }
+static int cross_splits(const CbModel& m) {
+  return m.sparse_topk > 0 ? ceil_div(m.sparse_topk + 1, kMkCrossSplit) : 32;
+}
 
 static Workspace carve(const CbModel& m, int batch, int T, int max_ctx, char* base) {
   Workspace w{};
@@ -77,6 +91,17 @@ static Workspace carve(const CbModel& m, int batch, int T, int max_ctx, char* ba
   w.sel_cnt = (int32_t*)take(sizeof(int32_t) * R);
   w.logits = (float*)take(sizeof(float) * R * (size_t)m.vocab_size);
   w.amax = (int32_t*)take(sizeof(int32_t) * R);
+  w.cross_splits = cross_splits(m);
+  w.part2 = (float*)take(sizeof(float) * R * m.n_q_heads * w.cross_splits * (m.head_dim + 2));
+  const bool sp = m.sparse_topk > 0;
+  w.hist = (unsigned*)take(sp ? sizeof(unsigned) * R * kMkHistBins : 0);
+  w.hi_list = (int32_t*)take(sp ? sizeof(int32_t) * R * (size_t)m.sparse_topk : 0);
+  w.hi_cnt = (int32_t*)take(sizeof(int32_t) * R);
+  w.cand = (unsigned long long*)take(sp ? sizeof(unsigned long long) * R * (size_t)max_ctx : 0);
+  w.cand_cnt = (int32_t*)take(sizeof(int32_t) * R);
+  w.arrive = (unsigned*)take(sizeof(unsigned) * kMkArrive);
+  w.amax64 = (unsigned long long*)take(sizeof(unsigned long long) * R);
+  w.sync = (unsigned*)take(256);
   w.bytes = off;
   return w;
 }
@@ -131,6 +156,53 @@ static int ffn(const CbMatrix& gate_up, const CbMatrix& down, const float* norm2
   return gemv(down, w.gu, F2, rows, nullptr, 0.f, PRE_SWIGLU, EPI_ADD, x, d, d, st);
 }
 
+static int launch_persistent(const CbModel& m, const CbCache& c, const Workspace& w, const int64_t* ids, int T, int nq,
+                             float* logits, float* hidden, int32_t* argmax, cudaStream_t st) {
+  MkArgs a{};
+  a.m = m;
+  a.c = c;
+  a.h = w.h;
+  a.proj = w.proj;
+  a.attn = w.attn;
+  a.act = w.gu;
+  a.xc = w.xc;
+  a.cproj = w.cproj;
+  a.part = w.part;
+  a.part2 = w.part2;
+  a.scores = w.scores;
+  a.ws_logits = w.logits;
+  a.hist = w.hist;
+  a.hi_list = w.hi_list;
+  a.hi_cnt = w.hi_cnt;
+  a.cand = w.cand;
+  a.cand_cnt = w.cand_cnt;
+  a.sel_idx = w.sel_idx;
+  a.sel_cnt = w.sel_cnt;
+  a.arrive = w.arrive;
+  a.amax = w.amax64;
+  a.sync = w.sync;
+  a.abort_flag = reinterpret_cast<int32_t*>(w.sync + 32);
+  a.status = w.status;
+  a.ldp = w.ldp;
+  a.att_ld = w.att_ld;
+  a.cr_ld = w.cr_ld;
+  a.sel_ld = w.sel_ld;
+  a.swa_splits = ceil_div(m.swa_window + CB_MAX_T, kMkSwaSplit);
+  a.cross_splits = w.cross_splits;
+  a.ids = ids;
+  a.ids_ld = T;
+  a.c0 = 0;
+  a.B = c.batch;
+  a.T = T;
+  a.nq = nq;
+  a.logits = logits;
+  a.hidden = hidden;
+  a.argmax = argmax;
+  a.timeout_ns = 200ull * 1000 * 1000;
+  if (cudaMemsetAsync(w.sync, 0, 256, st) != cudaSuccess) return CB_ERR_CUDA;
+  return launch_mk(a, num_sms(), st);
+}
+
 static int validate(const CbModel& m, const CbCache& c) {
   if (m.n_self_layers <= 0 || m.n_self_layers > CB_MAX_SELF || m.n_cross_layers <= 0 ||
       m.n_cross_layers > CB_MAX_CROSS || m.d_model <= 0 || m.d_model % 16 || m.vocab_size <= 0)
@@ -161,6 +233,7 @@ extern "C" const char* cb_status_string(int code) {
     case CB_ERR_CTX_FULL: return "context full (position >= max_ctx)";
     case CB_ERR_TOKEN: return "token id outside the vocabulary";
     case CB_ERR_TOO_LARGE: return "rows * max_ctx exceeds the static scratch of cb_indexer_topk_noalloc";
+    case CB_ERR_TIMEOUT: return "a bounded wait in the persistent kernel timed out";
     default: return "unknown status";
   }
 }
@@ -202,6 +275,11 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
   const int64_t gdn_conv_layer = (int64_t)(m.conv_size - 1) * C;
   const int64_t swa_layer = (int64_t)c.swa_slots * m.n_kv_heads * m.head_dim;
   const int64_t kv_seq = (int64_t)c.max_ctx * m.n_kv_heads * m.head_dim;
+
+  if (m.forward_path != CB_PATH_MULTI_KERNEL && T <= CB_MAX_T && mk_supported(m, c, T, nq)) {
+    const int rc = launch_persistent(m, c, w, ids, T, nq, logits, hidden, argmax, st);
+    if (rc != CB_ERR_SHAPE) return rc;  // CB_ERR_SHAPE: not co-resident on this device, use one launch per op
+  }
 
   for (int c0 = 0; c0 < T; c0 += Tc) {
     const int tc = std::min(Tc, T - c0);

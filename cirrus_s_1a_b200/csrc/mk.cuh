@@ -1,0 +1,60 @@
+// Persistent decode kernel: launch interface (decode_mk.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "cirrus_b200.h"
+
+namespace cb {
+
+constexpr int kMkThreads = 512;
+constexpr int kMkHistBins = 2048;      // top 11 bits of the score key
+constexpr int kMkSwaSplit = 128;       // window keys per SWA work item
+constexpr int kMkCrossSplit = 64;      // selected keys per cross-attention work item
+constexpr int kMkMaxRows = 8;          // batch * T handled by one persistent launch
+constexpr int kMkMaxQ = 24;            // (q heads per KV head) * T per SWA work item
+constexpr int kMkArrive = 512;         // last-arriver counters
+
+// Everything one persistent launch needs, passed by value (__grid_constant__).
+struct MkArgs {
+  CbModel m;
+  CbCache c;
+  // workspace
+  float* h;          // [M][d] residual stream of the self-decoder
+  float* proj;       // [M][ldp]
+  float* attn;       // [M][att_ld]
+  float* act;        // [M][ffn]   silu(gate) * up
+  float* xc;         // [RQ][d]   cross-decoder residual stream
+  float* cproj;      // [RQ][cr_ld]
+  float* part;       // SWA partials [M][Hq][swa_splits][hd + 2]
+  float* part2;      // cross partials [RQ][Hq][cross_splits][hd + 2]
+  float* scores;     // [RQ][max_ctx]
+  float* ws_logits;  // [RQ][vocab] when the caller passes no logits buffer
+  unsigned* hist;    // [RQ][kMkHistBins]
+  int32_t* hi_list;  // [RQ][k]  keys above the threshold bin
+  int32_t* hi_cnt;   // [RQ]
+  unsigned long long* cand;  // [RQ][max_ctx]  (key << 32 | index) in the threshold bin
+  int32_t* cand_cnt; // [RQ]
+  int32_t* sel_idx;  // [RQ][sel_ld]
+  int32_t* sel_cnt;  // [RQ]
+  unsigned* arrive;  // [kMkArrive]
+  unsigned long long* amax;  // [RQ] packed argmax
+  unsigned* sync;    // grid barrier counter (zeroed before every launch)
+  int32_t* abort_flag;
+  int32_t* status;
+  int ldp, att_ld, cr_ld, sel_ld, swa_splits, cross_splits;
+  // this launch
+  const int64_t* ids;
+  int ids_ld, c0, B, T, nq;  // rows b*T + t; cross rows = last nq of each sequence
+  float* logits;     // [RQ][vocab] or null
+  float* hidden;     // [RQ][d] or null
+  int32_t* argmax;   // [RQ] or null
+  unsigned long long timeout_ns;
+};
+
+size_t mk_smem_bytes();
+bool mk_supported(const CbModel& m, const CbCache& c, int T, int nq);
+int launch_mk(const MkArgs& a, int grid, cudaStream_t st);
+
+}  // namespace cb

@@ -82,7 +82,7 @@ class PackedMatrix:
 class DeviceModel:
     """NVFP4 weights of one model on one CUDA device plus its ``CbModel`` descriptor."""
 
-    def __init__(self, cfg, sd: dict, device, tensor_scale: float = 1.0):
+    def __init__(self, cfg, sd: dict, device, tensor_scale: float = 1.0, path: str = "auto"):
         self.cfg = cfg
         self.device = torch.device(device)
         dev = self.device
@@ -102,6 +102,7 @@ class DeviceModel:
         m.sparse_topk = 0 if cfg.sparse_topk is None else cfg.sparse_topk
         m.indexer_heads, m.indexer_dim, m.ffn_hidden = cfg.indexer_heads, cfg.indexer_dim, cfg.ffn_hidden
         m.norm_eps = cfg.norm_eps
+        m.forward_path = {"auto": _lib.CB_PATH_AUTO, "multi": _lib.CB_PATH_MULTI_KERNEL}[path]
         inv = f32(inv_freq_of(cfg))
         self._keep.append(inv)
         m.inv_freq = inv.data_ptr()
@@ -284,9 +285,13 @@ class CirrusB200:
 
     ``CirrusB200(cfg, state_dict)`` takes a reference ``state_dict`` (float
     weights; the reference key names) and quantises every Linear to NVFP4.
+    ``path="auto"`` runs a chunk of up to 8 rows (batch * tokens) as one
+    persistent launch and larger chunks as one launch per op; ``path="multi"``
+    always uses one launch per op.
     """
 
-    def __init__(self, cfg, state_dict: dict, device="cuda", max_ctx: int | None = None, tensor_scale: float = 1.0):
+    def __init__(self, cfg, state_dict: dict, device="cuda", max_ctx: int | None = None, tensor_scale: float = 1.0,
+                 path: str = "auto"):
         if not torch.cuda.is_available():
             raise _lib.CbError("CirrusB200 needs a CUDA device (there is no CPU path)")
         _lib.lib()
@@ -296,7 +301,7 @@ class CirrusB200:
             self.device = torch.device("cuda", torch.cuda.current_device())
         self.max_ctx = max_ctx or cfg.max_seq_len
         with torch.cuda.device(self.device):
-            self.model = DeviceModel(cfg, state_dict, self.device, tensor_scale)
+            self.model = DeviceModel(cfg, state_dict, self.device, tensor_scale, path)
         self.draft_ids = state_dict.get("draft_ids", torch.arange(min(cfg.mtp_draft_vocab, cfg.vocab_size)))
         self._ws: dict = {}
 

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define CB_ABI_VERSION 1
+#define CB_ABI_VERSION 2
 #define CB_MAX_SELF 32   /* self-decoder layers */
 #define CB_MAX_CROSS 16  /* cross-decoder layers */
 #define CB_MAX_T 8       /* tokens per sequence per launch chunk (1 + draft) */
@@ -45,8 +45,11 @@ enum {
   CB_ERR_WORKSPACE = 4,   /* workspace smaller than cb_workspace_bytes */
   CB_ERR_CTX_FULL = 5,    /* device status: a position reached max_ctx */
   CB_ERR_TOKEN = 6,       /* device status: token id outside the vocabulary */
-  CB_ERR_TOO_LARGE = 7    /* request larger than the static scratch of cb_indexer_topk_noalloc */
+  CB_ERR_TOO_LARGE = 7,   /* request larger than the static scratch of cb_indexer_topk_noalloc */
+  CB_ERR_TIMEOUT = 8      /* device status: a bounded wait in the persistent kernel gave up */
 };
+
+enum { CB_PATH_AUTO = 0, CB_PATH_MULTI_KERNEL = 1 };
 
 enum { CB_LAYER_GDN = 0, CB_LAYER_SWA = 1 };
 
@@ -97,6 +100,9 @@ typedef struct CbModel {
   int32_t swa_window, sparse_topk;            /* sparse_topk 0 = dense cross attention */
   int32_t indexer_heads, indexer_dim, ffn_hidden;
   float norm_eps;
+  int32_t forward_path;                       /* CB_PATH_AUTO: one persistent launch per chunk when
+                                                 batch*T <= 8, else one launch per op; CB_PATH_MULTI_KERNEL:
+                                                 always one launch per op */
   const float* inv_freq;                      /* [rot_dim/2], as layers.py:69 computes it */
   /* column offsets inside the concatenated projection outputs (each segment
    * starts on a multiple of 16) */

@@ -17,12 +17,15 @@ pytestmark = pytest.mark.gpu
 RTOL, ATOL = 1e-2, 2e-2
 
 
-def _setup(cfg, seed=0, max_ctx=512):
+PATHS = ["auto", "multi"]  # persistent launch per chunk / one launch per op
+
+
+def _setup(cfg, seed=0, max_ctx=512, path="auto"):
     from cirrus_s_1a_b200 import synthetic
     from cirrus_s_1a_b200.engine import CirrusB200
 
     sd = synthetic.random_state_dict(cfg, seed=seed, norm_jitter=0.1)
-    eng = CirrusB200(cfg, sd, max_ctx=max_ctx)
+    eng = CirrusB200(cfg, sd, max_ctx=max_ctx, path=path)
     return eng, om.quantized_params(sd)
 
 
@@ -40,12 +43,13 @@ def _close(a, b, what):
     torch.testing.assert_close(a, b, rtol=RTOL, atol=ATOL, msg=lambda m: f"{what}: max abs err {err}\n{m}")
 
 
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("name,prompt_len,steps", [("debug", 20, 12), ("debug_dense", 13, 6), ("baseline", 70, 6)])
-def test_prefill_decode_verify_match_oracle(name, prompt_len, steps):
+def test_prefill_decode_verify_match_oracle(name, prompt_len, steps, path):
     from cirrus_s_1a_b200 import synthetic
 
     cfg = _cfgs()[name]
-    eng, p = _setup(cfg, seed=1)
+    eng, p = _setup(cfg, seed=1, path=path)
     prompt = synthetic.random_prompt(prompt_len, cfg.vocab_size, seed=2)
     ids = torch.tensor([prompt])
     o_ref = om.forward(p, cfg, ids, use_cache=True, n_logits=1, casts=om.B200)
@@ -93,11 +97,12 @@ def test_long_prompt_chunks_and_full_logits():
     _close(o.logits, o_ref.logits[:, -11:], "last 11 logits")
 
 
-def test_batched_sequences_match_individual_runs():
+@pytest.mark.parametrize("path", PATHS)
+def test_batched_sequences_match_individual_runs(path):
     from cirrus_s_1a_b200 import synthetic
 
     cfg = _cfgs()["baseline"]
-    eng, p = _setup(cfg, seed=5)
+    eng, p = _setup(cfg, seed=5, path=path)
     prompts = [synthetic.random_prompt(24, cfg.vocab_size, seed=s) for s in (10, 11, 12)]
     o = eng(torch.tensor(prompts), use_cache=True, n_logits=2)
     cache = o.cache
@@ -121,11 +126,12 @@ def _tokens_agree(gpu, ref_tokens, margins):
     return len(gpu)
 
 
-def test_greedy_speculative_and_oracle_agree():
+@pytest.mark.parametrize("path", PATHS)
+def test_greedy_speculative_and_oracle_agree(path):
     from cirrus_s_1a_b200 import generate as G
 
     cfg = _cfgs()["debug"]
-    eng, p = _setup(cfg, seed=6)
+    eng, p = _setup(cfg, seed=6, path=path)
     g = torch.Generator().manual_seed(8)
     base = torch.randint(0, cfg.vocab_size, (12,), generator=g).tolist()
     prompt = base + torch.randint(0, cfg.vocab_size, (5,), generator=g).tolist() + base[:4]
@@ -145,11 +151,12 @@ def test_greedy_speculative_and_oracle_agree():
     _tokens_agree(ref, toks, margins)
 
 
-def test_graph_replay_matches_eager():
+@pytest.mark.parametrize("path", PATHS)
+def test_graph_replay_matches_eager(path):
     from cirrus_s_1a_b200.engine import DecodeGraph
 
     cfg = _cfgs()["baseline"]
-    eng, _ = _setup(cfg, seed=9)
+    eng, _ = _setup(cfg, seed=9, path=path)
     prompt = torch.randint(0, cfg.vocab_size, (1, 33), generator=torch.Generator().manual_seed(1))
     o1 = eng(prompt, use_cache=True, n_logits=1)
     o2 = eng(prompt, use_cache=True, n_logits=1)
@@ -174,3 +181,27 @@ def test_context_full_is_rejected_on_host():
     o = eng(torch.zeros(1, 10, dtype=torch.long), use_cache=True, n_logits=1)
     with pytest.raises(CbError):
         eng(torch.zeros(1, 7, dtype=torch.long), cache=o.cache, n_logits=1)
+
+
+def test_persistent_and_multikernel_paths_agree_at_long_context():
+    """The same 2K-context cache decoded by both GPU paths (one persistent launch
+    per step vs one launch per op) gives the same logits and selections."""
+    from cirrus_s_1a_b200 import synthetic
+
+    cfg = _cfgs()["baseline"]
+    sd = synthetic.random_state_dict(cfg, seed=11, norm_jitter=0.1)
+    from cirrus_s_1a_b200.engine import CirrusB200
+
+    engines = [CirrusB200(cfg, sd, max_ctx=4096, path=pth) for pth in PATHS]
+    g = torch.Generator().manual_seed(3)
+    prompt = torch.randint(0, cfg.vocab_size, (1, 2000), generator=g)
+    outs = [e(prompt, use_cache=True, n_logits=1) for e in engines]
+    _close(outs[0].logits, outs[1].logits, "prefill")
+    caches = [o.cache for o in outs]
+    tok = int(outs[1].logits[0, -1].argmax())
+    for s in range(4):
+        o = [e(torch.tensor([[tok]]), cache=c, n_logits=1) for e, c in zip(engines, caches)]
+        _close(o[0].logits, o[1].logits, f"step {s}")
+        tok = int(o[1].logits[0, -1].argmax())
+    for e, c in zip(engines, caches):
+        assert e.read_status(c) == 0
