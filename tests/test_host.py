@@ -44,7 +44,7 @@ def test_library_exports_every_header_symbol(built_lib):
     for n in names:
         assert hasattr(built_lib, n), n
     assert set(names) == set(_lib.EXPORTS)
-    assert built_lib.cb_abi_version() == 1
+    assert built_lib.cb_abi_version() == 2
     assert built_lib.cb_status_string(5) == b"context full (position >= max_ctx)"
 
 
