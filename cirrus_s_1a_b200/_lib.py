@@ -29,7 +29,7 @@ CB_NOALLOC_MAX_SCORES = 1 << 20
 
 EXPORTS = ("cb_abi_version", "cb_status_string", "cb_nvfp4_quantize", "cb_nvfp4_pack_tiles", "cb_gemv_nvfp4",
            "cb_embed", "cb_argmax", "cb_gdn_step", "cb_indexer_topk", "cb_workspace_bytes", "cb_forward",
-           "cb_read_status", "cb_clear_status", "cb_launch_count", "cb_indexer_topk_noalloc")
+           "cb_read_status", "cb_clear_status", "cb_launch_count", "cb_indexer_topk_noalloc", "cb_read_trace")
 
 P = C.c_void_p
 I32 = C.c_int32
@@ -108,6 +108,7 @@ def lib() -> C.CDLL:
         L.cb_forward.argtypes = [C.POINTER(CbModel), C.POINTER(CbCache), P, C.c_size_t, P, I32, I32, P, P, P, P]
         L.cb_read_status.argtypes = [P, C.POINTER(I32), P]
         L.cb_clear_status.argtypes = [P, P]
+        L.cb_read_trace.argtypes = [C.POINTER(CbModel), I32, I32, I32, P, P, I32, P]
         L.cb_launch_count.restype = C.c_int64
         L.cb_launch_count.argtypes = []
         for name in EXPORTS:

@@ -58,6 +58,8 @@ __device__ bool grid_sync(const MkArgs& a, unsigned& gen, int* s_ok) {
   if (threadIdx.x == 0) {
     gen += 1;
     const unsigned target = gen * gridDim.x;
+    const bool tr = blockIdx.x == 0 && 2 * gen < (unsigned)kMkTrace;
+    if (tr) a.trace[2 * gen - 1] = gtimer();
     __threadfence();
     atomicAdd(a.sync, 1u);
     int ok = 1;
@@ -77,6 +79,7 @@ __device__ bool grid_sync(const MkArgs& a, unsigned& gen, int* s_ok) {
         }
       }
     }
+    if (tr) a.trace[2 * gen] = gtimer();
     *s_ok = ok;
   }
   __syncthreads();
@@ -1093,7 +1096,10 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     }
     for (int i = tid; i < kMkArrive; i += kT) a.arrive[i] = 0u;
   }
-  if (tid == 0) prefetch_all(a);
+  if (tid == 0) {
+    if (cta == 0) a.trace[0] = gtimer();
+    prefetch_all(a);
+  }
   if (!grid_sync(a, gen, &s_ok)) return;
 
   for (int i = 0; i < m.n_self_layers; ++i) {

@@ -50,6 +50,7 @@ struct Workspace {
   unsigned* arrive;
   unsigned long long* amax64;
   unsigned* sync;     // [0] barrier counter, [32] abort flag
+  unsigned long long* trace;
   size_t bytes;
   int ldp, att_ld, cr_ld, n_splits, sel_ld, cross_splits;
 };
@@ -102,6 +103,7 @@ static Workspace carve(const CbModel& m, int batch, int T, int max_ctx, char* ba
   w.arrive = (unsigned*)take(sizeof(unsigned) * kMkArrive);
   w.amax64 = (unsigned long long*)take(sizeof(unsigned long long) * R);
   w.sync = (unsigned*)take(256);
+  w.trace = (unsigned long long*)take(sizeof(unsigned long long) * kMkTrace);
   w.bytes = off;
   return w;
 }
@@ -181,6 +183,7 @@ static int launch_persistent(const CbModel& m, const CbCache& c, const Workspace
   a.arrive = w.arrive;
   a.amax = w.amax64;
   a.sync = w.sync;
+  a.trace = w.trace;
   a.abort_flag = reinterpret_cast<int32_t*>(w.sync + 32);
   a.status = w.status;
   a.ldp = w.ldp;
@@ -249,6 +252,18 @@ extern "C" int cb_read_status(const void* workspace, int32_t* status, void* stre
       cudaSuccess)
     return CB_ERR_CUDA;
   return cudaStreamSynchronize((cudaStream_t)stream) == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
+
+extern "C" int cb_read_trace(const CbModel* m, int32_t batch, int32_t T, int32_t max_ctx, const void* workspace,
+                             uint64_t* out, int32_t n, void* stream) {
+  if (!m || !workspace || !out || n <= 0 || batch <= 0 || max_ctx <= 0) return -CB_ERR_ARG;
+  const Workspace w = carve(*m, batch, T, max_ctx, (char*)workspace);
+  const int cnt = std::min(n, kMkTrace);
+  if (cudaMemcpyAsync(out, w.trace, sizeof(uint64_t) * cnt, cudaMemcpyDeviceToHost, (cudaStream_t)stream) !=
+      cudaSuccess)
+    return -CB_ERR_CUDA;
+  if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return -CB_ERR_CUDA;
+  return cnt;
 }
 
 extern "C" int cb_clear_status(void* workspace, void* stream) {

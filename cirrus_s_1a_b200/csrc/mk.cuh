@@ -15,6 +15,7 @@ constexpr int kMkCrossSplit = 64;      // selected keys per cross-attention work
 constexpr int kMkMaxRows = 8;          // batch * T handled by one persistent launch
 constexpr int kMkMaxQ = 24;            // (q heads per KV head) * T per SWA work item
 constexpr int kMkArrive = 512;         // last-arriver counters
+constexpr int kMkTrace = 512;          // phase timestamps
 
 // Everything one persistent launch needs, passed by value (__grid_constant__).
 struct MkArgs {
@@ -41,6 +42,7 @@ struct MkArgs {
   unsigned* arrive;  // [kMkArrive]
   unsigned long long* amax;  // [RQ] packed argmax
   unsigned* sync;    // grid barrier counter (zeroed before every launch)
+  unsigned long long* trace;  // [kMkTrace] phase timestamps of CTA 0
   int32_t* abort_flag;
   int32_t* status;
   int ldp, att_ld, cr_ld, sel_ld, swa_splits, cross_splits;

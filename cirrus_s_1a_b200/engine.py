@@ -337,6 +337,25 @@ class CirrusB200:
         _lib.check(_lib.lib().cb_read_status(ws.data_ptr(), C.byref(out), _stream_ptr(self.device)), "status")
         return int(out.value)
 
+    def phase_trace(self, cache: DeviceCache, T: int = 1) -> list:
+        """Per-phase timing of the last persistent launch on this cache's workspace:
+        a list of (phase index, CTA-0 work us, barrier wait us) from %globaltimer stamps."""
+        ws = self.workspace(cache.batch, T, cache.max_ctx)
+        buf = (C.c_uint64 * 512)()
+        n = _lib.lib().cb_read_trace(C.byref(self.model.desc), cache.batch, min(T, CB_MAX_T), cache.max_ctx,
+                                     ws.data_ptr(), buf, 512, _stream_ptr(self.device))
+        if n < 0:
+            raise _lib.CbError("cb_read_trace failed")
+        vals = list(buf[:n])
+        out, prev = [], vals[0]
+        for i in range(1, n // 2):
+            arrive, leave = vals[2 * i - 1], vals[2 * i]
+            if arrive == 0 or leave < arrive or arrive < prev:
+                break
+            out.append((i, (arrive - prev) / 1e3, (leave - arrive) / 1e3))
+            prev = leave
+        return out
+
     # ----------------------------------------------------------- forward
     @torch.no_grad()
     def forward(self, input_ids: torch.Tensor, cache: DeviceCache | None = None, use_cache: bool = False,

@@ -231,6 +231,14 @@ int cb_clear_status(void* workspace, void* stream);
 /* Number of kernels this library has launched in this process (all entry points). */
 int64_t cb_launch_count(void);
 
+/* Phase trace of the last persistent launch that used this workspace: out[0] =
+ * %globaltimer (ns) at kernel start, then for barrier i >= 1: out[2i-1] = when
+ * CTA 0 arrived at barrier i, out[2i] = when it left.  Returns the number of
+ * values written (<= n) or a negative CB_ERR code (synchronises on the stream).
+ * (The reference's per-stage clock / globaltimer stamps, bench_kernels.cu:904-988.) */
+int cb_read_trace(const CbModel* m, int32_t batch, int32_t T, int32_t max_ctx, const void* workspace, uint64_t* out,
+                  int32_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
