@@ -32,6 +32,7 @@ constexpr int kT = kMkThreads;
 constexpr int kW = kMkThreads / 32;
 constexpr int kSmem = 160 * 1024;
 constexpr int kMaxSort = 4096;
+constexpr int kMkBitmapWords = 4096;  // selection bitmap: up to 131072 keys
 
 enum { PRE_NONE_ = 0, PRE_RMS_ = 1, PRE_EMBED_ = 2 };
 enum { EPI_STORE_ = 0, EPI_ADD_ = 1, EPI_ACT_ = 2 };
@@ -107,44 +108,50 @@ __device__ void prefetch_share(const void* p, size_t bytes) {
 
 __device__ __forceinline__ size_t matrix_bytes(const CbMatrix& W) { return (size_t)(W.rows / kTileRows) * tile_bytes(W.k); }
 
-// Thread 0 of every CTA: prefetch, in phase order, the weights and the state the step reads.
+// Every thread of every CTA: prefetch, in phase order, the weights and the
+// state the step reads; region r is issued by thread r % kT of each CTA, which
+// takes its 1/gridDim share of the region.
 __device__ void prefetch_all(const MkArgs& a) {
   const CbModel& m = a.m;
   const CbCache& c = a.c;
   const int H = m.gdn_heads, C = 2 * H * m.gdn_dk + H * m.gdn_dv;
+  int r = 0;
+  auto take = [&](const void* p, size_t bytes) {
+    if (r++ % kT == (int)threadIdx.x) prefetch_share(p, bytes);
+  };
   for (int i = 0; i < m.n_self_layers; ++i) {
     const CbSelfLayer& L = m.self_layers[i];
-    prefetch_share(L.in_proj.tiles, matrix_bytes(L.in_proj));
+    take(L.in_proj.tiles, matrix_bytes(L.in_proj));
     for (int b = 0; b < a.B; ++b) {
       if (L.kind == CB_LAYER_GDN) {
         const int64_t slot = (int64_t)b * c.n_gdn + L.slot;
-        prefetch_share(c.gdn_state + slot * H * m.gdn_dk * m.gdn_dv, sizeof(float) * H * m.gdn_dk * m.gdn_dv);
-        prefetch_share(c.gdn_conv + slot * (m.conv_size - 1) * C, sizeof(float) * (m.conv_size - 1) * C);
+        take(c.gdn_state + slot * H * m.gdn_dk * m.gdn_dv, sizeof(float) * H * m.gdn_dk * m.gdn_dv);
+        take(c.gdn_conv + slot * (m.conv_size - 1) * C, sizeof(float) * (m.conv_size - 1) * C);
       } else {
         const int64_t ring = (int64_t)(b * c.n_swa + L.slot) * c.swa_slots * m.n_kv_heads * m.head_dim;
         const size_t bytes = sizeof(uint16_t) * (size_t)c.swa_slots * m.n_kv_heads * m.head_dim;
-        prefetch_share(c.swa_k + ring, bytes);
-        prefetch_share(c.swa_v + ring, bytes);
+        take(c.swa_k + ring, bytes);
+        take(c.swa_v + ring, bytes);
       }
     }
-    prefetch_share(L.o_proj.tiles, matrix_bytes(L.o_proj));
-    prefetch_share(L.gate_up.tiles, matrix_bytes(L.gate_up));
-    prefetch_share(L.down.tiles, matrix_bytes(L.down));
+    take(L.o_proj.tiles, matrix_bytes(L.o_proj));
+    take(L.gate_up.tiles, matrix_bytes(L.gate_up));
+    take(L.down.tiles, matrix_bytes(L.down));
   }
-  prefetch_share(m.shared_proj.tiles, matrix_bytes(m.shared_proj));
+  take(m.shared_proj.tiles, matrix_bytes(m.shared_proj));
   if (m.sparse_topk > 0)
     for (int b = 0; b < a.B; ++b) {
       const int p0 = min(max(c.pos[b] + a.c0, 0), c.max_ctx);
-      prefetch_share(c.kv_ik + (int64_t)b * c.max_ctx * m.indexer_dim, (size_t)p0 * m.indexer_dim);
+      take(c.kv_ik + (int64_t)b * c.max_ctx * m.indexer_dim, (size_t)p0 * m.indexer_dim);
     }
   for (int j = 0; j < m.n_cross_layers; ++j) {
     const CbCrossLayer& L = m.cross_layers[j];
-    prefetch_share(L.q_gate.tiles, matrix_bytes(L.q_gate));
-    prefetch_share(L.o_proj.tiles, matrix_bytes(L.o_proj));
-    prefetch_share(L.gate_up.tiles, matrix_bytes(L.gate_up));
-    prefetch_share(L.down.tiles, matrix_bytes(L.down));
+    take(L.q_gate.tiles, matrix_bytes(L.q_gate));
+    take(L.o_proj.tiles, matrix_bytes(L.o_proj));
+    take(L.gate_up.tiles, matrix_bytes(L.gate_up));
+    take(L.down.tiles, matrix_bytes(L.down));
   }
-  prefetch_share(m.lm_head.tiles, matrix_bytes(m.lm_head));
+  take(m.lm_head.tiles, matrix_bytes(m.lm_head));
 }
 
 // ------------------------------------------------------------------ GEMV
@@ -161,66 +168,51 @@ struct GemvJob {
   bool argmax;
 };
 
-// Two weight rows (a, and b when has_b) against the M input rows in smem.
+// One weight row as seen by one lane: the 8-code chunks lane, lane+32, ...
+// (K <= 2048, so at most 8 chunks), code words and scale bytes.
+struct RowW {
+  uint32_t w[8];
+  uint32_t s[8];
+};
+
+__device__ __forceinline__ void load_row(const CbMatrix& W, int64_t tb, int K, int row, bool valid, RowW& r) {
+  const int lane = threadIdx.x & 31, kc = K >> 3;
+  const uint8_t* t = W.tiles + (int64_t)(row >> 4) * tb;
+  const uint32_t* cw = reinterpret_cast<const uint32_t*>(t + (row & 15) * (K / 2));
+  const uint8_t* sb = t + kTileRows * (K / 2) + (row & 15) * (K / 16);
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int c = u * 32 + lane;
+    const bool ok = valid && c < kc;
+    r.w[u] = ok ? __ldg(cw + c) : 0u;
+    r.s[u] = ok ? (uint32_t)__ldg(sb + (c >> 1)) : 0u;
+  }
+}
+
 template <int M>
-__device__ __forceinline__ void dot_rows(const CbMatrix& W, int64_t tb, int K, int ra, int rb, bool has_b,
-                                         const float* xs, float (&aa)[M], float (&ab)[M]) {
-  const int lane = threadIdx.x & 31;
-  const uint8_t* ta = W.tiles + (int64_t)(ra >> 4) * tb;
-  const uint8_t* tbp = W.tiles + (int64_t)((has_b ? rb : ra) >> 4) * tb;
-  const int rra = ra & 15, rrb = (has_b ? rb : ra) & 15;
-  const uint32_t* ca = reinterpret_cast<const uint32_t*>(ta + rra * (K / 2));
-  const uint32_t* cbw = reinterpret_cast<const uint32_t*>(tbp + rrb * (K / 2));
-  const uint8_t* sa = ta + kTileRows * (K / 2) + rra * (K / 16);
-  const uint8_t* sb = tbp + kTileRows * (K / 2) + rrb * (K / 16);
+__device__ __forceinline__ void dot_row(const RowW& r, int K, const float* xs, float (&acc)[M]) {
+  const int lane = threadIdx.x & 31, kc = K >> 3;
 #pragma unroll
-  for (int m = 0; m < M; ++m) aa[m] = ab[m] = 0.0f;
-  const int kc = K >> 3;
-  for (int c0 = 0; c0 < kc; c0 += 128) {
-    uint32_t wa[4], wb[4], qa[4], qb[4];
+  for (int u = 0; u < 8; ++u) {
+    const int c = u * 32 + lane;
+    if (c < kc) {
+      const float sc = e4m3_to_f32(r.s[u]);
+      float2 f[4];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int c = c0 + u * 32 + lane;
-      const bool ok = c < kc;
-      wa[u] = ok ? __ldg(ca + c) : 0u;
-      qa[u] = ok ? __ldg(sa + (c >> 1)) : 0u;
-      wb[u] = (ok && has_b) ? __ldg(cbw + c) : 0u;
-      qb[u] = (ok && has_b) ? __ldg(sb + (c >> 1)) : 0u;
-    }
+      for (int j = 0; j < 4; ++j) f[j] = e2m1x2_to_f32x2(r.w[u] >> (8 * j));
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int c = c0 + u * 32 + lane;
-      if (c < kc) {
-        const float sca = e4m3_to_f32(qa[u]), scb = e4m3_to_f32(qb[u]);
-        float2 fa[4], fb[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          fa[j] = e2m1x2_to_f32x2(wa[u] >> (8 * j));
-          fb[j] = e2m1x2_to_f32x2(wb[u] >> (8 * j));
-        }
-#pragma unroll
-        for (int m = 0; m < M; ++m) {
-          const float4 x0 = *reinterpret_cast<const float4*>(xs + m * K + c * 8);
-          const float4 x1 = *reinterpret_cast<const float4*>(xs + m * K + c * 8 + 4);
-          float pa = fa[0].x * x0.x;
-          pa = fmaf(fa[0].y, x0.y, pa);
-          pa = fmaf(fa[1].x, x0.z, pa);
-          pa = fmaf(fa[1].y, x0.w, pa);
-          pa = fmaf(fa[2].x, x1.x, pa);
-          pa = fmaf(fa[2].y, x1.y, pa);
-          pa = fmaf(fa[3].x, x1.z, pa);
-          pa = fmaf(fa[3].y, x1.w, pa);
-          float pb = fb[0].x * x0.x;
-          pb = fmaf(fb[0].y, x0.y, pb);
-          pb = fmaf(fb[1].x, x0.z, pb);
-          pb = fmaf(fb[1].y, x0.w, pb);
-          pb = fmaf(fb[2].x, x1.x, pb);
-          pb = fmaf(fb[2].y, x1.y, pb);
-          pb = fmaf(fb[3].x, x1.z, pb);
-          pb = fmaf(fb[3].y, x1.w, pb);
-          aa[m] = fmaf(pa, sca, aa[m]);
-          ab[m] = fmaf(pb, scb, ab[m]);
-        }
+      for (int m = 0; m < M; ++m) {
+        const float4 x0 = *reinterpret_cast<const float4*>(xs + m * K + c * 8);
+        const float4 x1 = *reinterpret_cast<const float4*>(xs + m * K + c * 8 + 4);
+        float p = f[0].x * x0.x;
+        p = fmaf(f[0].y, x0.y, p);
+        p = fmaf(f[1].x, x0.z, p);
+        p = fmaf(f[1].y, x0.w, p);
+        p = fmaf(f[2].x, x1.x, p);
+        p = fmaf(f[2].y, x1.y, p);
+        p = fmaf(f[3].x, x1.z, p);
+        p = fmaf(f[3].y, x1.w, p);
+        acc[m] = fmaf(p, sc, acc[m]);
       }
     }
   }
@@ -238,6 +230,29 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
   float* xs = smem;  // [M][K]
   __shared__ float rs[kMkMaxRows];
   __shared__ unsigned long long s_best[kMkMaxRows];
+  const int64_t tb = tile_bytes(K);
+  const int step = g.epi == EPI_ACT_ ? ncta : 2 * ncta;
+  auto rows_of = [&](int u, int& ra, int& rb, bool& hb) {
+    if (g.epi == EPI_ACT_) {
+      ra = u * kTileRows + warp;
+      rb = g.W.rows / 2 + u * kTileRows + warp;
+      hb = true;
+    } else {
+      const int ub = u + ncta;
+      ra = u * kTileRows + warp;
+      hb = ub < units;
+      rb = ub * kTileRows + warp;
+    }
+  };
+  // the first unit's weights do not depend on the input: load them before staging it
+  RowW A0, B0;
+  {
+    int ra, rb;
+    bool hb;
+    rows_of(cta, ra, rb, hb);
+    load_row(g.W, tb, K, ra, true, A0);
+    load_row(g.W, tb, K, rb, hb, B0);
+  }
 
   if (g.pre == PRE_EMBED_) {
     const CbMatrix& E = a.m.lm_head;
@@ -264,6 +279,7 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
       xs[mr * K + 2 * j + 1] = v1;
     }
   } else {
+#pragma unroll 4
     for (int i = tid; i < M * K; i += kT) {
       const int mr = i / K, k = i - mr * K;
       float v = 0.0f;
@@ -296,26 +312,22 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
     __syncthreads();
   }
 
-  const int64_t tb = tile_bytes(K);
   unsigned long long best[M];
 #pragma unroll
   for (int mr = 0; mr < M; ++mr) best[mr] = 0ull;
-  const int step = g.epi == EPI_ACT_ ? ncta : 2 * ncta;
   for (int u = cta; u < units; u += step) {
     int ra, rb;
     bool hb;
-    if (g.epi == EPI_ACT_) {
-      ra = u * kTileRows + warp;
-      rb = g.W.rows / 2 + u * kTileRows + warp;
-      hb = true;
-    } else {
-      const int ub = u + ncta;
-      ra = u * kTileRows + warp;
-      hb = ub < units;
-      rb = ub * kTileRows + warp;
+    rows_of(u, ra, rb, hb);
+    if (u != cta) {  // the first unit's rows were loaded before the input staging
+      load_row(g.W, tb, K, ra, true, A0);
+      load_row(g.W, tb, K, rb, hb, B0);
     }
     float aa[M], ab[M];
-    dot_rows<M>(g.W, tb, K, ra, rb, hb, xs, aa, ab);
+#pragma unroll
+    for (int mr = 0; mr < M; ++mr) aa[mr] = ab[mr] = 0.0f;
+    dot_row<M>(A0, K, xs, aa);
+    if (hb) dot_row<M>(B0, K, xs, ab);
     const float tsa = g.W.tile_scale[ra >> 4];
     const float tsb = hb ? g.W.tile_scale[rb >> 4] : 0.0f;
 #pragma unroll
@@ -411,17 +423,30 @@ __device__ void gdn_item(const MkArgs& a, const CbSelfLayer& L, int h, int b, fl
     if (c < Dk) { ch = h * Dk + c; dst = qs; dstride = Dk; di = c; }
     else if (c < 2 * Dk) { ch = H * Dk + h * Dk + (c - Dk); dst = ks; dstride = Dk; di = c - Dk; }
     else { ch = 2 * H * Dk + h * Dv + (c - 2 * Dk); dst = vs; dstride = Dv; di = c - 2 * Dk; }
-    float w[8], win[8];
-    for (int j = 0; j < KC; ++j) w[j] = L.conv_w[(int64_t)ch * KC + j];
-    for (int j = 0; j < KC - 1; ++j) win[j] = conv[(int64_t)j * C + ch];
-    for (int t = 0; t < T; ++t) {
-      win[KC - 1] = __ldcg(proj + (int64_t)t * a.ldp + ch);
-      float y = 0.0f;
-      for (int j = 0; j < KC; ++j) y += win[j] * w[j];
-      dst[t * dstride + di] = silu(y);
-      for (int j = 0; j < KC - 1; ++j) win[j] = win[j + 1];
+    // causal conv with 4 taps (the persistent path requires conv_size == 4): y_t = sum_j w[j] * xx[t + j]
+    float w0 = L.conv_w[(int64_t)ch * 4 + 0], w1 = L.conv_w[(int64_t)ch * 4 + 1];
+    float w2 = L.conv_w[(int64_t)ch * 4 + 2], w3 = L.conv_w[(int64_t)ch * 4 + 3];
+    float c0 = conv[ch], c1 = conv[(int64_t)C + ch], c2 = conv[(int64_t)2 * C + ch];
+    float xin[kMkMaxRows];
+#pragma unroll
+    for (int t = 0; t < kMkMaxRows; ++t) xin[t] = t < T ? __ldcg(proj + (int64_t)t * a.ldp + ch) : 0.0f;
+#pragma unroll
+    for (int t = 0; t < kMkMaxRows; ++t) {
+      if (t < T) {
+        const float x = xin[t];
+        float y = c0 * w0;
+        y += c1 * w1;
+        y += c2 * w2;
+        y += x * w3;
+        dst[t * dstride + di] = silu(y);
+        c0 = c1;
+        c1 = c2;
+        c2 = x;
+      }
     }
-    for (int j = 0; j < KC - 1; ++j) conv[(int64_t)j * C + ch] = win[j];
+    conv[ch] = c0;
+    conv[(int64_t)C + ch] = c1;
+    conv[(int64_t)2 * C + ch] = c2;
   }
   if (tid < T) {
     const float av = __ldcg(proj + (int64_t)tid * a.ldp + m.gdn_off_a + h);
@@ -563,6 +588,7 @@ __device__ void attend_chunk(const float* Qs, const float* Ks, const float* Vs, 
     const int q = i / hd, d = i - q * hd;
     float o = oacc[i] * corr[q];
     const float* e = Sc + q * ldsc;
+#pragma unroll 8
     for (int key = 0; key < n; ++key) o = fmaf(e[key], Vs[key * hd + d], o);
     oacc[i] = o;
   }
@@ -627,12 +653,22 @@ __device__ void swa_item(const MkArgs& a, const CbSelfLayer& L, int b, int g, in
       Vs[idx * hd + d] = bf16_to_f32(bits);
     }
   }
-  for (int i = tid; i < n * hd; i += kT) {
-    const int key = i / hd, d = i - key * hd, kp = ks + key;
+  const int vpk = hd / 8;  // 16-byte vectors per key row
+#pragma unroll 4
+  for (int i = tid; i < n * vpk; i += kT) {
+    const int key = i / vpk, e8 = (i - key * vpk) * 8, kp = ks + key;
     if (kp < p0) {
-      const int64_t off = ((int64_t)(kp % c.swa_slots) * Hkv + g) * hd + d;
-      Ks[key * (hd + 1) + d] = bf16_to_f32(kr[off]);
-      Vs[key * hd + d] = bf16_to_f32(vr[off]);
+      const int64_t off = ((int64_t)(kp % c.swa_slots) * Hkv + g) * hd + e8;
+      const uint4 kq = __ldg(reinterpret_cast<const uint4*>(kr + off));
+      const uint4 vq = __ldg(reinterpret_cast<const uint4*>(vr + off));
+      const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w}, vw[4] = {vq.x, vq.y, vq.z, vq.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        Ks[key * (hd + 1) + e8 + 2 * e] = bf16_to_f32(kw[e]);
+        Ks[key * (hd + 1) + e8 + 2 * e + 1] = bf16_to_f32(kw[e] >> 16);
+        Vs[key * hd + e8 + 2 * e] = bf16_to_f32(vw[e]);
+        Vs[key * hd + e8 + 2 * e + 1] = bf16_to_f32(vw[e] >> 16);
+      }
     }
   }
   for (int i = tid; i < n; i += kT) kpos[i] = ks + i;
@@ -716,11 +752,21 @@ __device__ void cross_item(const MkArgs& a, const CbCrossLayer& L, int r, int g,
     __syncthreads();
     for (int i = tid; i < cn; i += kT) kid[i] = dense ? c0 + i : __ldcg(a.sel_idx + (int64_t)r * a.sel_ld + c0 + i);
     __syncthreads();
-    for (int i = tid; i < cn * hd; i += kT) {
-      const int key = i / hd, d = i - key * hd;
-      const int64_t off = ((int64_t)kid[key] * Hkv + g) * hd + d;
-      Ks[key * (hd + 1) + d] = bf16_to_f32(__ldcg(kb + off));
-      Vs[key * hd + d] = bf16_to_f32(__ldcg(vb + off));
+    const int vpk = hd / 8;
+#pragma unroll 4
+    for (int i = tid; i < cn * vpk; i += kT) {
+      const int key = i / vpk, e8 = (i - key * vpk) * 8;
+      const int64_t off = ((int64_t)kid[key] * Hkv + g) * hd + e8;
+      const uint4 kq = __ldcg(reinterpret_cast<const uint4*>(kb + off));
+      const uint4 vq = __ldcg(reinterpret_cast<const uint4*>(vb + off));
+      const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w}, vw[4] = {vq.x, vq.y, vq.z, vq.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        Ks[key * (hd + 1) + e8 + 2 * e] = bf16_to_f32(kw[e]);
+        Ks[key * (hd + 1) + e8 + 2 * e + 1] = bf16_to_f32(kw[e] >> 16);
+        Vs[key * hd + e8 + 2 * e] = bf16_to_f32(vw[e]);
+        Vs[key * hd + e8 + 2 * e + 1] = bf16_to_f32(vw[e] >> 16);
+      }
     }
     __syncthreads();
     attend_chunk(Qs, Ks, Vs, Sc, Lc, G, cn, hd, rsqrtf((float)hd), qm, ql, corr, oacc, nullptr, nullptr, 0);
@@ -959,8 +1005,11 @@ __device__ void compact_phase(const MkArgs& a, int cta, int ncta, float* smem) {
   }
 }
 
-// Exact selection of one query row: the top `need` candidates by (key, index),
-// the keys above the threshold bin, and the diagonal; sorted ascending.
+// Exact selection of one query row: the keys above the threshold bin, the top
+// `need` threshold-bin candidates by (key, index) -- all of them share the top
+// 11 bits, so a 7-pass radix select over the low 53 bits -- and the diagonal.
+// The selection is marked in a bitmap over the row's keys and written out in
+// ascending order by a block-wide scan of the bitmap.
 __device__ void resolve_row(const MkArgs& a, int r, float* smem) {
   const CbModel& m = a.m;
   const CbCache& c = a.c;
@@ -974,31 +1023,42 @@ __device__ void resolve_row(const MkArgs& a, int r, float* smem) {
     return;
   }
   __shared__ unsigned hist256[256];
-  __shared__ int s_digit, s_rem, s_cnt, s_diag;
-  int nsort = 1;
-  while (nsort < k + 1) nsort <<= 1;
-  int* lst = reinterpret_cast<int*>(smem);                                        // [nsort]
-  unsigned long long* cs = reinterpret_cast<unsigned long long*>(smem) + kMaxSort / 2;  // candidates
-  const int cap = (kSmem - kMaxSort * (int)sizeof(int)) / (int)sizeof(unsigned long long);
+  __shared__ unsigned wsum[32], s_total;
+  __shared__ int s_digit, s_rem;
+  unsigned* bits = reinterpret_cast<unsigned*>(smem);  // [kMkBitmapWords]
+  unsigned long long* cs = reinterpret_cast<unsigned long long*>(smem) + kMkBitmapWords / 2;
+  const int cap = (kSmem - kMkBitmapWords * (int)sizeof(unsigned)) / (int)sizeof(unsigned long long);
+  const int nw = (n + 31) / 32;
   const int above = min(max(__ldcg(a.hi_cnt + r), 0), k - 1);
   const int nc = min(max(__ldcg(a.cand_cnt + r), 0), c.max_ctx);
   const int need = k - above;
   const unsigned long long* cg = a.cand + (int64_t)r * c.max_ctx;
   const unsigned long long* cand = cg;
+  for (int i = tid; i < nw; i += kT) bits[i] = 0u;
   if (nc <= cap) {
+#pragma unroll 4
     for (int i = tid; i < nc; i += kT) cs[i] = __ldcg(cg + i);
     cand = cs;
   }
-  for (int i = tid; i < above; i += kT) lst[i] = __ldcg(a.hi_list + (int64_t)r * k + i);
   __syncthreads();
+#pragma unroll 2
+  for (int i = tid; i < above; i += kT) {
+    const int j = __ldcg(a.hi_list + (int64_t)r * k + i);
+    if (j >= 0 && j < n) atomicOr(&bits[j >> 5], 1u << (j & 31));
+  }
   unsigned long long prefix = 0ull, pmask = 0ull;
   int remaining = need;
-  for (int shift = 56; shift >= 0; shift -= 8) {
+  const int shifts[7] = {45, 37, 29, 21, 13, 5, 0};
+  const unsigned widths[7] = {0xFF, 0xFF, 0xFF, 0xFF, 0xFF, 0xFF, 0x1F};
+#pragma unroll 1
+  for (int ps = 0; ps < 7; ++ps) {
+    const int shift = shifts[ps];
+    const unsigned dm = widths[ps];
     for (int i = tid; i < 256; i += kT) hist256[i] = 0u;
     __syncthreads();
     for (int i = tid; i < nc; i += kT) {
       const unsigned long long v = cand[i];
-      if ((v & pmask) == prefix) atomicAdd(&hist256[(v >> shift) & 0xFF], 1u);
+      if ((v & pmask) == prefix) atomicAdd(&hist256[(v >> shift) & dm], 1u);
     }
     __syncthreads();
     if (warp == 0) {
@@ -1029,50 +1089,37 @@ __device__ void resolve_row(const MkArgs& a, int r, float* smem) {
     }
     __syncthreads();
     prefix |= (unsigned long long)s_digit << shift;
-    pmask |= 0xFFull << shift;
+    pmask |= (unsigned long long)dm << shift;
     remaining = s_rem;
     __syncthreads();
   }
-  const unsigned long long thr = prefix;  // the need-th largest candidate
-  if (tid == 0) {
-    s_cnt = 0;
-    s_diag = 0;
-  }
-  __syncthreads();
+  // candidates at or above the need-th largest (low 53 bits; the top 11 are equal)
+  const unsigned long long thr = prefix;
+  const unsigned long long low = (1ull << 53) - 1;
   for (int i = tid; i < nc; i += kT) {
     const unsigned long long v = cand[i];
-    if (v >= thr) {
-      const int slot = above + atomicAdd(&s_cnt, 1);
-      if (slot < k) lst[slot] = (int)(v & 0xFFFFFFFFull);
+    if ((v & low) >= thr) {
+      const int j = (int)(v & 0xFFFFFFFFull);
+      if (j >= 0 && j < n) atomicOr(&bits[j >> 5], 1u << (j & 31));
     }
   }
+  if (tid == 0) atomicOr(&bits[p >> 5], 1u << (p & 31));  // the diagonal
   __syncthreads();
-  for (int i = tid; i < k; i += kT)
-    if (lst[i] == p) s_diag = 1;
-  __syncthreads();
-  int cnt = k;
-  if (!s_diag) {
-    if (tid == 0) lst[k] = p;
-    cnt = k + 1;
-  }
-  for (int i = cnt + tid; i < nsort; i += kT) lst[i] = 0x7fffffff;
-  __syncthreads();
-  for (int size = 2; size <= nsort; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = tid; i < nsort / 2; i += kT) {
-        const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
-        const bool up = (lo & size) == 0;
-        const int x = lst[lo], y = lst[hi];
-        if ((x > y) == up) {
-          lst[lo] = y;
-          lst[hi] = x;
-        }
-      }
-      __syncthreads();
+  // ascending output: thread tid owns words [tid * wpt, (tid + 1) * wpt)
+  const int wpt = (nw + kT - 1) / kT;
+  unsigned cnt = 0;
+  for (int wi = tid * wpt; wi < min(nw, (tid + 1) * wpt); ++wi) cnt += __popc(bits[wi]);
+  unsigned pos = block_excl_scan(cnt, wsum, &s_total);
+  for (int wi = tid * wpt; wi < min(nw, (tid + 1) * wpt); ++wi) {
+    unsigned wv = bits[wi];
+    while (wv) {
+      const int bpos = __ffs(wv) - 1;
+      wv &= wv - 1;
+      if (pos < (unsigned)a.sel_ld) out[pos] = wi * 32 + bpos;
+      ++pos;
     }
   }
-  for (int i = tid; i < cnt; i += kT) out[i] = lst[i];
-  if (tid == 0) a.sel_cnt[r] = cnt;
+  if (tid == 0) a.sel_cnt[r] = (int)min(s_total, (unsigned)a.sel_ld);
   __syncthreads();
 }
 
@@ -1096,10 +1143,8 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     }
     for (int i = tid; i < kMkArrive; i += kT) a.arrive[i] = 0u;
   }
-  if (tid == 0) {
-    if (cta == 0) a.trace[0] = gtimer();
-    prefetch_all(a);
-  }
+  if (cta == 0 && tid == 0) a.trace[0] = gtimer();
+  prefetch_all(a);
   if (!grid_sync(a, gen, &s_ok)) return;
 
   for (int i = 0; i < m.n_self_layers; ++i) {
@@ -1273,8 +1318,9 @@ bool mk_supported(const CbModel& m, const CbCache& c, int T, int nq) {
   if (m.head_dim > 128 || m.head_dim % 8 || G * T > kMkMaxQ) return false;
   if (m.gdn_dv > kMkThreads || kMkThreads % m.gdn_dv || m.gdn_dk * m.gdn_dv / kMkThreads > 32) return false;
   if ((m.gdn_dk * m.gdn_dv) % kMkThreads && m.gdn_dk * m.gdn_dv > kMkThreads) return false;
-  if (m.conv_size > 8 || m.conv_size < 1) return false;
+  if (m.conv_size != 4) return false;
   if (m.d_model > 2048 || m.ffn_hidden > 2048 || m.d_model % 16 || m.ffn_hidden % 16) return false;
+  if (m.sparse_topk > 0 && c.max_ctx > kMkBitmapWords * 32) return false;
   if (m.sparse_topk > 0 && (m.sparse_topk + 1 > kMaxSort || m.indexer_dim % 8 || m.indexer_dim > 256 ||
                             m.indexer_heads > 16 || (m.indexer_heads * m.indexer_dim + 16 + kMkHistBins) * 4 +
                             CB_MAX_T * m.indexer_dim > kSmem))
