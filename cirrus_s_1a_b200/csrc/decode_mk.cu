@@ -108,10 +108,13 @@ __device__ void prefetch_share(const void* p, size_t bytes) {
 
 __device__ __forceinline__ size_t matrix_bytes(const CbMatrix& W) { return (size_t)(W.rows / kTileRows) * tile_bytes(W.k); }
 
-// Every thread of every CTA: prefetch, in phase order, the weights and the
-// state the step reads; region r is issued by thread r % kT of each CTA, which
-// takes its 1/gridDim share of the region.
-__device__ void prefetch_all(const MkArgs& a) {
+// Paced L2 prefetch.  The step is a sequence of prefetch units: the self
+// layers (weights + that layer's recurrent / window state), the shared-KV
+// unit (projection + indexer keys), the cross layers and the LM head.  Unit u
+// is prefetched when unit u - 2 starts, so about two layers are in flight and
+// the prefetched lines are not evicted before use.  Region r of a unit is
+// issued by thread r % kT of every CTA, each taking its 1/gridDim share.
+__device__ void prefetch_unit(const MkArgs& a, int u) {
   const CbModel& m = a.m;
   const CbCache& c = a.c;
   const int H = m.gdn_heads, C = 2 * H * m.gdn_dk + H * m.gdn_dv;
@@ -119,8 +122,9 @@ __device__ void prefetch_all(const MkArgs& a) {
   auto take = [&](const void* p, size_t bytes) {
     if (r++ % kT == (int)threadIdx.x) prefetch_share(p, bytes);
   };
-  for (int i = 0; i < m.n_self_layers; ++i) {
-    const CbSelfLayer& L = m.self_layers[i];
+  if (u < 0) return;
+  if (u < m.n_self_layers) {
+    const CbSelfLayer& L = m.self_layers[u];
     take(L.in_proj.tiles, matrix_bytes(L.in_proj));
     for (int b = 0; b < a.B; ++b) {
       if (L.kind == CB_LAYER_GDN) {
@@ -137,22 +141,31 @@ __device__ void prefetch_all(const MkArgs& a) {
     take(L.o_proj.tiles, matrix_bytes(L.o_proj));
     take(L.gate_up.tiles, matrix_bytes(L.gate_up));
     take(L.down.tiles, matrix_bytes(L.down));
+    return;
   }
-  take(m.shared_proj.tiles, matrix_bytes(m.shared_proj));
-  if (m.sparse_topk > 0)
-    for (int b = 0; b < a.B; ++b) {
-      const int p0 = min(max(c.pos[b] + a.c0, 0), c.max_ctx);
-      take(c.kv_ik + (int64_t)b * c.max_ctx * m.indexer_dim, (size_t)p0 * m.indexer_dim);
-    }
-  for (int j = 0; j < m.n_cross_layers; ++j) {
-    const CbCrossLayer& L = m.cross_layers[j];
+  u -= m.n_self_layers;
+  if (u == 0) {
+    take(m.shared_proj.tiles, matrix_bytes(m.shared_proj));
+    if (m.sparse_topk > 0)
+      for (int b = 0; b < a.B; ++b) {
+        const int p0 = min(max(c.pos[b] + a.c0, 0), c.max_ctx);
+        take(c.kv_ik + (int64_t)b * c.max_ctx * m.indexer_dim, (size_t)p0 * m.indexer_dim);
+      }
+    return;
+  }
+  u -= 1;
+  if (u < m.n_cross_layers) {
+    const CbCrossLayer& L = m.cross_layers[u];
     take(L.q_gate.tiles, matrix_bytes(L.q_gate));
     take(L.o_proj.tiles, matrix_bytes(L.o_proj));
     take(L.gate_up.tiles, matrix_bytes(L.gate_up));
     take(L.down.tiles, matrix_bytes(L.down));
+    return;
   }
-  take(m.lm_head.tiles, matrix_bytes(m.lm_head));
+  if (u == m.n_cross_layers) take(m.lm_head.tiles, matrix_bytes(m.lm_head));
 }
+
+constexpr int kPrefetchAhead = 2;
 
 // ------------------------------------------------------------------ GEMV
 struct GemvJob {
@@ -1144,11 +1157,12 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     for (int i = tid; i < kMkArrive; i += kT) a.arrive[i] = 0u;
   }
   if (cta == 0 && tid == 0) a.trace[0] = gtimer();
-  prefetch_all(a);
+  for (int u = 0; u < kPrefetchAhead; ++u) prefetch_unit(a, u);
   if (!grid_sync(a, gen, &s_ok)) return;
 
   for (int i = 0; i < m.n_self_layers; ++i) {
     const CbSelfLayer& L = m.self_layers[i];
+    prefetch_unit(a, i + kPrefetchAhead);
     GemvJob in{};
     in.W = L.in_proj;
     in.x = a.h;
@@ -1199,6 +1213,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     if (!grid_sync(a, gen, &s_ok)) return;
   }
 
+  prefetch_unit(a, m.n_self_layers + kPrefetchAhead);
   {
     GemvJob sh{};
     sh.W = m.shared_proj;
@@ -1223,6 +1238,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
 
   for (int j = 0; j < m.n_cross_layers; ++j) {
     const CbCrossLayer& L = m.cross_layers[j];
+    prefetch_unit(a, m.n_self_layers + 1 + j + kPrefetchAhead);
     GemvJob q{};
     q.W = L.q_gate;
     q.x = j == 0 ? a.h : a.xc;
