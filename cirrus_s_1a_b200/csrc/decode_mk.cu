@@ -88,21 +88,20 @@ __device__ bool grid_sync(const MkArgs& a, unsigned& gen, int* s_ok) {
 }
 
 // -------------------------------------------------------------- prefetch
-__device__ __forceinline__ void prefetch_l2(const void* p, unsigned bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+__device__ __forceinline__ void prefetch_line(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
-// This CTA's contiguous share of [p, p + bytes): whole 16-byte units inside the range.
+// [p, p + bytes) in 128-byte lines spread over every thread of the grid.
 __device__ void prefetch_share(const void* p, size_t bytes) {
-  if (p == nullptr || bytes < 16) return;
-  const uintptr_t b0 = reinterpret_cast<uintptr_t>(p);
-  const uintptr_t b = (b0 + 15) & ~(uintptr_t)15, e = (b0 + bytes) & ~(uintptr_t)15;
-  if (e <= b) return;
-  const size_t n16 = (e - b) / 16, per = (n16 + gridDim.x - 1) / gridDim.x;
-  const size_t s = min(n16, per * blockIdx.x), t = min(n16, s + per);
-  for (size_t u = s; u < t; u += 4096) {
-    const size_t cnt = min((size_t)4096, t - u);
-    prefetch_l2(reinterpret_cast<const void*>(b + u * 16), (unsigned)(cnt * 16));
+  if (p == nullptr || bytes == 0) return;
+  const uintptr_t b = reinterpret_cast<uintptr_t>(p) & ~(uintptr_t)127;
+  const uintptr_t e = reinterpret_cast<uintptr_t>(p) + bytes;
+  const size_t lines = (e - b + 127) / 128;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < lines; i += stride) {
+    const uintptr_t addr = b + i * 128;
+    prefetch_line(reinterpret_cast<const void*>(addr < reinterpret_cast<uintptr_t>(p) ? reinterpret_cast<uintptr_t>(p) : addr));
   }
 }
 
@@ -112,16 +111,13 @@ __device__ __forceinline__ size_t matrix_bytes(const CbMatrix& W) { return (size
 // layers (weights + that layer's recurrent / window state), the shared-KV
 // unit (projection + indexer keys), the cross layers and the LM head.  Unit u
 // is prefetched when unit u - 2 starts, so about two layers are in flight and
-// the prefetched lines are not evicted before use.  Region r of a unit is
-// issued by thread r % kT of every CTA, each taking its 1/gridDim share.
+// the prefetched lines are not evicted before use.  Every thread of the grid
+// issues L2 prefetches for its share of each region's 128-byte lines.
 __device__ void prefetch_unit(const MkArgs& a, int u) {
   const CbModel& m = a.m;
   const CbCache& c = a.c;
   const int H = m.gdn_heads, C = 2 * H * m.gdn_dk + H * m.gdn_dv;
-  int r = 0;
-  auto take = [&](const void* p, size_t bytes) {
-    if (r++ % kT == (int)threadIdx.x) prefetch_share(p, bytes);
-  };
+  auto take = [&](const void* p, size_t bytes) { prefetch_share(p, bytes); };
   if (u < 0) return;
   if (u < m.n_self_layers) {
     const CbSelfLayer& L = m.self_layers[u];
