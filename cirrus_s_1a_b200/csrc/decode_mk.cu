@@ -253,16 +253,40 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
       rb = ub * kTileRows + warp;
     }
   };
-  // the first unit's weights do not depend on the input: load them before staging it
+  // the first unit's weights (and, for a residual add, the old outputs) do not
+  // depend on the input: load them before staging it
   RowW A0, B0;
+  float resa[M], resb[M];
+  auto load_res = [&](int ra, int rb, bool hb) {
+#pragma unroll
+    for (int mr = 0; mr < M; ++mr) {
+      resa[mr] = resb[mr] = 0.0f;
+      if (g.epi == EPI_ADD_ && lane == 0 && mr < m_rows) {
+        if (ra < g.rows_out) resa[mr] = __ldcg(g.y + (int64_t)mr * g.ldy + ra);
+        if (hb && rb < g.rows_out) resb[mr] = __ldcg(g.y + (int64_t)mr * g.ldy + rb);
+      }
+    }
+  };
   {
     int ra, rb;
     bool hb;
     rows_of(cta, ra, rb, hb);
     load_row(g.W, tb, K, ra, true, A0);
     load_row(g.W, tb, K, rb, hb, B0);
+    load_res(ra, rb, hb);
   }
 
+  // Stage pre(x) = x * norm_w (RMSNorm's per-row scale is applied to the dot
+  // products at the end); the sum of squares of each row is reduced on the way.
+  __shared__ float rsum[kMkMaxRows];
+  if (tid < kMkMaxRows) rsum[tid] = 0.0f;
+  if (g.argmax && tid < kMkMaxRows) s_best[tid] = 0ull;
+  __syncthreads();
+  const bool norm = g.pre != PRE_NONE_;
+  const bool copy = g.copy_x != nullptr && cta == 0;
+  float sq[M];
+#pragma unroll
+  for (int mr = 0; mr < M; ++mr) sq[mr] = 0.0f;
   if (g.pre == PRE_EMBED_) {
     const CbMatrix& E = a.m.lm_head;
     const int64_t etb = tile_bytes(K);
@@ -284,8 +308,15 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
           set_status(a.status, CB_ERR_TOKEN);
         }
       }
-      xs[mr * K + 2 * j] = v0;
-      xs[mr * K + 2 * j + 1] = v1;
+      if (copy && mr < m_rows) {
+        g.copy_x[mr * K + 2 * j] = v0;
+        g.copy_x[mr * K + 2 * j + 1] = v1;
+      }
+#pragma unroll
+      for (int q = 0; q < M; ++q)
+        if (q == mr) sq[q] += v0 * v0 + v1 * v1;
+      xs[mr * K + 2 * j] = v0 * g.norm_w[2 * j];
+      xs[mr * K + 2 * j + 1] = v1 * g.norm_w[2 * j + 1];
     }
   } else {
 #pragma unroll 4
@@ -295,31 +326,28 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
       if (mr < m_rows) {
         const int xr = g.xmap_nq > 0 ? (mr / g.xmap_nq) * g.xmap_T + g.xmap_off + mr % g.xmap_nq : mr;
         v = __ldcg(g.x + (int64_t)xr * g.ldx + k);
+        if (copy) g.copy_x[mr * K + k] = v;
+      }
+      if (norm) {
+#pragma unroll
+        for (int q = 0; q < M; ++q)
+          if (q == mr) sq[q] += v * v;
+        v *= g.norm_w[k];
       }
       xs[i] = v;
     }
   }
-  if (g.argmax && tid < kMkMaxRows) s_best[tid] = 0ull;
-  __syncthreads();
-  if (g.copy_x != nullptr && cta == 0)
-    for (int i = tid; i < m_rows * K; i += kT) g.copy_x[i] = xs[i];
-  if (g.pre != PRE_NONE_) {
-    if (warp < M) {
-      float ss = 0.0f;
-      for (int k = lane; k < K; k += 32) {
-        const float v = xs[warp * K + k];
-        ss += v * v;
-      }
-      ss = warp_sum(ss);
-      if (lane == 0) rs[warp] = rsqrtf(ss / (float)K + a.m.norm_eps);
+  if (norm) {
+#pragma unroll
+    for (int mr = 0; mr < M; ++mr) {
+      const float t = warp_sum(sq[mr]);
+      if (lane == 0 && t != 0.0f) atomicAdd(&rsum[mr], t);
     }
-    __syncthreads();
-    for (int i = tid; i < M * K; i += kT) {
-      const int mr = i / K, k = i - mr * K;
-      xs[i] = xs[i] * rs[mr] * g.norm_w[k];
-    }
-    __syncthreads();
   }
+  __syncthreads();
+  float rn[M];
+#pragma unroll
+  for (int mr = 0; mr < M; ++mr) rn[mr] = norm ? rsqrtf(rsum[mr] / (float)K + a.m.norm_eps) : 1.0f;
 
   unsigned long long best[M];
 #pragma unroll
@@ -331,6 +359,7 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
     if (u != cta) {  // the first unit's rows were loaded before the input staging
       load_row(g.W, tb, K, ra, true, A0);
       load_row(g.W, tb, K, rb, hb, B0);
+      load_res(ra, rb, hb);
     }
     float aa[M], ab[M];
 #pragma unroll
@@ -341,20 +370,20 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
     const float tsb = hb ? g.W.tile_scale[rb >> 4] : 0.0f;
 #pragma unroll
     for (int mr = 0; mr < M; ++mr) {
-      const float va = warp_sum(aa[mr]) * tsa;
-      const float vb = hb ? warp_sum(ab[mr]) * tsb : 0.0f;
+      const float va = warp_sum(aa[mr]) * tsa * rn[mr];
+      const float vb = hb ? warp_sum(ab[mr]) * tsb * rn[mr] : 0.0f;
       if (lane == 0 && mr < m_rows) {
         float* yr = g.y + (int64_t)mr * g.ldy;
         if (g.epi == EPI_ACT_) {
           if (ra < g.rows_out) yr[ra] = silu(va) * vb;
         } else {
           if (ra < g.rows_out) {
-            if (g.epi == EPI_ADD_) yr[ra] += va;
+            if (g.epi == EPI_ADD_) yr[ra] = resa[mr] + va;
             else yr[ra] = va;
             if (g.argmax) best[mr] = max(best[mr], pack_argmax(va, ra));
           }
           if (hb && rb < g.rows_out) {
-            if (g.epi == EPI_ADD_) yr[rb] += vb;
+            if (g.epi == EPI_ADD_) yr[rb] = resb[mr] + vb;
             else yr[rb] = vb;
             if (g.argmax) best[mr] = max(best[mr], pack_argmax(vb, rb));
           }
@@ -424,6 +453,11 @@ __device__ void gdn_item(const MkArgs& a, const CbSelfLayer& L, int h, int b, fl
   float* conv = a.c.gdn_conv + slot * (KC - 1) * C;
   float* S = a.c.gdn_state + slot * H * Dk * Dv + (int64_t)h * Dk * Dv;
   const float* proj = a.proj + (int64_t)b * T * a.ldp;
+  float s[KPT];  // state rows of this thread, loaded first (they do not depend on the step's input)
+  if (holds) {
+#pragma unroll
+    for (int i = 0; i < KPT; ++i) s[i] = S[(int64_t)(kg * KPT + i) * Dv + v];
+  }
 
   for (int c = tid; c < 2 * Dk + Dv; c += kT) {
     int ch, di;
@@ -471,11 +505,6 @@ __device__ void gdn_item(const MkArgs& a, const CbSelfLayer& L, int h, int b, fl
     ss = warp_sum(ss);
     const float inv = 1.0f / fmaxf(sqrtf(ss), 1e-12f);
     for (int i = lane; i < Dk; i += 32) x[i] *= inv;
-  }
-  float s[KPT];
-  if (holds) {
-#pragma unroll
-    for (int i = 0; i < KPT; ++i) s[i] = S[(int64_t)(kg * KPT + i) * Dv + v];
   }
   __syncthreads();
   const float scale = rsqrtf((float)Dk);
@@ -620,6 +649,49 @@ __device__ bool arrive_last(unsigned* ctr, unsigned count, int* s_flag) {
   return *s_flag != 0;
 }
 
+// Combine the split partials (m, l, o[hd]) of nq queries.  base(q) points at
+// query q's S consecutive partials; out(q, d) receives (sum_s w_s o_s[d]) /
+// (sum_s w_s l_s) * gate(q) with w_s = exp(m_s - max_s m_s).  All partials are
+// loaded into shared memory in one pass.
+template <typename BaseF, typename GateF, typename OutF>
+__device__ void combine_splits(int nq, int S, int hd, float* smem, BaseF base, GateF gate, OutF out) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int per = S * (hd + 2);
+  float* P = smem;  // [nq][S][hd + 2]
+  __shared__ float qL[kMkMaxQ], qg[kMkMaxQ];
+#pragma unroll 4
+  for (int i = tid; i < nq * per; i += kT) {
+    const int q = i / per, e = i - q * per;
+    P[i] = __ldcg(base(q) + e);
+  }
+  for (int q = tid; q < nq; q += kT) qg[q] = gate(q);
+  __syncthreads();
+  for (int q = warp; q < nq; q += kW) {
+    float* Pq = P + q * per;
+    float M = -INFINITY;
+    for (int s2 = lane; s2 < S; s2 += 32) M = fmaxf(M, Pq[s2 * (hd + 2)]);
+    M = warp_max(M);
+    float L = 0.0f;
+    for (int s2 = lane; s2 < S; s2 += 32) {
+      const float ms = Pq[s2 * (hd + 2)];
+      const float w = ms == -INFINITY ? 0.0f : expf(ms - M);
+      L += w * Pq[s2 * (hd + 2) + 1];
+      Pq[s2 * (hd + 2)] = w;
+    }
+    L = warp_sum(L);
+    if (lane == 0) qL[q] = L;
+  }
+  __syncthreads();
+  for (int i = tid; i < nq * hd; i += kT) {
+    const int q = i / hd, d = i - q * hd;
+    const float* Pq = P + q * per;
+    float O = 0.0f;
+    for (int s2 = 0; s2 < S; ++s2) O = fmaf(Pq[s2 * (hd + 2)], Pq[s2 * (hd + 2) + 2 + d], O);
+    out(q, d, (O / qL[q]) * qg[q]);
+  }
+  __syncthreads();
+}
+
 // ------------------------------------------------------------------- SWA
 __device__ void swa_item(const MkArgs& a, const CbSelfLayer& L, int b, int g, int s, float* smem) {
   const CbModel& m = a.m;
@@ -697,23 +769,20 @@ __device__ void swa_item(const MkArgs& a, const CbSelfLayer& L, int b, int g, in
   }
   if (!arrive_last(&a.arrive[b * Hkv + g], (unsigned)S, &s_flag)) return;
   __threadfence();
-  for (int i = tid; i < nqry * hd; i += kT) {
-    const int q = i / hd, d = i - q * hd, t = q / G, j = q - t * G, qh = g * G + j;
-    const float* base = a.part + (((int64_t)b * T + t) * Hq + qh) * S * (hd + 2);
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, __ldcg(base + s2 * (hd + 2)));
-    float Lsum = 0.0f, O = 0.0f;
-    for (int s2 = 0; s2 < S; ++s2) {
-      const float ms = __ldcg(base + s2 * (hd + 2));
-      if (ms == -INFINITY) continue;
-      const float w = expf(ms - M);
-      Lsum += __ldcg(base + s2 * (hd + 2) + 1) * w;
-      O += __ldcg(base + s2 * (hd + 2) + 2 + d) * w;
-    }
-    const float gate = sigmoid(__ldcg(a.proj + ((int64_t)b * T + t) * a.ldp + m.swa_off_gate + qh));
-    a.attn[((int64_t)b * T + t) * a.att_ld + qh * hd + d] = (O / Lsum) * gate;
-  }
-  __syncthreads();
+  combine_splits(
+      nqry, S, hd, smem,
+      [&](int q) {
+        const int t = q / G, j = q - t * G;
+        return a.part + (((int64_t)b * T + t) * Hq + g * G + j) * S * (hd + 2);
+      },
+      [&](int q) {
+        const int t = q / G, j = q - t * G;
+        return sigmoid(__ldcg(a.proj + ((int64_t)b * T + t) * a.ldp + m.swa_off_gate + g * G + j));
+      },
+      [&](int q, int d, float v) {
+        const int t = q / G, j = q - t * G;
+        a.attn[((int64_t)b * T + t) * a.att_ld + (g * G + j) * hd + d] = v;
+      });
 }
 
 __device__ void swa_phase(const MkArgs& a, const CbSelfLayer& L, int cta, int ncta, float* smem) {
@@ -788,23 +857,10 @@ __device__ void cross_item(const MkArgs& a, const CbCrossLayer& L, int r, int g,
   }
   if (!arrive_last(&a.arrive[kMkArrive / 2 + r * Hkv + g], (unsigned)S, &s_flag)) return;
   __threadfence();
-  for (int i = tid; i < G * hd; i += kT) {
-    const int j = i / hd, d = i - j * hd, qh = g * G + j;
-    const float* base = a.part2 + ((int64_t)r * Hq + qh) * S * (hd + 2);
-    float M = -INFINITY;
-    for (int s2 = 0; s2 < S; ++s2) M = fmaxf(M, __ldcg(base + s2 * (hd + 2)));
-    float Lsum = 0.0f, O = 0.0f;
-    for (int s2 = 0; s2 < S; ++s2) {
-      const float ms = __ldcg(base + s2 * (hd + 2));
-      if (ms == -INFINITY) continue;
-      const float w = expf(ms - M);
-      Lsum += __ldcg(base + s2 * (hd + 2) + 1) * w;
-      O += __ldcg(base + s2 * (hd + 2) + 2 + d) * w;
-    }
-    const float gate = sigmoid(__ldcg(row + m.cr_off_gate + qh));
-    a.attn[(int64_t)r * a.att_ld + qh * hd + d] = (O / Lsum) * gate;
-  }
-  __syncthreads();
+  combine_splits(
+      G, S, hd, smem, [&](int j) { return a.part2 + ((int64_t)r * Hq + g * G + j) * S * (hd + 2); },
+      [&](int j) { return sigmoid(__ldcg(row + m.cr_off_gate + g * G + j)); },
+      [&](int j, int d, float v) { a.attn[(int64_t)r * a.att_ld + (g * G + j) * hd + d] = v; });
 }
 
 __device__ void cross_phase(const MkArgs& a, const CbCrossLayer& L, int cta, int ncta, float* smem) {
