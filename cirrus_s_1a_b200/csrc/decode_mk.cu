@@ -278,8 +278,7 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
 
   // Stage pre(x) = x * norm_w (RMSNorm's per-row scale is applied to the dot
   // products at the end); the sum of squares of each row is reduced on the way.
-  __shared__ float rsum[kMkMaxRows];
-  if (tid < kMkMaxRows) rsum[tid] = 0.0f;
+  __shared__ float wsq[kW][kMkMaxRows];  // per-warp partial sums of squares (summed in a fixed order)
   if (g.argmax && tid < kMkMaxRows) s_best[tid] = 0ull;
   __syncthreads();
   const bool norm = g.pre != PRE_NONE_;
@@ -341,13 +340,20 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
 #pragma unroll
     for (int mr = 0; mr < M; ++mr) {
       const float t = warp_sum(sq[mr]);
-      if (lane == 0 && t != 0.0f) atomicAdd(&rsum[mr], t);
+      if (lane == 0) wsq[warp][mr] = t;
     }
   }
   __syncthreads();
   float rn[M];
 #pragma unroll
-  for (int mr = 0; mr < M; ++mr) rn[mr] = norm ? rsqrtf(rsum[mr] / (float)K + a.m.norm_eps) : 1.0f;
+  for (int mr = 0; mr < M; ++mr) {
+    rn[mr] = 1.0f;
+    if (norm) {
+      float t = 0.0f;
+      for (int w = 0; w < kW; ++w) t += wsq[w][mr];
+      rn[mr] = rsqrtf(t / (float)K + a.m.norm_eps);
+    }
+  }
 
   unsigned long long best[M];
 #pragma unroll
