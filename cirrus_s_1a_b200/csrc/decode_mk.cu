@@ -54,7 +54,7 @@ __device__ __forceinline__ unsigned long long gtimer() {
 
 // Grid barrier on a monotonic arrival counter.  Returns false when the launch
 // must stop (this CTA's wait timed out, or another CTA's did).
-__device__ __noinline__ bool grid_sync(const MkArgs& a, unsigned& gen, int* s_ok) {
+__device__ bool grid_sync(const MkArgs& a, unsigned& gen, int* s_ok) {
   __syncthreads();
   if (threadIdx.x == 0) {
     gen += 1;
@@ -113,7 +113,7 @@ __device__ __forceinline__ size_t matrix_bytes(const CbMatrix& W) { return (size
 // is prefetched when unit u - 2 starts, so about two layers are in flight and
 // the prefetched lines are not evicted before use.  Every thread of the grid
 // issues L2 prefetches for its share of each region's 128-byte lines.
-__device__ __noinline__ void prefetch_unit(const MkArgs& a, int u) {
+__device__ void prefetch_unit(const MkArgs& a, int u) {
   const CbModel& m = a.m;
   const CbCache& c = a.c;
   const int H = m.gdn_heads, C = 2 * H * m.gdn_dk + H * m.gdn_dv;
@@ -232,7 +232,7 @@ __device__ __forceinline__ unsigned long long pack_argmax(float v, int idx) {
 }
 
 template <int M>
-__device__ __noinline__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int cta, int ncta, float* smem) {
+__device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int cta, int ncta, float* smem) {
   const int units = g.epi == EPI_ACT_ ? g.W.rows / 32 : g.W.rows / kTileRows;
   if (cta < 0 || cta >= units || ncta <= 0) return;
   const int K = g.W.k, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -411,7 +411,7 @@ __device__ __noinline__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m
 // One warp: RMSNorm(x) * w (over hd) then partial interleaved RoPE at position
 // p; lane owns the pairs j = lane, lane + 32, ...  Results to out (smem).
 // When bf16 is set the values are rounded to bfloat16 and the bits also go to bits_out.
-__device__ __noinline__ void norm_rope_warp(const float* x, const float* w, int hd, int rot2, int p, const float* inv_freq,
+__device__ void norm_rope_warp(const float* x, const float* w, int hd, int rot2, int p, const float* inv_freq,
                                float eps, float* out, bool bf16, uint16_t* bits_out) {
   const int lane = threadIdx.x & 31, npairs = hd / 2;
   float ss = 0.0f;
@@ -441,7 +441,7 @@ __device__ __noinline__ void norm_rope_warp(const float* x, const float* w, int 
 
 // ------------------------------------------------------------------- GDN
 template <int KPT>
-__device__ __noinline__ void gdn_item(const MkArgs& a, const CbSelfLayer& L, int h, int b, float* smem) {
+__device__ void gdn_item(const MkArgs& a, const CbSelfLayer& L, int h, int b, float* smem) {
   const CbModel& m = a.m;
   const int H = m.gdn_heads, Dk = m.gdn_dk, Dv = m.gdn_dv, T = a.T, KC = m.conv_size;
   const int C = 2 * H * Dk + H * Dv;
@@ -566,7 +566,7 @@ __device__ __noinline__ void gdn_item(const MkArgs& a, const CbSelfLayer& L, int
   __syncthreads();
 }
 
-__device__ __noinline__ void gdn_phase(const MkArgs& a, const CbSelfLayer& L, int cta, int ncta, float* smem) {
+__device__ void gdn_phase(const MkArgs& a, const CbSelfLayer& L, int cta, int ncta, float* smem) {
   const int H = a.m.gdn_heads;
   const int kpt = max(1, a.m.gdn_dk * a.m.gdn_dv / kT);
   for (int it = cta; it < H * a.B; it += ncta) {
@@ -585,7 +585,7 @@ __device__ __noinline__ void gdn_phase(const MkArgs& a, const CbSelfLayer& L, in
 // ------------------------------------------- attention helpers (split softmax)
 // Scores of nq queries (Qs [nq][hd]) against n keys (Ks [n][hd+1]) into Sc [nq][ldsc],
 // masked entries -inf; then per query max / exp / sum (qm, ql) and o += e V into oacc.
-__device__ __noinline__ void attend_chunk(const float* Qs, const float* Ks, const float* Vs, float* Sc, int ldsc, int nq, int n,
+__device__ void attend_chunk(const float* Qs, const float* Ks, const float* Vs, float* Sc, int ldsc, int nq, int n,
                              int hd, float scale, float* qm, float* ql, float* corr, float* oacc,
                              const int* key_pos, const int* q_pos, int window) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -699,7 +699,7 @@ __device__ void combine_splits(int nq, int S, int hd, float* smem, BaseF base, G
 }
 
 // ------------------------------------------------------------------- SWA
-__device__ __noinline__ void swa_item(const MkArgs& a, const CbSelfLayer& L, int b, int g, int s, float* smem) {
+__device__ void swa_item(const MkArgs& a, const CbSelfLayer& L, int b, int g, int s, float* smem) {
   const CbModel& m = a.m;
   const CbCache& c = a.c;
   const int hd = m.head_dim, Hq = m.n_q_heads, Hkv = m.n_kv_heads, G = Hq / Hkv, T = a.T;
@@ -791,7 +791,7 @@ __device__ __noinline__ void swa_item(const MkArgs& a, const CbSelfLayer& L, int
       });
 }
 
-__device__ __noinline__ void swa_phase(const MkArgs& a, const CbSelfLayer& L, int cta, int ncta, float* smem) {
+__device__ void swa_phase(const MkArgs& a, const CbSelfLayer& L, int cta, int ncta, float* smem) {
   const int Hkv = a.m.n_kv_heads, S = a.swa_splits;
   for (int it = cta; it < a.B * Hkv * S; it += ncta) {
     const int s = it % S, g = (it / S) % Hkv, b = it / (S * Hkv);
@@ -800,7 +800,7 @@ __device__ __noinline__ void swa_phase(const MkArgs& a, const CbSelfLayer& L, in
 }
 
 // -------------------------------------------------------- cross attention
-__device__ __noinline__ void cross_item(const MkArgs& a, const CbCrossLayer& L, int r, int g, int s, float* smem) {
+__device__ void cross_item(const MkArgs& a, const CbCrossLayer& L, int r, int g, int s, float* smem) {
   const CbModel& m = a.m;
   const CbCache& c = a.c;
   const int hd = m.head_dim, Hq = m.n_q_heads, Hkv = m.n_kv_heads, G = Hq / Hkv, S = a.cross_splits;
@@ -869,7 +869,7 @@ __device__ __noinline__ void cross_item(const MkArgs& a, const CbCrossLayer& L, 
       [&](int j, int d, float v) { a.attn[(int64_t)r * a.att_ld + (g * G + j) * hd + d] = v; });
 }
 
-__device__ __noinline__ void cross_phase(const MkArgs& a, const CbCrossLayer& L, int cta, int ncta, float* smem) {
+__device__ void cross_phase(const MkArgs& a, const CbCrossLayer& L, int cta, int ncta, float* smem) {
   const int Hkv = a.m.n_kv_heads, S = a.cross_splits, RQ = a.B * a.nq;
   for (int it = cta; it < RQ * Hkv * S; it += ncta) {
     const int s = it % S, g = (it / S) % Hkv, r = it / (S * Hkv);
@@ -886,7 +886,7 @@ __device__ __forceinline__ void query_row(const MkArgs& a, int r, int& b, int& t
 }
 
 // New rows of the shared cache: k = RoPE(RMSNorm(k)), v, indexer key (E4M3).
-__device__ __noinline__ void shared_append(const MkArgs& a, int cta, int ncta, float* smem) {
+__device__ void shared_append(const MkArgs& a, int cta, int ncta, float* smem) {
   const CbModel& m = a.m;
   const CbCache& c = a.c;
   const int Mrows = a.B * a.T, hd = m.head_dim, Hkv = m.n_kv_heads;
@@ -948,7 +948,7 @@ __device__ __forceinline__ void key_range(int n, int cta, int ncta, int& js, int
 }
 
 // Scores of this CTA's key range for every query row + histogram of the top 11 key bits.
-__device__ __noinline__ void score_phase(const MkArgs& a, int cta, int ncta, float* smem) {
+__device__ void score_phase(const MkArgs& a, int cta, int ncta, float* smem) {
   const CbModel& m = a.m;
   const CbCache& c = a.c;
   const int RQ = a.B * a.nq, Hi = m.indexer_heads, Di = m.indexer_dim, k = m.sparse_topk;
@@ -1017,7 +1017,7 @@ __device__ unsigned block_excl_scan(unsigned v, unsigned* wsum, unsigned* total)
 }
 
 // Threshold bin of the k-th largest key, then this CTA's keys above it to hi_list and in it to cand.
-__device__ __noinline__ void compact_phase(const MkArgs& a, int cta, int ncta, float* smem) {
+__device__ void compact_phase(const MkArgs& a, int cta, int ncta, float* smem) {
   const CbModel& m = a.m;
   const CbCache& c = a.c;
   const int RQ = a.B * a.nq, k = m.sparse_topk;
@@ -1081,7 +1081,7 @@ __device__ __noinline__ void compact_phase(const MkArgs& a, int cta, int ncta, f
 // 11 bits, so a 7-pass radix select over the low 53 bits -- and the diagonal.
 // The selection is marked in a bitmap over the row's keys and written out in
 // ascending order by a block-wide scan of the bitmap.
-__device__ __noinline__ void resolve_row(const MkArgs& a, int r, float* smem) {
+__device__ void resolve_row(const MkArgs& a, int r, float* smem) {
   const CbModel& m = a.m;
   const CbCache& c = a.c;
   const int k = m.sparse_topk, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
