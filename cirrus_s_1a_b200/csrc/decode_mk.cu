@@ -34,6 +34,8 @@ constexpr int kSmem = 160 * 1024;
 constexpr int kMaxSort = 4096;
 constexpr int kMkBitmapWords = 4096;  // selection bitmap: up to 131072 keys
 
+enum { PRE_NONE_ = 0, PRE_RMS_ = 1, PRE_EMBED_ = 2 };
+enum { EPI_STORE_ = 0, EPI_ADD_ = 1, EPI_ACT_ = 2 };
 
 // ------------------------------------------------------------------ sync
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
@@ -162,6 +164,19 @@ __device__ void prefetch_unit(const MkArgs& a, int u) {
 constexpr int kPrefetchAhead = 2;
 
 // ------------------------------------------------------------------ GEMV
+struct GemvJob {
+  CbMatrix W;
+  const float* x;
+  int ldx;
+  int xmap_nq, xmap_T, xmap_off;  // x row of m = (m / nq) * T + off + m % nq when xmap_nq > 0
+  int pre;
+  const float* norm_w;
+  float* y;
+  int ldy, rows_out, epi;
+  float* copy_x;                  // local CTA 0 stores the raw input rows here ([m][K])
+  bool argmax;
+};
+
 // One weight row as seen by one lane: the 8-code chunks lane, lane+32, ...
 // (K <= 2048, so at most 8 chunks), code words and scale bytes.
 struct RowW {
@@ -218,16 +233,16 @@ __device__ __forceinline__ unsigned long long pack_argmax(float v, int idx) {
 
 template <int M>
 __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int cta, int ncta, float* smem) {
-  const int units = g.epi == MK_EPI_ACT ? g.W.rows / 32 : g.W.rows / kTileRows;
+  const int units = g.epi == EPI_ACT_ ? g.W.rows / 32 : g.W.rows / kTileRows;
   if (cta < 0 || cta >= units || ncta <= 0) return;
   const int K = g.W.k, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float* xs = smem;  // [M][K]
   __shared__ float rs[kMkMaxRows];
   __shared__ unsigned long long s_best[kMkMaxRows];
   const int64_t tb = tile_bytes(K);
-  const int step = g.epi == MK_EPI_ACT ? ncta : 2 * ncta;
+  const int step = g.epi == EPI_ACT_ ? ncta : 2 * ncta;
   auto rows_of = [&](int u, int& ra, int& rb, bool& hb) {
-    if (g.epi == MK_EPI_ACT) {
+    if (g.epi == EPI_ACT_) {
       ra = u * kTileRows + warp;
       rb = g.W.rows / 2 + u * kTileRows + warp;
       hb = true;
@@ -246,7 +261,7 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
 #pragma unroll
     for (int mr = 0; mr < M; ++mr) {
       resa[mr] = resb[mr] = 0.0f;
-      if (g.epi == MK_EPI_ADD && lane == 0 && mr < m_rows) {
+      if (g.epi == EPI_ADD_ && lane == 0 && mr < m_rows) {
         if (ra < g.rows_out) resa[mr] = __ldcg(g.y + (int64_t)mr * g.ldy + ra);
         if (hb && rb < g.rows_out) resb[mr] = __ldcg(g.y + (int64_t)mr * g.ldy + rb);
       }
@@ -266,12 +281,12 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
   __shared__ float wsq[kW][kMkMaxRows];  // per-warp partial sums of squares (summed in a fixed order)
   if (g.argmax && tid < kMkMaxRows) s_best[tid] = 0ull;
   __syncthreads();
-  const bool norm = g.pre != MK_PRE_NONE;
+  const bool norm = g.pre != PRE_NONE_;
   const bool copy = g.copy_x != nullptr && cta == 0;
   float sq[M];
 #pragma unroll
   for (int mr = 0; mr < M; ++mr) sq[mr] = 0.0f;
-  if (g.pre == MK_PRE_EMBED) {
+  if (g.pre == PRE_EMBED_) {
     const CbMatrix& E = a.m.lm_head;
     const int64_t etb = tile_bytes(K);
     for (int i = tid; i < M * (K / 2); i += kT) {
@@ -365,16 +380,16 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
       const float vb = hb ? warp_sum(ab[mr]) * tsb * rn[mr] : 0.0f;
       if (lane == 0 && mr < m_rows) {
         float* yr = g.y + (int64_t)mr * g.ldy;
-        if (g.epi == MK_EPI_ACT) {
+        if (g.epi == EPI_ACT_) {
           if (ra < g.rows_out) yr[ra] = silu(va) * vb;
         } else {
           if (ra < g.rows_out) {
-            if (g.epi == MK_EPI_ADD) yr[ra] = resa[mr] + va;
+            if (g.epi == EPI_ADD_) yr[ra] = resa[mr] + va;
             else yr[ra] = va;
             if (g.argmax) best[mr] = max(best[mr], pack_argmax(va, ra));
           }
           if (hb && rb < g.rows_out) {
-            if (g.epi == MK_EPI_ADD) yr[rb] = resb[mr] + vb;
+            if (g.epi == EPI_ADD_) yr[rb] = resb[mr] + vb;
             else yr[rb] = vb;
             if (g.argmax) best[mr] = max(best[mr], pack_argmax(vb, rb));
           }
@@ -1180,8 +1195,6 @@ __device__ void resolve_row(const MkArgs& a, int r, float* smem) {
 }
 
 // ------------------------------------------------------------------ kernel
-// Interprets the plan: each phase is one case of the switch, so every phase
-// type exists once in the binary and stays resident in the instruction cache.
 template <int M>
 __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_constant__ MkArgs a) {
   extern __shared__ __align__(16) float smem[];
@@ -1189,7 +1202,8 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
   unsigned gen = 0;
   const int cta = blockIdx.x, ncta = gridDim.x, tid = threadIdx.x;
   const CbModel& m = a.m;
-  const int RQ = a.B * a.nq;
+  const int d = m.d_model, Mrows = a.B * a.T, RQ = a.B * a.nq, F = m.ffn_hidden;
+  const bool sparse = m.sparse_topk > 0;
 
   if (cta == 0) {
     for (int i = tid; i < RQ * kMkHistBins; i += kT) a.hist[i] = 0u;
@@ -1199,44 +1213,167 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
       a.amax[i] = 0ull;
     }
     for (int i = tid; i < kMkArrive; i += kT) a.arrive[i] = 0u;
-    if (tid == 0) a.trace[0] = gtimer();
   }
+  if (cta == 0 && tid == 0) a.trace[0] = gtimer();
   for (int u = 0; u < kPrefetchAhead; ++u) prefetch_unit(a, u);
   if (!grid_sync(a, gen, &s_ok)) return;
 
-  for (int p = 0; p < a.n_phases; ++p) {
-    const MkPhase& ph = a.phases[p];
-    if (ph.prefetch_unit >= 0) prefetch_unit(a, ph.prefetch_unit);
-    switch (ph.type) {
-      case MK_PH_GEMV: {
-        const int off = ph.resolve_ctas;
-        if (cta < off) resolve_row(a, cta, smem);
-        else gemv_phase<M>(a, ph.g, ph.m_rows, cta - off, ncta - off, smem);
-        if (ph.copy_hidden && a.hidden != nullptr && cta == ncta - 1)
-          for (int i = tid; i < RQ * m.d_model; i += kT) a.hidden[i] = __ldcg(a.xc + i);
-        break;
-      }
-      case MK_PH_GDN:
-        gdn_phase(a, m.self_layers[ph.layer], cta, ncta, smem);
-        break;
-      case MK_PH_SWA:
-        swa_phase(a, m.self_layers[ph.layer], cta, ncta, smem);
-        break;
-      case MK_PH_SHARED:
-        shared_append(a, cta, ncta, smem);
-        if (m.sparse_topk > 0) score_phase(a, cta, ncta, smem);
-        break;
-      case MK_PH_COMPACT:
-        compact_phase(a, cta, ncta, smem);
-        break;
-      case MK_PH_CROSS:
-        cross_phase(a, m.cross_layers[ph.layer], cta, ncta, smem);
-        break;
-      default:
-        break;
-    }
+  for (int i = 0; i < m.n_self_layers; ++i) {
+    const CbSelfLayer& L = m.self_layers[i];
+    prefetch_unit(a, i + kPrefetchAhead);
+    GemvJob in{};
+    in.W = L.in_proj;
+    in.x = a.h;
+    in.ldx = d;
+    in.pre = i == 0 ? PRE_EMBED_ : PRE_RMS_;
+    in.norm_w = L.norm1;
+    in.y = a.proj;
+    in.ldy = a.ldp;
+    in.rows_out = L.in_proj.rows;
+    in.epi = EPI_STORE_;
+    in.copy_x = i == 0 ? a.h : nullptr;
+    gemv_phase<M>(a, in, Mrows, cta, ncta, smem);
+    if (!grid_sync(a, gen, &s_ok)) return;
+    if (L.kind == CB_LAYER_GDN) gdn_phase(a, L, cta, ncta, smem);
+    else swa_phase(a, L, cta, ncta, smem);
+    if (!grid_sync(a, gen, &s_ok)) return;
+    GemvJob o{};
+    o.W = L.o_proj;
+    o.x = a.attn;
+    o.ldx = a.att_ld;
+    o.y = a.h;
+    o.ldy = d;
+    o.rows_out = d;
+    o.epi = EPI_ADD_;
+    gemv_phase<M>(a, o, Mrows, cta, ncta, smem);
+    if (!grid_sync(a, gen, &s_ok)) return;
+    GemvJob gu{};
+    gu.W = L.gate_up;
+    gu.x = a.h;
+    gu.ldx = d;
+    gu.pre = PRE_RMS_;
+    gu.norm_w = L.norm2;
+    gu.y = a.act;
+    gu.ldy = F;
+    gu.rows_out = F;
+    gu.epi = EPI_ACT_;
+    gemv_phase<M>(a, gu, Mrows, cta, ncta, smem);
+    if (!grid_sync(a, gen, &s_ok)) return;
+    GemvJob dn{};
+    dn.W = L.down;
+    dn.x = a.act;
+    dn.ldx = F;
+    dn.y = a.h;
+    dn.ldy = d;
+    dn.rows_out = d;
+    dn.epi = EPI_ADD_;
+    gemv_phase<M>(a, dn, Mrows, cta, ncta, smem);
     if (!grid_sync(a, gen, &s_ok)) return;
   }
+
+  prefetch_unit(a, m.n_self_layers + kPrefetchAhead);
+  {
+    GemvJob sh{};
+    sh.W = m.shared_proj;
+    sh.x = a.h;
+    sh.ldx = d;
+    sh.pre = PRE_RMS_;
+    sh.norm_w = m.shared_norm;
+    sh.y = a.proj;
+    sh.ldy = a.ldp;
+    sh.rows_out = m.shared_proj.rows;
+    sh.epi = EPI_STORE_;
+    gemv_phase<M>(a, sh, Mrows, cta, ncta, smem);
+  }
+  if (!grid_sync(a, gen, &s_ok)) return;
+  shared_append(a, cta, ncta, smem);
+  if (sparse) score_phase(a, cta, ncta, smem);
+  if (!grid_sync(a, gen, &s_ok)) return;
+  if (sparse) {
+    compact_phase(a, cta, ncta, smem);
+    if (!grid_sync(a, gen, &s_ok)) return;
+  }
+
+  for (int j = 0; j < m.n_cross_layers; ++j) {
+    const CbCrossLayer& L = m.cross_layers[j];
+    prefetch_unit(a, m.n_self_layers + 1 + j + kPrefetchAhead);
+    GemvJob q{};
+    q.W = L.q_gate;
+    q.x = j == 0 ? a.h : a.xc;
+    q.ldx = d;
+    if (j == 0) {
+      q.xmap_nq = a.nq;
+      q.xmap_T = a.T;
+      q.xmap_off = a.T - a.nq;
+      q.copy_x = a.xc;
+    }
+    q.pre = PRE_RMS_;
+    q.norm_w = L.norm1;
+    q.y = a.cproj;
+    q.ldy = a.cr_ld;
+    q.rows_out = L.q_gate.rows;
+    q.epi = EPI_STORE_;
+    if (j == 0 && sparse) {
+      // the exact selection of each query row runs beside the first q projection
+      if (cta < RQ) resolve_row(a, cta, smem);
+      else gemv_phase<M>(a, q, RQ, cta - RQ, ncta - RQ, smem);
+    } else {
+      gemv_phase<M>(a, q, RQ, cta, ncta, smem);
+    }
+    if (!grid_sync(a, gen, &s_ok)) return;
+    cross_phase(a, L, cta, ncta, smem);
+    if (!grid_sync(a, gen, &s_ok)) return;
+    GemvJob o{};
+    o.W = L.o_proj;
+    o.x = a.attn;
+    o.ldx = a.att_ld;
+    o.y = a.xc;
+    o.ldy = d;
+    o.rows_out = d;
+    o.epi = EPI_ADD_;
+    gemv_phase<M>(a, o, RQ, cta, ncta, smem);
+    if (!grid_sync(a, gen, &s_ok)) return;
+    GemvJob gu{};
+    gu.W = L.gate_up;
+    gu.x = a.xc;
+    gu.ldx = d;
+    gu.pre = PRE_RMS_;
+    gu.norm_w = L.norm2;
+    gu.y = a.act;
+    gu.ldy = F;
+    gu.rows_out = F;
+    gu.epi = EPI_ACT_;
+    gemv_phase<M>(a, gu, RQ, cta, ncta, smem);
+    if (!grid_sync(a, gen, &s_ok)) return;
+    GemvJob dn{};
+    dn.W = L.down;
+    dn.x = a.act;
+    dn.ldx = F;
+    dn.y = a.xc;
+    dn.ldy = d;
+    dn.rows_out = d;
+    dn.epi = EPI_ADD_;
+    gemv_phase<M>(a, dn, RQ, cta, ncta, smem);
+    if (!grid_sync(a, gen, &s_ok)) return;
+  }
+
+  {
+    GemvJob hd{};
+    hd.W = m.lm_head;
+    hd.x = a.xc;
+    hd.ldx = d;
+    hd.pre = PRE_RMS_;
+    hd.norm_w = m.final_norm;
+    hd.y = a.logits ? a.logits : a.ws_logits;
+    hd.ldy = m.vocab_size;
+    hd.rows_out = m.vocab_size;
+    hd.epi = EPI_STORE_;
+    hd.argmax = true;
+    gemv_phase<M>(a, hd, RQ, cta, ncta, smem);
+    if (a.hidden != nullptr && cta == ncta - 1)
+      for (int i = tid; i < RQ * d; i += kT) a.hidden[i] = __ldcg(a.xc + i);
+  }
+  if (!grid_sync(a, gen, &s_ok)) return;
   if (cta == 0) {
     if (a.argmax != nullptr)
       for (int r = tid; r < RQ; r += kT)
@@ -1248,80 +1385,6 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
 }  // namespace
 
 size_t mk_smem_bytes() { return kSmem; }
-
-bool mk_build_plan(MkArgs& a) {
-  const CbModel& m = a.m;
-  const int d = m.d_model, F = m.ffn_hidden, Mrows = a.B * a.T, RQ = a.B * a.nq;
-  const bool sparse = m.sparse_topk > 0;
-  int n = 0;
-  auto add = [&](int type, int layer, int prefetch) -> MkPhase* {
-    if (n >= kMkMaxPhases) return nullptr;
-    MkPhase& ph = a.phases[n++];
-    ph = MkPhase{};
-    ph.type = type;
-    ph.layer = layer;
-    ph.prefetch_unit = prefetch;
-    ph.m_rows = Mrows;
-    return &ph;
-  };
-  auto gemv = [&](const CbMatrix& W, const float* x, int ldx, int pre, const float* norm_w, float* y, int ldy,
-                  int rows_out, int epi, int m_rows, int prefetch) -> MkPhase* {
-    MkPhase* ph = add(MK_PH_GEMV, 0, prefetch);
-    if (!ph) return nullptr;
-    ph->m_rows = m_rows;
-    GemvJob& g = ph->g;
-    g.W = W;
-    g.x = x;
-    g.ldx = ldx;
-    g.pre = pre;
-    g.norm_w = norm_w;
-    g.y = y;
-    g.ldy = ldy;
-    g.rows_out = rows_out;
-    g.epi = epi;
-    return ph;
-  };
-  for (int i = 0; i < m.n_self_layers; ++i) {
-    const CbSelfLayer& L = m.self_layers[i];
-    MkPhase* in = gemv(L.in_proj, a.h, d, i == 0 ? MK_PRE_EMBED : MK_PRE_RMS, L.norm1, a.proj, a.ldp, L.in_proj.rows,
-                       MK_EPI_STORE, Mrows, i + kPrefetchAhead);
-    if (!in) return false;
-    if (i == 0) in->g.copy_x = a.h;
-    if (!add(L.kind == CB_LAYER_GDN ? MK_PH_GDN : MK_PH_SWA, i, -1)) return false;
-    if (!gemv(L.o_proj, a.attn, a.att_ld, MK_PRE_NONE, nullptr, a.h, d, d, MK_EPI_ADD, Mrows, -1)) return false;
-    if (!gemv(L.gate_up, a.h, d, MK_PRE_RMS, L.norm2, a.act, F, F, MK_EPI_ACT, Mrows, -1)) return false;
-    if (!gemv(L.down, a.act, F, MK_PRE_NONE, nullptr, a.h, d, d, MK_EPI_ADD, Mrows, -1)) return false;
-  }
-  if (!gemv(m.shared_proj, a.h, d, MK_PRE_RMS, m.shared_norm, a.proj, a.ldp, m.shared_proj.rows, MK_EPI_STORE, Mrows,
-            m.n_self_layers + kPrefetchAhead))
-    return false;
-  if (!add(MK_PH_SHARED, 0, -1)) return false;
-  if (sparse && !add(MK_PH_COMPACT, 0, -1)) return false;
-  for (int j = 0; j < m.n_cross_layers; ++j) {
-    const CbCrossLayer& L = m.cross_layers[j];
-    MkPhase* q = gemv(L.q_gate, j == 0 ? a.h : a.xc, d, MK_PRE_RMS, L.norm1, a.cproj, a.cr_ld, L.q_gate.rows,
-                      MK_EPI_STORE, RQ, m.n_self_layers + 1 + j + kPrefetchAhead);
-    if (!q) return false;
-    if (j == 0) {
-      q->g.xmap_nq = a.nq;
-      q->g.xmap_T = a.T;
-      q->g.xmap_off = a.T - a.nq;
-      q->g.copy_x = a.xc;
-      q->resolve_ctas = sparse ? RQ : 0;  // the exact selection runs beside the first q projection
-    }
-    if (!add(MK_PH_CROSS, j, -1)) return false;
-    if (!gemv(L.o_proj, a.attn, a.att_ld, MK_PRE_NONE, nullptr, a.xc, d, d, MK_EPI_ADD, RQ, -1)) return false;
-    if (!gemv(L.gate_up, a.xc, d, MK_PRE_RMS, L.norm2, a.act, F, F, MK_EPI_ACT, RQ, -1)) return false;
-    if (!gemv(L.down, a.act, F, MK_PRE_NONE, nullptr, a.xc, d, d, MK_EPI_ADD, RQ, -1)) return false;
-  }
-  MkPhase* hd = gemv(m.lm_head, a.xc, d, MK_PRE_RMS, m.final_norm, a.logits ? a.logits : a.ws_logits, m.vocab_size,
-                     m.vocab_size, MK_EPI_STORE, RQ, -1);
-  if (!hd) return false;
-  hd->g.argmax = 1;
-  hd->copy_hidden = 1;
-  a.n_phases = n;
-  return true;
-}
 
 bool mk_supported(const CbModel& m, const CbCache& c, int T, int nq) {
   const int G = m.n_q_heads / m.n_kv_heads;

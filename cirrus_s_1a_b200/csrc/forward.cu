@@ -202,7 +202,6 @@ static int launch_persistent(const CbModel& m, const CbCache& c, const Workspace
   a.hidden = hidden;
   a.argmax = argmax;
   a.timeout_ns = 200ull * 1000 * 1000;
-  if (!mk_build_plan(a)) return CB_ERR_SHAPE;
   if (cudaMemsetAsync(w.sync, 0, 256, st) != cudaSuccess) return CB_ERR_CUDA;
   return launch_mk(a, num_sms(), st);
 }
