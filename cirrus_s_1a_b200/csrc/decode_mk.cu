@@ -5,15 +5,17 @@
 // Phases (each followed by a grid barrier):
 //   self layer:  in-proj GEMV (norm1 fused; layer 0 gathers the embedding)
 //                -> GDN heads | SWA (q/k norm + RoPE + ring append + split
-//                   attention, the last CTA of a KV head combines and gates)
-//                -> o-proj GEMV (+ residual) -> gate_up GEMV producing silu(g)*u
+//                   attention partials)
+//                -> o-proj GEMV (+ residual; after SWA its input staging merges
+//                   the split partials and applies the output gate)
+//                -> gate_up GEMV producing silu(g)*u
 //                -> down GEMV (+ residual)
 //   shared KV:   projection GEMV -> K/V/indexer-key append + indexer scores with
 //                a 2048-bin histogram of the score keys -> threshold bin and
 //                compaction -> exact selection (one CTA per query row, run
 //                alongside the first cross layer's q GEMV)
-//   cross layer: q|gate GEMV -> selected-key attention (split, last arriver
-//                combines) -> o-proj -> gate_up -> down
+//   cross layer: q|gate GEMV -> selected-key attention (split partials)
+//                -> o-proj (merging the partials) -> gate_up -> down
 //   head:        LM-head GEMV (final norm fused) with a per-row argmax
 // At start every CTA issues L2 prefetches for its share of all weights and of
 // the recurrent / window state the step will read, so HBM streams at full
@@ -34,7 +36,7 @@ constexpr int kSmem = 160 * 1024;
 constexpr int kMaxSort = 4096;
 constexpr int kMkBitmapWords = 4096;  // selection bitmap: up to 131072 keys
 
-enum { PRE_NONE_ = 0, PRE_RMS_ = 1, PRE_EMBED_ = 2 };
+enum { PRE_NONE_ = 0, PRE_RMS_ = 1, PRE_EMBED_ = 2, PRE_COMBINE_ = 3 };
 enum { EPI_STORE_ = 0, EPI_ADD_ = 1, EPI_ACT_ = 2 };
 
 // ------------------------------------------------------------------ sync
@@ -175,6 +177,13 @@ struct GemvJob {
   int ldy, rows_out, epi;
   float* copy_x;                  // local CTA 0 stores the raw input rows here ([m][K])
   bool argmax;
+  // PRE_COMBINE: the input is the gated merge of split-softmax attention
+  // partials, part[((m * H + h) * S + s) * (hd + 2)] = (max, sum, o[hd]), with
+  // the output gate sigmoid(gate_x[m * gate_ld + gate_off + h])
+  const float* part;
+  int S, hd;
+  const float* gate_x;
+  int gate_ld, gate_off;
 };
 
 // One weight row as seen by one lane: the 8-code chunks lane, lane+32, ...
@@ -237,7 +246,6 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
   if (cta < 0 || cta >= units || ncta <= 0) return;
   const int K = g.W.k, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float* xs = smem;  // [M][K]
-  __shared__ float rs[kMkMaxRows];
   __shared__ unsigned long long s_best[kMkMaxRows];
   const int64_t tb = tile_bytes(K);
   const int step = g.epi == EPI_ACT_ ? ncta : 2 * ncta;
@@ -281,7 +289,7 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
   __shared__ float wsq[kW][kMkMaxRows];  // per-warp partial sums of squares (summed in a fixed order)
   if (g.argmax && tid < kMkMaxRows) s_best[tid] = 0ull;
   __syncthreads();
-  const bool norm = g.pre != PRE_NONE_;
+  const bool norm = g.pre == PRE_RMS_ || g.pre == PRE_EMBED_;
   const bool copy = g.copy_x != nullptr && cta == 0;
   float sq[M];
 #pragma unroll
@@ -316,6 +324,41 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
         if (q == mr) sq[q] += v0 * v0 + v1 * v1;
       xs[mr * K + 2 * j] = v0 * g.norm_w[2 * j];
       xs[mr * K + 2 * j + 1] = v1 * g.norm_w[2 * j + 1];
+    }
+  } else if (g.pre == PRE_COMBINE_) {
+    // Merge the S <= 32 split partials of every (row, head): a warp per pair,
+    // a lane per split: w_s = exp(m_s - max m), coef_s = w_s * gate / sum_s w_s l_s;
+    // then x = sum_s coef_s o_s with the loads of 8 splits in flight at a time.
+    const int hd = g.hd, H = K / hd, S = g.S, per = hd + 2;
+    float* coef = smem + M * K;  // [M][H][32]
+    for (int i = warp; i < m_rows * H; i += kW) {
+      const int mr = i / H, h = i - mr * H;
+      const float* pb = g.part + (int64_t)i * S * per + lane * per;
+      const float ms = lane < S ? __ldcg(pb) : -INFINITY;
+      const float ls = lane < S ? __ldcg(pb + 1) : 0.0f;
+      const float gt = __ldcg(g.gate_x + (int64_t)mr * g.gate_ld + g.gate_off + h);
+      const float mx = warp_max(ms);
+      const float w = ms == -INFINITY ? 0.0f : expf(ms - mx);
+      const float L = warp_sum(w * ls);
+      coef[i * 32 + lane] = w * (sigmoid(gt) / L);
+    }
+    __syncthreads();
+    for (int i = tid; i < M * K; i += kT) {
+      const int mr = i / K, k = i - mr * K;
+      float v = 0.0f;
+      if (mr < m_rows) {
+        const int h = k / hd, d = k - h * hd;
+        const float* pb = g.part + (int64_t)(mr * H + h) * S * per + 2 + d;
+        const float* cf = coef + (mr * H + h) * 32;
+        for (int s0 = 0; s0 < S; s0 += 8) {  // 8 loads in flight per batch
+          float o[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[e] = s0 + e < S ? __ldcg(pb + (s0 + e) * per) : 0.0f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v = fmaf(cf[s0 + e], o[e], v);
+        }
+      }
+      xs[i] = v;
     }
   } else {
 #pragma unroll 4
@@ -582,6 +625,15 @@ __device__ void gdn_phase(const MkArgs& a, const CbSelfLayer& L, int cta, int nc
   }
 }
 
+// 16-byte asynchronous global -> shared copies (no registers held while they fly)
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 // ------------------------------------------- attention helpers (split softmax)
 // Scores of nq queries (Qs [nq][hd]) against n keys (Ks [n][hd+1]) into Sc [nq][ldsc],
 // masked entries -inf; then per query max / exp / sum (qm, ql) and o += e V into oacc.
@@ -597,12 +649,18 @@ __device__ void attend_chunk(const float* Qs, const float* Ks, const float* Vs, 
       ok = kp <= pt && kp > pt - window;
     }
     float sc = -INFINITY;
-    if (ok) {
+    if (ok) {  // four independent chains over d (hd % 8 == 0), summed in a fixed order
       const float* qq = Qs + q * hd;
       const float* kk = Ks + key * (hd + 1);
-      float acc = 0.0f;
-      for (int d = 0; d < hd; ++d) acc = fmaf(qq[d], kk[d], acc);
-      sc = acc * scale;
+      float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+#pragma unroll 2
+      for (int d = 0; d < hd; d += 4) {
+        a0 = fmaf(qq[d], kk[d], a0);
+        a1 = fmaf(qq[d + 1], kk[d + 1], a1);
+        a2 = fmaf(qq[d + 2], kk[d + 2], a2);
+        a3 = fmaf(qq[d + 3], kk[d + 3], a3);
+      }
+      sc = ((a0 + a1) + (a2 + a3)) * scale;
     }
     Sc[q * ldsc + key] = sc;
   }
@@ -630,70 +688,18 @@ __device__ void attend_chunk(const float* Qs, const float* Ks, const float* Vs, 
   __syncthreads();
   for (int i = tid; i < nq * hd; i += kT) {
     const int q = i / hd, d = i - q * hd;
-    float o = oacc[i] * corr[q];
     const float* e = Sc + q * ldsc;
-#pragma unroll 8
-    for (int key = 0; key < n; ++key) o = fmaf(e[key], Vs[key * hd + d], o);
-    oacc[i] = o;
-  }
-  __syncthreads();
-}
-
-// Last arriver of `count` CTAs on counter `ctr`: returns true on exactly one CTA.
-__device__ bool arrive_last(unsigned* ctr, unsigned count, int* s_flag) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned prev = atomicAdd(ctr, 1u);
-    *s_flag = prev == count - 1;
-    if (*s_flag) {
-      *ctr = 0u;  // ready for the next phase (ordered after it by the grid barrier)
-      __threadfence();
+    float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;  // keys mod 4, summed in a fixed order
+    int key = 0;
+#pragma unroll 2
+    for (; key + 4 <= n; key += 4) {
+      o0 = fmaf(e[key], Vs[key * hd + d], o0);
+      o1 = fmaf(e[key + 1], Vs[(key + 1) * hd + d], o1);
+      o2 = fmaf(e[key + 2], Vs[(key + 2) * hd + d], o2);
+      o3 = fmaf(e[key + 3], Vs[(key + 3) * hd + d], o3);
     }
-  }
-  __syncthreads();
-  return *s_flag != 0;
-}
-
-// Combine the split partials (m, l, o[hd]) of nq queries.  base(q) points at
-// query q's S consecutive partials; out(q, d) receives (sum_s w_s o_s[d]) /
-// (sum_s w_s l_s) * gate(q) with w_s = exp(m_s - max_s m_s).  All partials are
-// loaded into shared memory in one pass.
-template <typename BaseF, typename GateF, typename OutF>
-__device__ void combine_splits(int nq, int S, int hd, float* smem, BaseF base, GateF gate, OutF out) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int per = S * (hd + 2);
-  float* P = smem;  // [nq][S][hd + 2]
-  __shared__ float qL[kMkMaxQ], qg[kMkMaxQ];
-#pragma unroll 4
-  for (int i = tid; i < nq * per; i += kT) {
-    const int q = i / per, e = i - q * per;
-    P[i] = __ldcg(base(q) + e);
-  }
-  for (int q = tid; q < nq; q += kT) qg[q] = gate(q);
-  __syncthreads();
-  for (int q = warp; q < nq; q += kW) {
-    float* Pq = P + q * per;
-    float M = -INFINITY;
-    for (int s2 = lane; s2 < S; s2 += 32) M = fmaxf(M, Pq[s2 * (hd + 2)]);
-    M = warp_max(M);
-    float L = 0.0f;
-    for (int s2 = lane; s2 < S; s2 += 32) {
-      const float ms = Pq[s2 * (hd + 2)];
-      const float w = ms == -INFINITY ? 0.0f : expf(ms - M);
-      L += w * Pq[s2 * (hd + 2) + 1];
-      Pq[s2 * (hd + 2)] = w;
-    }
-    L = warp_sum(L);
-    if (lane == 0) qL[q] = L;
-  }
-  __syncthreads();
-  for (int i = tid; i < nq * hd; i += kT) {
-    const int q = i / hd, d = i - q * hd;
-    const float* Pq = P + q * per;
-    float O = 0.0f;
-    for (int s2 = 0; s2 < S; ++s2) O = fmaf(Pq[s2 * (hd + 2)], Pq[s2 * (hd + 2) + 2 + d], O);
-    out(q, d, (O / qL[q]) * qg[q]);
+    for (; key < n; ++key) o0 = fmaf(e[key], Vs[key * hd + d], o0);
+    oacc[i] = fmaf(oacc[i], corr[q], (o0 + o1) + (o2 + o3));
   }
   __syncthreads();
 }
@@ -715,19 +721,30 @@ __device__ void swa_item(const MkArgs& a, const CbSelfLayer& L, int b, int g, in
   float* oacc = Sc + kMkMaxQ * Ls;     // [kMkMaxQ][hd]
   __shared__ float qm[kMkMaxQ], ql[kMkMaxQ], corr[kMkMaxQ];
   __shared__ int kpos[kMkSwaSplit], qpos[kMkMaxQ];
-  __shared__ int s_flag;
   const int64_t ring = (int64_t)(b * c.n_swa + L.slot) * c.swa_slots * Hkv * hd;
   uint16_t* kr = c.swa_k + ring;
   uint16_t* vr = c.swa_v + ring;
 
+  uint16_t* raw = reinterpret_cast<uint16_t*>(oacc + kMkMaxQ * hd);  // [2][Ls][hd] bf16 ring rows
+  const int vpk = hd / 8;  // 16-byte vectors per key row
+  // the window's ring rows do not depend on this step: start their copies first
+  for (int i = tid; i < n * vpk; i += kT) {
+    const int key = i / vpk, e8 = (i - key * vpk) * 8, kp = ks + key;
+    if (kp < p0) {
+      const int64_t off = ((int64_t)(kp % c.swa_slots) * Hkv + g) * hd + e8;
+      cp_async16(raw + key * hd + e8, kr + off);
+      cp_async16(raw + (Ls + key) * hd + e8, vr + off);
+    }
+  }
   for (int q = warp; q < nqry; q += kW) {
     const int t = q / G, j = q - t * G;
     norm_rope_warp(a.proj + ((int64_t)b * T + t) * a.ldp + (g * G + j) * hd, L.q_norm, hd, m.rot_dim / 2, p0 + t,
                    m.inv_freq, m.norm_eps, Qs + q * hd, false, nullptr);
   }
-  // keys of this chunk's own tokens come from the projection (and are appended to the ring here)
-  const int new0 = max(ks, p0);
-  for (int kp = new0 + warp; kp < ke; kp += kW) {
+  // keys of this chunk's own tokens come from the projection (and are appended
+  // to the ring here), on the warps after the query ones
+  const int new0 = max(ks, p0), wk = (warp + kW - nqry % kW) % kW;
+  for (int kp = new0 + wk; kp < ke; kp += kW) {
     const int idx = kp - ks, t2 = kp - p0;
     const float* row = a.proj + ((int64_t)b * T + t2) * a.ldp;
     const int64_t off = ((int64_t)(kp % c.swa_slots) * Hkv + g) * hd;
@@ -740,14 +757,14 @@ __device__ void swa_item(const MkArgs& a, const CbSelfLayer& L, int b, int g, in
       Vs[idx * hd + d] = bf16_to_f32(bits);
     }
   }
-  const int vpk = hd / 8;  // 16-byte vectors per key row
-#pragma unroll 4
+  cp_async_wait_all();
+  __syncthreads();
+#pragma unroll 2
   for (int i = tid; i < n * vpk; i += kT) {
     const int key = i / vpk, e8 = (i - key * vpk) * 8, kp = ks + key;
     if (kp < p0) {
-      const int64_t off = ((int64_t)(kp % c.swa_slots) * Hkv + g) * hd + e8;
-      const uint4 kq = __ldg(reinterpret_cast<const uint4*>(kr + off));
-      const uint4 vq = __ldg(reinterpret_cast<const uint4*>(vr + off));
+      const uint4 kq = *reinterpret_cast<const uint4*>(raw + key * hd + e8);
+      const uint4 vq = *reinterpret_cast<const uint4*>(raw + (Ls + key) * hd + e8);
       const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w}, vw[4] = {vq.x, vq.y, vq.z, vq.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -773,22 +790,7 @@ __device__ void swa_item(const MkArgs& a, const CbSelfLayer& L, int b, int g, in
     float* pp = a.part + ((((int64_t)b * T + t) * Hq + g * G + j) * S + s) * (hd + 2);
     pp[e] = e == 0 ? qm[q] : (e == 1 ? ql[q] : oacc[q * hd + e - 2]);
   }
-  if (!arrive_last(&a.arrive[b * Hkv + g], (unsigned)S, &s_flag)) return;
-  __threadfence();
-  combine_splits(
-      nqry, S, hd, smem,
-      [&](int q) {
-        const int t = q / G, j = q - t * G;
-        return a.part + (((int64_t)b * T + t) * Hq + g * G + j) * S * (hd + 2);
-      },
-      [&](int q) {
-        const int t = q / G, j = q - t * G;
-        return sigmoid(__ldcg(a.proj + ((int64_t)b * T + t) * a.ldp + m.swa_off_gate + g * G + j));
-      },
-      [&](int q, int d, float v) {
-        const int t = q / G, j = q - t * G;
-        a.attn[((int64_t)b * T + t) * a.att_ld + (g * G + j) * hd + d] = v;
-      });
+  // the o projection merges the partials (PRE_COMBINE)
 }
 
 __device__ void swa_phase(const MkArgs& a, const CbSelfLayer& L, int cta, int ncta, float* smem) {
@@ -819,7 +821,6 @@ __device__ void cross_item(const MkArgs& a, const CbCrossLayer& L, int r, int g,
   float* oacc = Sc + kMkMaxQ * Lc;  // [G][hd]
   __shared__ float qm[kMkMaxQ], ql[kMkMaxQ], corr[kMkMaxQ];
   __shared__ int kid[kMkSwaSplit];
-  __shared__ int s_flag;
   const float* row = a.cproj + (int64_t)r * a.cr_ld;
   for (int j = warp; j < G; j += kW)
     norm_rope_warp(row + (g * G + j) * hd, L.q_norm, hd, m.rot_dim / 2, position, m.inv_freq, m.norm_eps, Qs + j * hd,
@@ -833,8 +834,10 @@ __device__ void cross_item(const MkArgs& a, const CbCrossLayer& L, int r, int g,
   const uint16_t* vb = c.kv_v + (int64_t)b * c.max_ctx * Hkv * hd;
   for (int c0 = ks; c0 < ke; c0 += Lc) {
     const int cn = min(Lc, ke - c0);
-    __syncthreads();
-    for (int i = tid; i < cn; i += kT) kid[i] = dense ? c0 + i : __ldcg(a.sel_idx + (int64_t)r * a.sel_ld + c0 + i);
+    // (the previous chunk's attend_chunk ended with a barrier; kid is free)
+    // on the warps after the query ones, so the first chunk's ids load beside the q RoPE
+    for (int i = (tid + kT - 32 * (G % kW)) % kT; i < cn; i += kT)
+      kid[i] = dense ? c0 + i : __ldcg(a.sel_idx + (int64_t)r * a.sel_ld + c0 + i);
     __syncthreads();
     const int vpk = hd / 8;
 #pragma unroll 4
@@ -861,12 +864,7 @@ __device__ void cross_item(const MkArgs& a, const CbCrossLayer& L, int r, int g,
     float* pp = a.part2 + (((int64_t)r * Hq + g * G + j) * S + s) * (hd + 2);
     pp[e] = e == 0 ? qm[j] : (e == 1 ? ql[j] : oacc[j * hd + e - 2]);
   }
-  if (!arrive_last(&a.arrive[kMkArrive / 2 + r * Hkv + g], (unsigned)S, &s_flag)) return;
-  __threadfence();
-  combine_splits(
-      G, S, hd, smem, [&](int j) { return a.part2 + ((int64_t)r * Hq + g * G + j) * S * (hd + 2); },
-      [&](int j) { return sigmoid(__ldcg(row + m.cr_off_gate + g * G + j)); },
-      [&](int j, int d, float v) { a.attn[(int64_t)r * a.att_ld + (g * G + j) * hd + d] = v; });
+  // the o projection merges the partials (PRE_COMBINE)
 }
 
 __device__ void cross_phase(const MkArgs& a, const CbCrossLayer& L, int cta, int ncta, float* smem) {
@@ -1212,7 +1210,6 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
       a.cand_cnt[i] = 0;
       a.amax[i] = 0ull;
     }
-    for (int i = tid; i < kMkArrive; i += kT) a.arrive[i] = 0u;
   }
   if (cta == 0 && tid == 0) a.trace[0] = gtimer();
   for (int u = 0; u < kPrefetchAhead; ++u) prefetch_unit(a, u);
@@ -1241,6 +1238,15 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     o.W = L.o_proj;
     o.x = a.attn;
     o.ldx = a.att_ld;
+    if (L.kind == CB_LAYER_SWA) {
+      o.pre = PRE_COMBINE_;
+      o.part = a.part;
+      o.S = a.swa_splits;
+      o.hd = m.head_dim;
+      o.gate_x = a.proj;
+      o.gate_ld = a.ldp;
+      o.gate_off = m.swa_off_gate;
+    }
     o.y = a.h;
     o.ldy = d;
     o.rows_out = d;
@@ -1327,6 +1333,13 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     o.W = L.o_proj;
     o.x = a.attn;
     o.ldx = a.att_ld;
+    o.pre = PRE_COMBINE_;
+    o.part = a.part2;
+    o.S = a.cross_splits;
+    o.hd = m.head_dim;
+    o.gate_x = a.cproj;
+    o.gate_ld = a.cr_ld;
+    o.gate_off = m.cr_off_gate;
     o.y = a.xc;
     o.ldy = d;
     o.rows_out = d;
@@ -1400,9 +1413,16 @@ bool mk_supported(const CbModel& m, const CbCache& c, int T, int nq) {
                             CB_MAX_T * m.indexer_dim > kSmem))
     return false;
   const size_t att = sizeof(float) * ((size_t)kMkSwaSplit * (2 * m.head_dim + 1) + (size_t)kMkMaxQ * m.head_dim * 2 +
-                                      (size_t)kMkMaxQ * kMkSwaSplit);
+                                      (size_t)kMkMaxQ * kMkSwaSplit) +
+                     sizeof(uint16_t) * 2 * kMkSwaSplit * m.head_dim;
   if (att > (size_t)kSmem) return false;
   if ((size_t)kMkMaxRows * 2048 * sizeof(float) > (size_t)kSmem) return false;
+  {  // o projection staging with the split merge: [M][K] inputs + [M][H][32] weights, S <= 32 splits
+    const int sw = ceil_div(m.swa_window + CB_MAX_T, kMkSwaSplit);
+    const int sc = m.sparse_topk > 0 ? ceil_div(m.sparse_topk + 1, kMkCrossSplit) : 32;
+    const size_t need = (size_t)kMkMaxRows * m.n_q_heads * (m.head_dim + 32) * sizeof(float);
+    if (need > (size_t)kSmem || sw > 32 || sc > 32) return false;
+  }
   return true;
 }
 

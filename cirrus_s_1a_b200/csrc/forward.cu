@@ -47,7 +47,6 @@ struct Workspace {
   int32_t* hi_cnt;
   unsigned long long* cand;
   int32_t* cand_cnt;
-  unsigned* arrive;
   unsigned long long* amax64;
   unsigned* sync;     // [0] barrier counter, [32] abort flag
   unsigned long long* trace;
@@ -100,7 +99,6 @@ static Workspace carve(const CbModel& m, int batch, int T, int max_ctx, char* ba
   w.hi_cnt = (int32_t*)take(sizeof(int32_t) * R);
   w.cand = (unsigned long long*)take(sp ? sizeof(unsigned long long) * R * (size_t)max_ctx : 0);
   w.cand_cnt = (int32_t*)take(sizeof(int32_t) * R);
-  w.arrive = (unsigned*)take(sizeof(unsigned) * kMkArrive);
   w.amax64 = (unsigned long long*)take(sizeof(unsigned long long) * R);
   w.sync = (unsigned*)take(256);
   w.trace = (unsigned long long*)take(sizeof(unsigned long long) * kMkTrace);
@@ -180,7 +178,6 @@ static int launch_persistent(const CbModel& m, const CbCache& c, const Workspace
   a.cand_cnt = w.cand_cnt;
   a.sel_idx = w.sel_idx;
   a.sel_cnt = w.sel_cnt;
-  a.arrive = w.arrive;
   a.amax = w.amax64;
   a.sync = w.sync;
   a.trace = w.trace;

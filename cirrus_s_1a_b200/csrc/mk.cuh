@@ -14,7 +14,6 @@ constexpr int kMkSwaSplit = 128;       // window keys per SWA work item
 constexpr int kMkCrossSplit = 64;      // selected keys per cross-attention work item
 constexpr int kMkMaxRows = 8;          // batch * T handled by one persistent launch
 constexpr int kMkMaxQ = 24;            // (q heads per KV head) * T per SWA work item
-constexpr int kMkArrive = 512;         // last-arriver counters
 constexpr int kMkTrace = 512;          // phase timestamps
 
 // Everything one persistent launch needs, passed by value (__grid_constant__).
@@ -39,7 +38,6 @@ struct MkArgs {
   int32_t* cand_cnt; // [RQ]
   int32_t* sel_idx;  // [RQ][sel_ld]
   int32_t* sel_cnt;  // [RQ]
-  unsigned* arrive;  // [kMkArrive]
   unsigned long long* amax;  // [RQ] packed argmax
   unsigned* sync;    // grid barrier counter (zeroed before every launch)
   unsigned long long* trace;  // [kMkTrace] phase timestamps of CTA 0
