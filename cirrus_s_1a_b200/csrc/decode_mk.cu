@@ -54,17 +54,24 @@ __device__ __forceinline__ unsigned long long gtimer() {
   return t;
 }
 
-// Grid barrier on a monotonic arrival counter.  Returns false when the launch
+// Grid barrier on a monotonic arrival counter, split in two: grid_arrive
+// publishes this CTA's writes and counts it in; grid_wait waits for every CTA.
+// Work that does not depend on the other CTAs' writes (the next phase's
+// weight loads) goes between the two.  grid_wait returns false when the launch
 // must stop (this CTA's wait timed out, or another CTA's did).
-__device__ bool grid_sync(const MkArgs& a, unsigned& gen, int* s_ok) {
+__device__ __forceinline__ void grid_arrive(const MkArgs& a, unsigned& gen) {
   __syncthreads();
+  gen += 1;
   if (threadIdx.x == 0) {
-    gen += 1;
-    const unsigned target = gen * gridDim.x;
-    const bool tr = blockIdx.x == 0 && 2 * gen < (unsigned)kMkTrace;
-    if (tr) a.trace[2 * gen - 1] = gtimer();
+    if (blockIdx.x == 0 && 2 * gen < (unsigned)kMkTrace) a.trace[2 * gen - 1] = gtimer();
     __threadfence();
     atomicAdd(a.sync, 1u);
+  }
+}
+
+__device__ __forceinline__ bool grid_wait(const MkArgs& a, unsigned gen, int* s_ok) {
+  if (threadIdx.x == 0) {
+    const unsigned target = gen * gridDim.x;
     int ok = 1;
     const unsigned long long t0 = gtimer();
     unsigned spin = 0;
@@ -82,11 +89,29 @@ __device__ bool grid_sync(const MkArgs& a, unsigned& gen, int* s_ok) {
         }
       }
     }
-    if (tr) a.trace[2 * gen] = gtimer();
+    if (blockIdx.x == 0 && 2 * gen < (unsigned)kMkTrace) a.trace[2 * gen] = gtimer();
     *s_ok = ok;
   }
   __syncthreads();
   return *s_ok != 0;
+}
+
+__device__ __forceinline__ bool grid_sync(const MkArgs& a, unsigned& gen, int* s_ok) {
+  grid_arrive(a, gen);
+  return grid_wait(a, gen, s_ok);
+}
+
+// Asynchronous global -> shared copies (no registers held while they fly)
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
 // -------------------------------------------------------------- prefetch
@@ -240,31 +265,109 @@ __device__ __forceinline__ unsigned long long pack_argmax(float v, int idx) {
   return ((unsigned long long)score_key(v) << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)idx);
 }
 
+// Rows of unit u for this warp: ACT pairs gate row ra with up row rb; the
+// other epilogues pair units u and u + ncta (rb valid when hb).
+__device__ __forceinline__ void gemv_rows(const GemvJob& g, int units, int ncta, int u, int& ra, int& rb, bool& hb) {
+  const int warp = threadIdx.x >> 5;
+  if (g.epi == EPI_ACT_) {
+    ra = u * kTileRows + warp;
+    rb = g.W.rows / 2 + u * kTileRows + warp;
+    hb = true;
+  } else {
+    const int ub = u + ncta;
+    ra = u * kTileRows + warp;
+    hb = ub < units;
+    rb = ub * kTileRows + warp;
+  }
+}
+
+__device__ __forceinline__ int gemv_units(const GemvJob& g) {
+  return g.epi == EPI_ACT_ ? g.W.rows / 32 : g.W.rows / kTileRows;
+}
+
+// The first unit's weights and, for a residual add, the old outputs: they do
+// not depend on the previous phase, so they are fetched between the arrival at
+// its barrier and the wait there.  The weight rows go by asynchronous copies
+// into a per-warp shared-memory slot at kPreOff (two rows of codes + scales),
+// so no registers stay live across the barrier; the residuals are registers.
+constexpr int kPreOff = 96 * 1024;
+__host__ __device__ constexpr int pre_row_bytes(int K) { return ((9 * K / 16) + 15) & ~15; }
+static_assert(kPreOff + kW * 2 * pre_row_bytes(2048) <= kSmem, "preload slots exceed the scratch");
+
 template <int M>
-__device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int cta, int ncta, float* smem) {
-  const int units = g.epi == EPI_ACT_ ? g.W.rows / 32 : g.W.rows / kTileRows;
+struct GemvPre {
+  float resa[M], resb[M];
+};
+
+// The copies move 16-byte code chunks and 4-byte scale chunks: K % 64 == 0.
+// Other K load the first unit directly after the barrier.
+__device__ __forceinline__ bool pre_staged(int K) { return K % 64 == 0; }
+
+__device__ __forceinline__ uint8_t* pre_slot(float* smem, int K) {
+  return reinterpret_cast<uint8_t*>(smem) + kPreOff + (threadIdx.x >> 5) * 2 * pre_row_bytes(K);
+}
+
+__device__ __forceinline__ void pre_copy_row(const CbMatrix& W, int K, int row, uint8_t* dst) {
+  const int lane = threadIdx.x & 31;
+  const uint8_t* t = W.tiles + (int64_t)(row >> 4) * tile_bytes(K);
+  const uint8_t* codes = t + (row & 15) * (K / 2);
+  const uint8_t* sc = t + kTileRows * (K / 2) + (row & 15) * (K / 16);
+  for (int i = lane; i < K / 32; i += 32) cp_async16(dst + 16 * i, codes + 16 * i);
+  for (int i = lane; i < K / 64; i += 32) cp_async4(dst + K / 2 + 4 * i, sc + 4 * i);
+}
+
+// The lane's view of a preloaded row (the layout load_row produces).
+__device__ __forceinline__ void pre_read_row(const uint8_t* src, int K, bool valid, RowW& r) {
+  const int lane = threadIdx.x & 31, kc = K >> 3;
+  const uint32_t* cw = reinterpret_cast<const uint32_t*>(src);
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int c = u * 32 + lane;
+    const bool ok = valid && c < kc;
+    r.w[u] = ok ? cw[c] : 0u;
+    r.s[u] = ok ? (uint32_t)src[K / 2 + (c >> 1)] : 0u;
+  }
+}
+
+template <int M>
+__device__ __forceinline__ void gemv_pre(const GemvJob& g, int m_rows, int cta, int ncta, float* smem,
+                                         GemvPre<M>& p) {
+  const int units = gemv_units(g);
+  if (cta < 0 || cta >= units || ncta <= 0) return;
+  const int K = g.W.k, lane = threadIdx.x & 31;
+  int ra, rb;
+  bool hb;
+  gemv_rows(g, units, ncta, cta, ra, rb, hb);
+  if (pre_staged(K)) {
+    uint8_t* slot = pre_slot(smem, K);
+    pre_copy_row(g.W, K, ra, slot);
+    if (hb) pre_copy_row(g.W, K, rb, slot + pre_row_bytes(K));
+  }
+#pragma unroll
+  for (int mr = 0; mr < M; ++mr) {
+    p.resa[mr] = p.resb[mr] = 0.0f;
+    if (g.epi == EPI_ADD_ && lane == 0 && mr < m_rows) {
+      if (ra < g.rows_out) p.resa[mr] = __ldcg(g.y + (int64_t)mr * g.ldy + ra);
+      if (hb && rb < g.rows_out) p.resb[mr] = __ldcg(g.y + (int64_t)mr * g.ldy + rb);
+    }
+  }
+}
+
+template <int M>
+__device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int cta, int ncta, float* smem,
+                           GemvPre<M>& p) {
+  const int units = gemv_units(g);
   if (cta < 0 || cta >= units || ncta <= 0) return;
   const int K = g.W.k, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float* xs = smem;  // [M][K]
   __shared__ unsigned long long s_best[kMkMaxRows];
   const int64_t tb = tile_bytes(K);
   const int step = g.epi == EPI_ACT_ ? ncta : 2 * ncta;
-  auto rows_of = [&](int u, int& ra, int& rb, bool& hb) {
-    if (g.epi == EPI_ACT_) {
-      ra = u * kTileRows + warp;
-      rb = g.W.rows / 2 + u * kTileRows + warp;
-      hb = true;
-    } else {
-      const int ub = u + ncta;
-      ra = u * kTileRows + warp;
-      hb = ub < units;
-      rb = ub * kTileRows + warp;
-    }
-  };
-  // the first unit's weights (and, for a residual add, the old outputs) do not
-  // depend on the input: load them before staging it
+  auto rows_of = [&](int u, int& ra, int& rb, bool& hb) { gemv_rows(g, units, ncta, u, ra, rb, hb); };
+  cp_async_wait_all();  // this warp's preloaded rows (read after the staging barrier)
   RowW A0, B0;
-  float resa[M], resb[M];
+  float(&resa)[M] = p.resa;
+  float(&resb)[M] = p.resb;
   auto load_res = [&](int ra, int rb, bool hb) {
 #pragma unroll
     for (int mr = 0; mr < M; ++mr) {
@@ -275,14 +378,6 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
       }
     }
   };
-  {
-    int ra, rb;
-    bool hb;
-    rows_of(cta, ra, rb, hb);
-    load_row(g.W, tb, K, ra, true, A0);
-    load_row(g.W, tb, K, rb, hb, B0);
-    load_res(ra, rb, hb);
-  }
 
   // Stage pre(x) = x * norm_w (RMSNorm's per-row scale is applied to the dot
   // products at the end); the sum of squares of each row is reduced on the way.
@@ -405,10 +500,14 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
     int ra, rb;
     bool hb;
     rows_of(u, ra, rb, hb);
-    if (u != cta) {  // the first unit's rows were loaded before the input staging
+    if (u != cta || !pre_staged(K)) {
       load_row(g.W, tb, K, ra, true, A0);
       load_row(g.W, tb, K, rb, hb, B0);
-      load_res(ra, rb, hb);
+      if (u != cta) load_res(ra, rb, hb);
+    } else {  // the first unit's rows were copied to shared memory before the barrier
+      const uint8_t* slot = pre_slot(smem, K);
+      pre_read_row(slot, K, true, A0);
+      pre_read_row(slot + pre_row_bytes(K), K, hb, B0);
     }
     float aa[M], ab[M];
 #pragma unroll
@@ -623,15 +722,6 @@ __device__ void gdn_phase(const MkArgs& a, const CbSelfLayer& L, int cta, int nc
       default: gdn_item<32>(a, L, h, b, smem); break;
     }
   }
-}
-
-// 16-byte asynchronous global -> shared copies (no registers held while they fly)
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
 // ------------------------------------------- attention helpers (split softmax)
@@ -1213,7 +1303,10 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
   }
   if (cta == 0 && tid == 0) a.trace[0] = gtimer();
   for (int u = 0; u < kPrefetchAhead; ++u) prefetch_unit(a, u);
-  if (!grid_sync(a, gen, &s_ok)) return;
+  // Each GEMV's first weights (and residual) are loaded between the arrival at
+  // the barrier before it and the wait there (GemvPre): they do not depend on
+  // the previous phase, so their latency hides behind the barrier.
+  grid_arrive(a, gen);
 
   for (int i = 0; i < m.n_self_layers; ++i) {
     const CbSelfLayer& L = m.self_layers[i];
@@ -1229,11 +1322,19 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     in.rows_out = L.in_proj.rows;
     in.epi = EPI_STORE_;
     in.copy_x = i == 0 ? a.h : nullptr;
-    gemv_phase<M>(a, in, Mrows, cta, ncta, smem);
+    {
+      GemvPre<M> p;
+      gemv_pre<M>(in, Mrows, cta, ncta, smem, p);
+      if (!grid_wait(a, gen, &s_ok)) {
+        cp_async_wait_all();
+        return;
+      }
+      gemv_phase<M>(a, in, Mrows, cta, ncta, smem, p);
+    }
     if (!grid_sync(a, gen, &s_ok)) return;
     if (L.kind == CB_LAYER_GDN) gdn_phase(a, L, cta, ncta, smem);
     else swa_phase(a, L, cta, ncta, smem);
-    if (!grid_sync(a, gen, &s_ok)) return;
+    grid_arrive(a, gen);
     GemvJob o{};
     o.W = L.o_proj;
     o.x = a.attn;
@@ -1251,8 +1352,16 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     o.ldy = d;
     o.rows_out = d;
     o.epi = EPI_ADD_;
-    gemv_phase<M>(a, o, Mrows, cta, ncta, smem);
-    if (!grid_sync(a, gen, &s_ok)) return;
+    {
+      GemvPre<M> p;
+      gemv_pre<M>(o, Mrows, cta, ncta, smem, p);
+      if (!grid_wait(a, gen, &s_ok)) {
+        cp_async_wait_all();
+        return;
+      }
+      gemv_phase<M>(a, o, Mrows, cta, ncta, smem, p);
+    }
+    grid_arrive(a, gen);
     GemvJob gu{};
     gu.W = L.gate_up;
     gu.x = a.h;
@@ -1263,8 +1372,16 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     gu.ldy = F;
     gu.rows_out = F;
     gu.epi = EPI_ACT_;
-    gemv_phase<M>(a, gu, Mrows, cta, ncta, smem);
-    if (!grid_sync(a, gen, &s_ok)) return;
+    {
+      GemvPre<M> p;
+      gemv_pre<M>(gu, Mrows, cta, ncta, smem, p);
+      if (!grid_wait(a, gen, &s_ok)) {
+        cp_async_wait_all();
+        return;
+      }
+      gemv_phase<M>(a, gu, Mrows, cta, ncta, smem, p);
+    }
+    grid_arrive(a, gen);
     GemvJob dn{};
     dn.W = L.down;
     dn.x = a.act;
@@ -1273,8 +1390,16 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     dn.ldy = d;
     dn.rows_out = d;
     dn.epi = EPI_ADD_;
-    gemv_phase<M>(a, dn, Mrows, cta, ncta, smem);
-    if (!grid_sync(a, gen, &s_ok)) return;
+    {
+      GemvPre<M> p;
+      gemv_pre<M>(dn, Mrows, cta, ncta, smem, p);
+      if (!grid_wait(a, gen, &s_ok)) {
+        cp_async_wait_all();
+        return;
+      }
+      gemv_phase<M>(a, dn, Mrows, cta, ncta, smem, p);
+    }
+    grid_arrive(a, gen);
   }
 
   prefetch_unit(a, m.n_self_layers + kPrefetchAhead);
@@ -1289,15 +1414,22 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     sh.ldy = a.ldp;
     sh.rows_out = m.shared_proj.rows;
     sh.epi = EPI_STORE_;
-    gemv_phase<M>(a, sh, Mrows, cta, ncta, smem);
+    GemvPre<M> p;
+    gemv_pre<M>(sh, Mrows, cta, ncta, smem, p);
+    if (!grid_wait(a, gen, &s_ok)) {
+      cp_async_wait_all();
+      return;
+    }
+    gemv_phase<M>(a, sh, Mrows, cta, ncta, smem, p);
   }
   if (!grid_sync(a, gen, &s_ok)) return;
   shared_append(a, cta, ncta, smem);
   if (sparse) score_phase(a, cta, ncta, smem);
-  if (!grid_sync(a, gen, &s_ok)) return;
+  grid_arrive(a, gen);
   if (sparse) {
+    if (!grid_wait(a, gen, &s_ok)) return;
     compact_phase(a, cta, ncta, smem);
-    if (!grid_sync(a, gen, &s_ok)) return;
+    grid_arrive(a, gen);
   }
 
   for (int j = 0; j < m.n_cross_layers; ++j) {
@@ -1319,16 +1451,22 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     q.ldy = a.cr_ld;
     q.rows_out = L.q_gate.rows;
     q.epi = EPI_STORE_;
-    if (j == 0 && sparse) {
+    {
       // the exact selection of each query row runs beside the first q projection
-      if (cta < RQ) resolve_row(a, cta, smem);
-      else gemv_phase<M>(a, q, RQ, cta - RQ, ncta - RQ, smem);
-    } else {
-      gemv_phase<M>(a, q, RQ, cta, ncta, smem);
+      const bool beside = j == 0 && sparse;
+      const int qc = beside ? cta - RQ : cta, qn = beside ? ncta - RQ : ncta;
+      GemvPre<M> p;
+      gemv_pre<M>(q, RQ, qc, qn, smem, p);
+      if (!grid_wait(a, gen, &s_ok)) {
+        cp_async_wait_all();
+        return;
+      }
+      if (beside && cta < RQ) resolve_row(a, cta, smem);
+      else gemv_phase<M>(a, q, RQ, qc, qn, smem, p);
     }
     if (!grid_sync(a, gen, &s_ok)) return;
     cross_phase(a, L, cta, ncta, smem);
-    if (!grid_sync(a, gen, &s_ok)) return;
+    grid_arrive(a, gen);
     GemvJob o{};
     o.W = L.o_proj;
     o.x = a.attn;
@@ -1344,8 +1482,16 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     o.ldy = d;
     o.rows_out = d;
     o.epi = EPI_ADD_;
-    gemv_phase<M>(a, o, RQ, cta, ncta, smem);
-    if (!grid_sync(a, gen, &s_ok)) return;
+    {
+      GemvPre<M> p;
+      gemv_pre<M>(o, RQ, cta, ncta, smem, p);
+      if (!grid_wait(a, gen, &s_ok)) {
+        cp_async_wait_all();
+        return;
+      }
+      gemv_phase<M>(a, o, RQ, cta, ncta, smem, p);
+    }
+    grid_arrive(a, gen);
     GemvJob gu{};
     gu.W = L.gate_up;
     gu.x = a.xc;
@@ -1356,8 +1502,16 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     gu.ldy = F;
     gu.rows_out = F;
     gu.epi = EPI_ACT_;
-    gemv_phase<M>(a, gu, RQ, cta, ncta, smem);
-    if (!grid_sync(a, gen, &s_ok)) return;
+    {
+      GemvPre<M> p;
+      gemv_pre<M>(gu, RQ, cta, ncta, smem, p);
+      if (!grid_wait(a, gen, &s_ok)) {
+        cp_async_wait_all();
+        return;
+      }
+      gemv_phase<M>(a, gu, RQ, cta, ncta, smem, p);
+    }
+    grid_arrive(a, gen);
     GemvJob dn{};
     dn.W = L.down;
     dn.x = a.act;
@@ -1366,8 +1520,16 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     dn.ldy = d;
     dn.rows_out = d;
     dn.epi = EPI_ADD_;
-    gemv_phase<M>(a, dn, RQ, cta, ncta, smem);
-    if (!grid_sync(a, gen, &s_ok)) return;
+    {
+      GemvPre<M> p;
+      gemv_pre<M>(dn, RQ, cta, ncta, smem, p);
+      if (!grid_wait(a, gen, &s_ok)) {
+        cp_async_wait_all();
+        return;
+      }
+      gemv_phase<M>(a, dn, RQ, cta, ncta, smem, p);
+    }
+    grid_arrive(a, gen);
   }
 
   {
@@ -1382,7 +1544,13 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     hd.rows_out = m.vocab_size;
     hd.epi = EPI_STORE_;
     hd.argmax = true;
-    gemv_phase<M>(a, hd, RQ, cta, ncta, smem);
+    GemvPre<M> p;
+    gemv_pre<M>(hd, RQ, cta, ncta, smem, p);
+    if (!grid_wait(a, gen, &s_ok)) {
+      cp_async_wait_all();
+      return;
+    }
+    gemv_phase<M>(a, hd, RQ, cta, ncta, smem, p);
     if (a.hidden != nullptr && cta == ncta - 1)
       for (int i = tid; i < RQ * d; i += kT) a.hidden[i] = __ldcg(a.xc + i);
   }
@@ -1417,6 +1585,18 @@ bool mk_supported(const CbModel& m, const CbCache& c, int T, int nq) {
                      sizeof(uint16_t) * 2 * kMkSwaSplit * m.head_dim;
   if (att > (size_t)kSmem) return false;
   if ((size_t)kMkMaxRows * 2048 * sizeof(float) > (size_t)kSmem) return false;
+  {  // GEMV staging ([M][K] inputs, K <= 2048) stays below the preload slots at kPreOff
+    int kmax = std::max(m.lm_head.k, m.shared_proj.k);
+    for (int i = 0; i < m.n_self_layers; ++i) {
+      const CbSelfLayer& L = m.self_layers[i];
+      kmax = std::max({kmax, L.in_proj.k, L.o_proj.k, L.gate_up.k, L.down.k});
+    }
+    for (int j = 0; j < m.n_cross_layers; ++j) {
+      const CbCrossLayer& L = m.cross_layers[j];
+      kmax = std::max({kmax, L.q_gate.k, L.o_proj.k, L.gate_up.k, L.down.k});
+    }
+    if (kmax > 2048 || (size_t)kMkMaxRows * (kmax + m.n_q_heads * 32) * sizeof(float) > (size_t)kPreOff) return false;
+  }
   {  // o projection staging with the split merge: [M][K] inputs + [M][H][32] weights, S <= 32 splits
     const int sw = ceil_div(m.swa_window + CB_MAX_T, kMkSwaSplit);
     const int sc = m.sparse_topk > 0 ? ceil_div(m.sparse_topk + 1, kMkCrossSplit) : 32;
