@@ -17,10 +17,12 @@ One JSON line on rank 0:
   e2e          the same through the public DecodeGraph API with the token id
                copied in from pinned host memory and the argmax token copied
                back every step
-  roofline     the NVFP4 weight stream (every projection of a step, M = 1)
-               timed as its own CUDA graph: algorithmic bytes / time vs the
-               measured HBM copy bandwidth
-  step_roofline  the whole step's algorithmic bytes / step time
+  roofline     the dominant kernel, the persistent decode kernel (one launch
+               is one whole step): the step's algorithmic bytes / its CUDA-event
+               time vs the measured HBM copy bandwidth; ``traffic`` is the DRAM
+               read + write of one launch from an ncu capture of this workload
+  weight_stream  the NVFP4 weight stream alone (every projection of a step,
+               M = 1, as separate GEMV launches in one CUDA graph)
   cpu_baseline the oracle restatement of the reference forward on the host
                cores (rank 0, N = 1, a bounded number of 32K-context steps)
 
@@ -45,6 +47,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s (batch 1, τ=1, 32K ctx) per B200 + HBM GB/s vs 8 TB/s; box tok/s 1/2/4/8"
+# DRAM bytes (read + write) of one decode_mk_kernel<1> launch at this workload,
+# from `ncu --set full` (dram__bytes_read.sum + dram__bytes_write.sum); see
+# profiles/decode_mk_kernel_step_32k.md for the command
+DECODE_MK_TRAFFIC = 95_655_424 + 4_238_080
 PUBLISHED_TOK_S = 1815.0  # reference: decode tok/s at 32K, tau=1 (GB10, measured stream + roofline remainder)
 CTX = 32768
 FLUSH_BYTES = 512 << 20
@@ -98,7 +104,8 @@ class ClockSampler:
         mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
         reasons = sorted({n for r in self.rows for n, v in zip(names, r[3:]) if v.lower().startswith("active")})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+                "reasons": reasons, "samples": len(self.rows),
+                "window": "1.2 s of the same steps right before the timed steps, and the timed steps"}
 
 
 def step_bytes(cfg, weight_bytes: float, ctx: int) -> dict:
@@ -310,7 +317,16 @@ def main() -> None:
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize(dev)
+    # nvidia-smi samples every 200 ms: keep the GPU on this same workload for
+    # about a second before the timed steps so the samples cover the load the
+    # timed region runs under (and the timed region itself when it is long)
     sampler.start()
+    t_probe = time.perf_counter()
+    while time.perf_counter() - t_probe < 1.2:
+        for _ in range(20):
+            reset()
+            graph.replay()
+        torch.cuda.synchronize(dev)
     for i in range(args.steps):
         reset()
         torch.cuda.nvtx.range_push("cb_step")
@@ -375,13 +391,15 @@ def main() -> None:
                    "batch_per_gpu": 1, "ctx": CTX, "weights": "nvfp4 (e2m1 + e4m3/16 + f32)",
                    "kv": "bf16", "indexer_keys": "e4m3", "l2": "flushed between timed steps (512 MB write)",
                    "parallelism": f"replicas x{world} (independent sequences)"},
-        "roofline": {"bound": "hbm", "kernel": f"gemv_nvfp4 weight stream ({n_mats} launches, M=1)",
-                     "achieved": wbytes / w_avg_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": wbytes / w_avg_s / 1e9 / peaks["hbm_gbs"], "traffic": None,
-                     "bytes": wbytes, "us": w_avg_s * 1e6, "peak_source": peaks["source"]},
-        "step_roofline": {"bound": "hbm", "bytes": step_total, "parts": sb,
-                          "achieved": step_total / (ms_step * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                          "frac": step_total / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"]},
+        "roofline": {"bound": "hbm", "kernel": "decode_mk_kernel<1> (one launch = one decode step)",
+                     "achieved": step_total / (ms_step * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": step_total / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                     "traffic": DECODE_MK_TRAFFIC, "bytes": step_total, "parts": sb, "us": ms_step * 1e3,
+                     "peak_source": peaks["source"]},
+        "weight_stream": {"bound": "hbm", "kernel": f"gemv_nvfp4 ({n_mats} launches, M=1, one CUDA graph)",
+                          "achieved": wbytes / w_avg_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                          "frac": wbytes / w_avg_s / 1e9 / peaks["hbm_gbs"], "bytes": wbytes,
+                          "us": w_avg_s * 1e6},
         "e2e": {"value": world * args.steps / (e2e_total * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": 4, "ms_per_step": e2e_total / args.steps},
         "gpu_launches": launches_per_step * args.steps,
