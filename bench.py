@@ -142,9 +142,10 @@ def fill_cache(cache, ctx: int, seed: int) -> None:
     cache.pos_host = [ctx - 1] * cache.batch
 
 
-def weight_stream_graph(eng):
-    """CUDA graph of one M=1 GEMV per projection matrix of the model (the
-    reference's "decode-step weight stream", configs[1])."""
+def weight_stream_graph(eng, M: int = 1, tensor_cores: bool = False):
+    """CUDA graph of one GEMV per projection matrix of the model (the
+    reference's "decode-step weight stream", configs[1]) for M token rows:
+    the CUDA-core GEMV (fp32 x), or the tcgen05 verify GEMM (bf16 x)."""
     import ctypes as C
 
     import torch
@@ -155,15 +156,21 @@ def weight_stream_graph(eng):
     mats = [m for m in eng.model._keep if isinstance(m, PackedMatrix)]
     dev = eng.device
     kmax = max(m.k for m in mats)
-    x = torch.randn(1, kmax, device=dev)
-    y = torch.empty(max(m.rows for m in mats), device=dev)
+    x = torch.randn(M, kmax, device=dev)
+    xb = x.to(torch.bfloat16).view(torch.int16).contiguous()
+    y = torch.empty(M, max(m.rows for m in mats), device=dev)
+    ldy = y.shape[1]
     structs = [m.struct() for m in mats]
     L = _lib.lib()
     side = torch.cuda.Stream(dev)
 
     def run(st):
         for s in structs:
-            _lib.check(L.cb_gemv_nvfp4(C.byref(s), x.data_ptr(), s.k, 1, y.data_ptr(), s.rows, s.rows, st), "gemv")
+            if tensor_cores:
+                _lib.check(L.cb_verify_gemm_nvfp4(C.byref(s), xb.data_ptr(), kmax, M, y.data_ptr(), ldy, s.rows,
+                                                  None, st), "verify_gemm")
+            else:
+                _lib.check(L.cb_gemv_nvfp4(C.byref(s), x.data_ptr(), kmax, M, y.data_ptr(), ldy, s.rows, st), "gemv")
 
     side.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(side):
@@ -372,6 +379,28 @@ def main() -> None:
         if i >= args.warmup:
             w_ms.append(a.elapsed_time(b))
 
+    # ------------------------------------------------ verify GEMM (M = 2, 4, 8)
+    verify = {}
+    for M in (2, 4, 8):
+        row = {}
+        for kind, tc in (("tcgen05", True), ("cuda_core", False)):
+            vg, _, vbytes = weight_stream_graph(eng, M=M, tensor_cores=tc)
+            v_ms = []
+            for i in range(args.warmup + max(args.steps // 5, 3)):
+                flush.random_(0, 255)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                vg.replay()
+                b.record(stream)
+                b.synchronize()
+                if i >= args.warmup:
+                    v_ms.append(a.elapsed_time(b))
+            us = statistics.mean(v_ms) * 1e3
+            row[kind] = {"us": us, "achieved_gbs": vbytes / (us * 1e-6) / 1e9,
+                         "frac": vbytes / (us * 1e-6) / 1e9 / _peaks()["hbm_gbs"]}
+            del vg
+        verify[str(M)] = row
+
     tot = torch.tensor([t_total_ms, e2e_total], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(tot, op=torch.distributed.ReduceOp.MAX)
@@ -400,6 +429,9 @@ def main() -> None:
                           "achieved": wbytes / w_avg_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                           "frac": wbytes / w_avg_s / 1e9 / peaks["hbm_gbs"], "bytes": wbytes,
                           "us": w_avg_s * 1e6},
+        "verify_gemm": {"bytes": wbytes, "unit": "GB/s", "note": f"{n_mats} projections per pass, L2 flushed, "
+                        "M token rows; tcgen05 = cb_verify_gemm_nvfp4 (bf16 x), cuda_core = cb_gemv_nvfp4",
+                        "by_M": verify},
         "e2e": {"value": world * args.steps / (e2e_total * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": 4, "ms_per_step": e2e_total / args.steps},
         "gpu_launches": launches_per_step * args.steps,

@@ -30,7 +30,7 @@ CB_NOALLOC_MAX_SCORES = 1 << 20
 EXPORTS = ("cb_abi_version", "cb_status_string", "cb_nvfp4_quantize", "cb_nvfp4_pack_tiles", "cb_gemv_nvfp4",
            "cb_embed", "cb_argmax", "cb_gdn_step", "cb_indexer_topk", "cb_workspace_bytes", "cb_forward",
            "cb_read_status", "cb_clear_status", "cb_launch_count", "cb_indexer_topk_noalloc", "cb_read_trace",
-           "cb_verify_gemm_nvfp4")
+           "cb_verify_gemm_nvfp4", "cb_gdn_chunk_prefill")
 
 P = C.c_void_p
 I32 = C.c_int32
@@ -100,6 +100,7 @@ def lib() -> C.CDLL:
         L.cb_nvfp4_pack_tiles.argtypes = [P, P, I32, I32, P, P]
         L.cb_gemv_nvfp4.argtypes = [C.POINTER(CbMatrix), P, I32, I32, P, I32, I32, P]
         L.cb_verify_gemm_nvfp4.argtypes = [C.POINTER(CbMatrix), P, I32, I32, P, I32, I32, P, P]
+        L.cb_gdn_chunk_prefill.argtypes = [P, P, P, P, P, I32, I32, I32, I32, I32, C.c_float, P, P, P]
         L.cb_embed.argtypes = [C.POINTER(CbMatrix), P, I32, P, P, P]
         L.cb_argmax.argtypes = [P, I32, I32, I32, P, P]
         L.cb_gdn_step.argtypes = [C.POINTER(CbModel), I32, P, I32, I32, I32, P, C.c_int64, P, C.c_int64, P, I32, P]

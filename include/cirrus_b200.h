@@ -15,6 +15,7 @@
  *   cb_nvfp4_pack_tiles   pack_nvfp4_mma / pack_nvfp4_v3  scripts/bench_spark.py:369-391, 639-660
  *   cb_gemv_nvfp4         nvfp4_gemv                     cirrus/perf/bench_kernels.cu:202-227
  *   cb_verify_gemm_nvfp4  nvfp4_gemv, M = 2..16 (verify)  cirrus/perf/bench_kernels.cu:202-227, 1079-1300
+ *   cb_gdn_chunk_prefill  chunk_gated_delta_rule (fla)    cirrus/model/layers.py:165-170 (recurrence :108-129)
  *                         (and every nn.Linear of the model, layers.py)
  *   cb_gdn_step           GatedDeltaNet.forward          cirrus/model/layers.py:151-174
  *   cb_indexer_topk       indexer_scores + topk_mask     cirrus/model/layers.py:282-309
@@ -185,6 +186,16 @@ int cb_argmax(const float* x, int32_t rows, int32_t n, int32_t ld, int32_t* out,
 int cb_gdn_step(const CbModel* m, int32_t layer, const float* proj, int32_t ldp, int32_t batch, int32_t T,
                 float* state, int64_t state_stride, float* conv, int64_t conv_stride, float* out, int32_t ldo,
                 void* stream);
+
+/* Chunked Gated DeltaNet recurrence for prefill (64-token chunks, Dk = Dv = 64),
+ * the exact recurrence of layers.py:108-129 evaluated chunk-wise:
+ * q, k [B][T][H][64] (q, k L2-normalised by the caller), v [B][T][H][64],
+ * g [B][T][H] (log decay, <= 0), beta [B][T][H]; state S [B][H][Dk][Dv] fp32 is
+ * read and replaced by the state after token T-1; out [B][T][H][Dv] = S_t^T (q_t scale).
+ * Replaces fla's chunk_gated_delta_rule at layers.py:165-170. */
+int cb_gdn_chunk_prefill(const float* q, const float* k, const float* v, const float* g, const float* beta, int32_t B,
+                         int32_t T, int32_t H, int32_t Dk, int32_t Dv, float scale, float* state, float* out,
+                         void* stream);
 
 /* -------------------------------------------------- indexer + top-k */
 /* For each of `rows` query rows: scores over keys 0..qpos[r] of sequence

@@ -56,6 +56,7 @@ def test_host_argument_checks_fail_without_launching(built_lib):
     assert built_lib.cb_forward(None, None, None, 0, None, 1, 1, None, None, None, None) == 1
     assert built_lib.cb_workspace_bytes(None, 1, 1, 1) == 0
     assert built_lib.cb_verify_gemm_nvfp4(None, None, 0, 1, None, 0, 0, None, None) == 1
+    assert built_lib.cb_gdn_chunk_prefill(None, None, None, None, None, 1, 1, 1, 64, 64, 1.0, None, None, None) == 1
 
 
 def test_ctypes_structs_match_c_layout(built_lib):
