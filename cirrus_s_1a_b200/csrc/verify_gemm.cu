@@ -5,10 +5,11 @@
 // (draft width 2-8) as nvfp4_gemv with M > 1 (cirrus/perf/bench_kernels.cu
 // :202-227, mma.sync f16 in its v4/v5 kernels).  Here one CTA owns a 128-row
 // tile of W:
-//   * W: each K chunk of 64 is dequantised by all 256 threads straight from
-//     the packed NVFP4 tiles (E2M1 code x E4M3 block scale is exact in bf16)
-//     into a shared-memory stage in the canonical K-major layout (8-row x
-//     16-byte core matrices, no swizzle); two stages alternate;
+//   * W: each K chunk of 64 (128 rows x 32 code bytes + 4 scale bytes) comes
+//     by cp.async into a ring of 6 raw stages, 5 chunks ahead; all 256 threads
+//     dequantise it (E2M1 code x E4M3 block scale is exact in bf16) into a
+//     shared-memory stage in the canonical K-major layout (8-row x 16-byte core
+//     matrices, no swizzle); two such stages alternate;
 //   * x: staged once as bf16, 16 rows (tokens; rows >= m_rows are zero);
 //   * one thread issues tcgen05.mma.kind::f16 (M 128, N 16, K 16) x 4 per
 //     chunk into an fp32 accumulator in tensor memory and commits to the
@@ -29,6 +30,8 @@ constexpr int kVgM = 128;        // W rows per CTA (MMA M)
 constexpr int kVgN = 16;         // token columns (MMA N)
 constexpr int kVgKc = 64;        // K per stage
 constexpr int kVgStageBytes = kVgM * kVgKc * 2;  // 16 KB
+constexpr int kVgRing = 6;                         // raw NVFP4 chunks in flight
+constexpr int kVgRawBytes = kVgM * (kVgKc / 2) + kVgM * (kVgKc / 16);  // 4 KB codes + 512 B scales
 constexpr unsigned long long kVgTimeoutNs = 200ull * 1000 * 1000;
 
 struct VerifyParams {
@@ -127,40 +130,53 @@ __global__ void __launch_bounds__(kVgThreads, 1) verify_gemm_kernel(const __grid
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = tmem_base;
 
-  // this thread's share of a chunk: row r of the tile, 32 K values (half h)
+  // this thread's share of a chunk: row r of the tile, 32 K values (half h).
+  // Raw chunks travel by cp.async into a ring of kVgRing stages, kVgRing - 1
+  // chunks ahead of the one being converted.
   const int r = tid >> 1, h = tid & 1, grow = row0 + r;
   const bool rvalid = grow < p.rows;
   const int64_t tb = 9ll * K;
   const uint8_t* codes = p.tiles + (int64_t)(grow >> 4) * tb + (grow & 15) * (K / 2) + 16 * h;
-  const uint8_t* sc = p.tiles + (int64_t)(grow >> 4) * tb + kTileRows * (K / 2) + (grow & 15) * (K / 16) + 2 * h;
-  uint4 cw = make_uint4(0u, 0u, 0u, 0u);
-  uint32_t s2 = 0;
-  if (rvalid) {
-    cw = __ldg(reinterpret_cast<const uint4*>(codes));
-    s2 = (uint32_t)__ldg(sc) | ((uint32_t)__ldg(sc + 1) << 8);
-  }
+  const uint8_t* sc = p.tiles + (int64_t)(grow >> 4) * tb + kTileRows * (K / 2) + (grow & 15) * (K / 16);
+  uint8_t* raw = B + (size_t)kVgN * K * 2;  // [kVgRing][codes 128 x 32 | scales 128 x 4]
+  auto issue = [&](int c) {
+    if (rvalid && c < nchunks) {
+      uint8_t* rs = raw + (c % kVgRing) * kVgRawBytes;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(rs + r * 32 + 16 * h)),
+                   "l"(codes + c * 32)
+                   : "memory");
+      if (h == 0)
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(rs + kVgM * 32 + r * 4)),
+                     "l"(sc + c * 4)
+                     : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  for (int j = 0; j < kVgRing - 1; ++j) issue(j);
   unsigned par[2] = {0u, 0u};
   bool ok = true;
   for (int c = 0; c < nchunks; ++c) {
     const int st = c & 1;
     uint8_t* As = A + st * kVgStageBytes;
-    // the MMA of chunk c - 2 read this stage: wait for its commit
+    issue(c + kVgRing - 1);  // its stage held chunk c - 1, converted before the last barrier
+    asm volatile("cp.async.wait_group %0;" ::"n"(kVgRing - 1) : "memory");
+    // the MMA of chunk c - 2 read this A stage: wait for its commit
+    if (c >= 2 && tid == 0 && !mbar_wait(smem_u32(bar_mma + st), par[st])) s_abort = 1;
+    __syncthreads();  // chunk c's raw bytes (all threads' copies) visible; abort flag
+    if (s_abort) {
+      ok = false;
+      break;
+    }
     if (c >= 2) {
-      if (tid == 0 && !mbar_wait(smem_u32(bar_mma + st), par[st])) s_abort = 1;
-      __syncthreads();
-      if (s_abort) {
-        ok = false;
-        break;
-      }
       mbar_wait(smem_u32(bar_mma + st), par[st]);  // completed: returns at once
       par[st] ^= 1u;
     }
-    // next chunk's codes in flight while this one is converted
-    uint4 cn = make_uint4(0u, 0u, 0u, 0u);
-    uint32_t sn = 0;
-    if (rvalid && c + 1 < nchunks) {
-      cn = __ldg(reinterpret_cast<const uint4*>(codes + (c + 1) * 32));
-      sn = (uint32_t)__ldg(sc + (c + 1) * 4) | ((uint32_t)__ldg(sc + (c + 1) * 4 + 1) << 8);
+    const uint8_t* rs = raw + (c % kVgRing) * kVgRawBytes;
+    uint4 cw = make_uint4(0u, 0u, 0u, 0u);
+    uint32_t s2 = 0;
+    if (rvalid) {
+      cw = *reinterpret_cast<const uint4*>(rs + r * 32 + 16 * h);
+      s2 = (uint32_t)rs[kVgM * 32 + r * 4 + 2 * h] | ((uint32_t)rs[kVgM * 32 + r * 4 + 2 * h + 1] << 8);
     }
     // 32 codes -> bf16 x E4M3 scale (exact), into k-blocks 4h .. 4h + 3 of row r
     const uint32_t w4[4] = {cw.x, cw.y, cw.z, cw.w};
@@ -180,8 +196,6 @@ __global__ void __launch_bounds__(kVgThreads, 1) verify_gemm_kernel(const __grid
       *reinterpret_cast<uint4*>(As + (r >> 3) * 1024 + (4 * h + j) * 128 + (r & 7) * 16) =
           make_uint4(o[0], o[1], o[2], o[3]);
     }
-    cw = cn;
-    s2 = sn;
     // generic-proxy stores -> visible to the tensor core's async proxy
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
@@ -203,6 +217,7 @@ __global__ void __launch_bounds__(kVgThreads, 1) verify_gemm_kernel(const __grid
                    : "memory");
     }
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");  // no copy outlives the CTA
   // the last commit covers every MMA issued before it
   if (ok && nchunks > 0) {
     const int st = (nchunks - 1) & 1;
@@ -243,7 +258,7 @@ __global__ void __launch_bounds__(kVgThreads, 1) verify_gemm_kernel(const __grid
 
 }  // namespace
 
-size_t verify_gemm_smem(int K) { return (size_t)2 * kVgStageBytes + (size_t)kVgN * K * 2; }
+size_t verify_gemm_smem(int K) { return (size_t)2 * kVgStageBytes + (size_t)kVgN * K * 2 + (size_t)kVgRing * kVgRawBytes; }
 
 }  // namespace cb
 
