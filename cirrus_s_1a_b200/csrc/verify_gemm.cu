@@ -15,7 +15,10 @@
 //     chunk into an fp32 accumulator in tensor memory and commits to the
 //     stage's mbarrier, which frees the stage for the chunk after next;
 //   * the epilogue reads the accumulator with tcgen05.ld (warp w owns rows
-//     32w .. 32w + 31) and applies the fp32 tile scale.
+//     32w .. 32w + 31) and applies the fp32 tile scale;
+//   * a tile with few rows per SM splits K over a cluster of up to 8 CTAs; the
+//     partials meet in distributed shared memory and cluster rank 0 adds them
+//     in rank order (deterministic, no atomics).
 // Every wait is bounded (%globaltimer); on timeout the launch sets its status
 // word and skips the remaining work, and still frees its tensor memory.
 #include <cuda_bf16.h>
@@ -104,7 +107,13 @@ __global__ void __launch_bounds__(kVgThreads, 1) verify_gemm_kernel(const __grid
   __shared__ uint32_t tmem_base;
   __shared__ int s_abort;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int K = p.K, nchunks = K / kVgKc, row0 = blockIdx.x * kVgM;
+  // split K over the CTAs of a cluster (csize 1 without clusters): this CTA owns
+  // chunks [cbeg, cbeg + nchunks) of its 128-row tile
+  uint32_t crank, csize;
+  asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
+  asm("mov.u32 %0, %%cluster_nctarank;" : "=r"(csize));
+  const int K = p.K, nall = K / kVgKc, row0 = (int)(blockIdx.x / csize) * kVgM;
+  const int cbeg = (int)crank * nall / (int)csize, nchunks = ((int)crank + 1) * nall / (int)csize - cbeg;
   uint8_t* A = vsm;                          // [2][16 row groups][8 k-blocks][8 rows][16 B]
   uint8_t* B = vsm + 2 * kVgStageBytes;      // [2 row groups][K/8 k-blocks][8 rows][16 B]
   const uint32_t sbo_b = (uint32_t)(K / 8) * 128u;
@@ -143,11 +152,11 @@ __global__ void __launch_bounds__(kVgThreads, 1) verify_gemm_kernel(const __grid
     if (rvalid && c < nchunks) {
       uint8_t* rs = raw + (c % kVgRing) * kVgRawBytes;
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(rs + r * 32 + 16 * h)),
-                   "l"(codes + c * 32)
+                   "l"(codes + (cbeg + c) * 32)
                    : "memory");
       if (h == 0)
         asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(rs + kVgM * 32 + r * 4)),
-                     "l"(sc + c * 4)
+                     "l"(sc + (cbeg + c) * 4)
                      : "memory");
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
@@ -204,7 +213,7 @@ __global__ void __launch_bounds__(kVgThreads, 1) verify_gemm_kernel(const __grid
 #pragma unroll
       for (int s = 0; s < kVgKc / 16; ++s) {
         const uint64_t da = vg_desc(smem_u32(As) + s * 256, 128, 1024);
-        const uint64_t db = vg_desc(smem_u32(B) + (c * (kVgKc / 8) + 2 * s) * 128, 128, sbo_b);
+        const uint64_t db = vg_desc(smem_u32(B) + ((cbeg + c) * (kVgKc / 8) + 2 * s) * 128, 128, sbo_b);
         const uint32_t acc = (c > 0 || s > 0) ? 1u : 0u;
         asm volatile(
             "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -233,8 +242,10 @@ __global__ void __launch_bounds__(kVgThreads, 1) verify_gemm_kernel(const __grid
     __syncthreads();
   }
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  uint32_t d[16];
+#pragma unroll
+  for (int t = 0; t < 16; ++t) d[t] = 0u;
   if (ok && warp < 4) {
-    uint32_t d[16];
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
         "%15}, [%16];"
@@ -242,13 +253,39 @@ __global__ void __launch_bounds__(kVgThreads, 1) verify_gemm_kernel(const __grid
           "=r"(d[8]), "=r"(d[9]), "=r"(d[10]), "=r"(d[11]), "=r"(d[12]), "=r"(d[13]), "=r"(d[14]), "=r"(d[15])
         : "r"(tmem + ((uint32_t)(warp * 32) << 16)));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-    const int row = row0 + warp * 32 + lane;
-    if (row < p.rows_out) {
+  }
+  const int row = row0 + warp * 32 + lane;
+  if (csize == 1) {
+    if (ok && warp < 4 && row < p.rows_out) {
       const float ts = p.tile_scale[row >> 4];
 #pragma unroll
       for (int t = 0; t < kVgN; ++t)
         if (t < p.m_rows) p.y[(int64_t)t * p.ldy + row] = __uint_as_float(d[t]) * ts;
     }
+  } else {
+    // split K: every CTA parks its partial in shared memory (the A stages are
+    // idle now); rank 0 adds the partials of ranks 0 .. csize-1 in that order
+    float* red = reinterpret_cast<float*>(A);  // [128][17]
+    if (warp < 4)
+#pragma unroll
+      for (int t = 0; t < kVgN; ++t) red[(warp * 32 + lane) * 17 + t] = __uint_as_float(d[t]);
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (crank == 0 && warp < 4 && row < p.rows_out) {
+      const float ts = p.tile_scale[row >> 4];
+      for (int t = 0; t < p.m_rows; ++t) {
+        float acc = 0.0f;
+        for (uint32_t rk = 0; rk < csize; ++rk) {
+          uint32_t ra;
+          float v;
+          asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(red + (warp * 32 + lane) * 17 + t)), "r"(rk));
+          asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+          acc += v;
+        }
+        p.y[(int64_t)t * p.ldy + row] = acc * ts;
+      }
+    }
+    // rank 0 has read every partial before any CTA of the cluster exits
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
   }
   if (!ok && tid == 0 && p.status) atomicCAS(p.status, 0, CB_ERR_TIMEOUT);
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -294,8 +331,26 @@ extern "C" int cb_verify_gemm_nvfp4(const CbMatrix* w, const uint16_t* x, int32_
   p.ldy = ldy;
   p.rows_out = rows_out;
   p.status = status;
-  const int grid = (rows_out + kVgM - 1) / kVgM;
-  verify_gemm_kernel<<<grid, kVgThreads, smem, (cudaStream_t)stream>>>(p);
+  // split K over a cluster of up to 8 CTAs while the grid stays within two CTAs per SM
+  const int tiles = (rows_out + kVgM - 1) / kVgM, nall = K / kVgKc;
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int S = 1;
+  while (S < 8 && tiles * S * 2 <= 2 * sms && S * 2 <= nall) S *= 2;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(tiles * S);
+  cfg.blockDim = dim3(kVgThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = S;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, verify_gemm_kernel, p);
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+  return e == cudaSuccess ? CB_OK : CB_ERR_CUDA;
 }

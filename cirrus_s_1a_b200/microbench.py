@@ -4,6 +4,12 @@ weights of one (N, K) shape, M token rows, L2 flushed before every launch.
 
     python -m cirrus_s_1a_b200.microbench --n 32000 --k 768 --m 8 --iters 20 [--gemv]
 
+With --gdn it times the chunked Gated DeltaNet prefill instead (one layer:
+--batch sequences x 12 heads x --tokens tokens, Dk = Dv = 64, the C2
+distributions of the reference benchmark):
+
+    python -m cirrus_s_1a_b200.microbench --gdn --batch 1 --tokens 4096
+
 Prints one JSON line: mean launch time (CUDA events) and achieved GB/s of the
 packed weight bytes.  The shapes of the reference's weight-stream benchmark are
 768x768, 4096x768 (gate_up), 768x2048 (down) and 32000x768 (LM head).
@@ -30,7 +36,13 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--gemv", action="store_true", help="time the CUDA-core GEMV instead")
+    ap.add_argument("--gdn", action="store_true", help="time the chunked Gated DeltaNet prefill instead")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--tokens", type=int, default=4096)
     args = ap.parse_args()
+    if args.gdn:
+        gdn(args)
+        return
     dev = torch.device("cuda:0")
     g = torch.Generator().manual_seed(0)
     pm = PackedMatrix([torch.randn(args.n, args.k, generator=g) * 0.02], dev)
@@ -64,6 +76,39 @@ def main() -> None:
     print(json.dumps({"kernel": "gemv_nvfp4" if args.gemv else "verify_gemm (tcgen05)", "n": args.n, "k": args.k,
                       "m": args.m, "us": us, "bytes": pm.real_bytes, "gbs": pm.real_bytes / (us * 1e-6) / 1e9,
                       "flops": 2 * args.m * args.n * args.k}))
+
+
+def gdn(args) -> None:
+    dev = torch.device("cuda:0")
+    g = torch.Generator().manual_seed(0)
+    B, T, H, D = args.batch, args.tokens, 12, 64
+    q = torch.nn.functional.normalize(torch.randn(B, T, H, D, generator=g), dim=-1).to(dev)
+    k = torch.nn.functional.normalize(torch.randn(B, T, H, D, generator=g), dim=-1).to(dev)
+    v = torch.randn(B, T, H, D, generator=g).to(dev)
+    gl = torch.sigmoid(torch.randn(B, T, H, generator=g) + 3.0).log().to(dev)
+    beta = torch.sigmoid(torch.randn(B, T, H, generator=g)).to(dev)
+    S0 = (torch.randn(B, H, D, D, generator=g) * 0.1).to(dev)
+    S = torch.empty_like(S0)
+    out = torch.empty(B, T, H, D, device=dev)
+    L = _lib.lib()
+    st = torch.cuda.current_stream(dev).cuda_stream
+    times = []
+    for i in range(args.warmup + args.iters):
+        S.copy_(S0)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        _lib.check(L.cb_gdn_chunk_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), gl.data_ptr(), beta.data_ptr(),
+                                          B, T, H, D, D, C.c_float(D ** -0.5), S.data_ptr(), out.data_ptr(), st),
+                   "cb_gdn_chunk_prefill")
+        b.record()
+        b.synchronize()
+        if i >= args.warmup:
+            times.append(a.elapsed_time(b) * 1e3)
+    us = statistics.mean(times)
+    # per chunk and head: 6 products of 64^3 and the 64^2 x 64 solve, 2 flops per FMA
+    flops = 2.0 * B * H * ((T + 63) // 64) * (6 * 64 ** 3 + 64 ** 3)
+    print(json.dumps({"kernel": "gdn_chunk_prefill", "batch": B, "tokens": T, "heads": H, "us": us,
+                      "tokens_per_s": B * T / (us * 1e-6), "gflops": flops / (us * 1e-6) / 1e9}))
 
 
 if __name__ == "__main__":
