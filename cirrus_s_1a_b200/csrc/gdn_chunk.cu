@@ -17,7 +17,8 @@
 //
 // One CTA per (sequence, head) walks the chunks in order with S in shared
 // memory; every 64 x 64 x 64 product is fp32, 4 x 4 outputs per thread.  The
-// triangular solve runs one thread per right-hand-side column.
+// triangular solve goes in 16-row blocks: a parallel update from the finished
+// blocks, then one thread per right-hand-side column inside the block.
 #include "common.cuh"
 
 namespace cb {
@@ -120,20 +121,31 @@ __global__ void __launch_bounds__(kGThreads, 1) gdn_chunk_kernel(const __grid_co
         }
     }
     __syncthreads();
-    // forward substitution, one thread per column: U (rhs beta v), W (rhs beta e^G k)
-    if (tid < 2 * kGd) {
-      const bool isu = tid < kGd;
-      const int c = isu ? tid : tid - kGd;
-      float* X = isu ? U : W;
-      const float* R = isu ? Vc : Kc;
-      for (int t = 0; t < kGc; ++t) {
-        float s = 0.0f;
-        for (int i = 0; i < t; ++i) s = fmaf(A[t * kGp + i], X[i * kGp + c], s);
-        const float rhs = isu ? R[t * kGp + c] : expf(Gs[t]) * R[t * kGp + c];
-        X[t * kGp + c] = bs[t] * (rhs - s);
+    // forward substitution X_t = beta_t (R_t - sum_{i<t} A[t][i] X_i) for U (R = V) and
+    // W (R = e^G K), in 4 row blocks of 16: all threads subtract the finished
+    // blocks, then one thread per column finishes the block's rows in order
+    for (int blk = 0; blk < kGc / 16; ++blk) {
+      const int tb0 = 16 * blk;
+      for (int e = tid; e < 16 * 2 * kGd; e += kGThreads) {
+        const int t = tb0 + (e >> 7), col = e & 127, c = col & (kGd - 1);
+        const bool isu = col < kGd;
+        float* X = isu ? U : W;
+        float y = isu ? Vc[t * kGp + c] : expf(Gs[t]) * Kc[t * kGp + c];
+        for (int i = 0; i < tb0; ++i) y = fmaf(-A[t * kGp + i], X[i * kGp + c], y);
+        X[t * kGp + c] = y;
       }
+      __syncthreads();
+      if (tid < 2 * kGd) {
+        const int c = tid & (kGd - 1);
+        float* X = tid < kGd ? U : W;
+        for (int t = tb0; t < tb0 + 16; ++t) {
+          float y = X[t * kGp + c];
+          for (int i = tb0; i < t; ++i) y = fmaf(-A[t * kGp + i], X[i * kGp + c], y);
+          X[t * kGp + c] = bs[t] * y;
+        }
+      }
+      __syncthreads();
     }
-    __syncthreads();
     // D = U - W S0 (into U), and O = diag(e^G) Q~ S0 + P D
     float o[4][4] = {};
     {
