@@ -17,9 +17,10 @@
 //   cross layer: q|gate GEMV -> selected-key attention (split partials)
 //                -> o-proj (merging the partials) -> gate_up -> down
 //   head:        LM-head GEMV (final norm fused) with a per-row argmax
-// At start every CTA issues L2 prefetches for its share of all weights and of
-// the recurrent / window state the step will read, so HBM streams at full
-// rate while the phases walk the dependency chain.  Every wait is bounded
+// Each GEMV's first weight rows are copied to shared memory between the
+// arrival at the barrier before it and the wait there; there is no separate
+// L2 prefetch (measured: it costs more in issue and queueing than it saves).
+// Every wait is bounded
 // (%globaltimer); on timeout the launch sets CB_ERR_TIMEOUT and all CTAs exit.
 #include <algorithm>
 
@@ -113,82 +114,6 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
-
-// -------------------------------------------------------------- prefetch
-__device__ __forceinline__ void prefetch_line(const void* p) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
-}
-
-// [p, p + bytes) in 128-byte lines spread over every thread of the grid.
-__device__ void prefetch_share(const void* p, size_t bytes) {
-  if (p == nullptr || bytes == 0) return;
-  const uintptr_t b = reinterpret_cast<uintptr_t>(p) & ~(uintptr_t)127;
-  const uintptr_t e = reinterpret_cast<uintptr_t>(p) + bytes;
-  const size_t lines = (e - b + 127) / 128;
-  const size_t stride = (size_t)gridDim.x * blockDim.x;
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < lines; i += stride) {
-    const uintptr_t addr = b + i * 128;
-    prefetch_line(reinterpret_cast<const void*>(addr < reinterpret_cast<uintptr_t>(p) ? reinterpret_cast<uintptr_t>(p) : addr));
-  }
-}
-
-__device__ __forceinline__ size_t matrix_bytes(const CbMatrix& W) { return (size_t)(W.rows / kTileRows) * tile_bytes(W.k); }
-
-// Paced L2 prefetch.  The step is a sequence of prefetch units: the self
-// layers (weights + that layer's recurrent / window state), the shared-KV
-// unit (projection + indexer keys), the cross layers and the LM head.  Unit u
-// is prefetched when unit u - 2 starts, so about two layers are in flight and
-// the prefetched lines are not evicted before use.  Every thread of the grid
-// issues L2 prefetches for its share of each region's 128-byte lines.
-__device__ void prefetch_unit(const MkArgs& a, int u) {
-  const CbModel& m = a.m;
-  const CbCache& c = a.c;
-  const int H = m.gdn_heads, C = 2 * H * m.gdn_dk + H * m.gdn_dv;
-  auto take = [&](const void* p, size_t bytes) { prefetch_share(p, bytes); };
-  if (u < 0) return;
-  if (u < m.n_self_layers) {
-    const CbSelfLayer& L = m.self_layers[u];
-    take(L.in_proj.tiles, matrix_bytes(L.in_proj));
-    for (int b = 0; b < a.B; ++b) {
-      if (L.kind == CB_LAYER_GDN) {
-        const int64_t slot = (int64_t)b * c.n_gdn + L.slot;
-        take(c.gdn_state + slot * H * m.gdn_dk * m.gdn_dv, sizeof(float) * H * m.gdn_dk * m.gdn_dv);
-        take(c.gdn_conv + slot * (m.conv_size - 1) * C, sizeof(float) * (m.conv_size - 1) * C);
-      } else {
-        const int64_t ring = (int64_t)(b * c.n_swa + L.slot) * c.swa_slots * m.n_kv_heads * m.head_dim;
-        const size_t bytes = sizeof(uint16_t) * (size_t)c.swa_slots * m.n_kv_heads * m.head_dim;
-        take(c.swa_k + ring, bytes);
-        take(c.swa_v + ring, bytes);
-      }
-    }
-    take(L.o_proj.tiles, matrix_bytes(L.o_proj));
-    take(L.gate_up.tiles, matrix_bytes(L.gate_up));
-    take(L.down.tiles, matrix_bytes(L.down));
-    return;
-  }
-  u -= m.n_self_layers;
-  if (u == 0) {
-    take(m.shared_proj.tiles, matrix_bytes(m.shared_proj));
-    if (m.sparse_topk > 0)
-      for (int b = 0; b < a.B; ++b) {
-        const int p0 = min(max(c.pos[b] + a.c0, 0), c.max_ctx);
-        take(c.kv_ik + (int64_t)b * c.max_ctx * m.indexer_dim, (size_t)p0 * m.indexer_dim);
-      }
-    return;
-  }
-  u -= 1;
-  if (u < m.n_cross_layers) {
-    const CbCrossLayer& L = m.cross_layers[u];
-    take(L.q_gate.tiles, matrix_bytes(L.q_gate));
-    take(L.o_proj.tiles, matrix_bytes(L.o_proj));
-    take(L.gate_up.tiles, matrix_bytes(L.gate_up));
-    take(L.down.tiles, matrix_bytes(L.down));
-    return;
-  }
-  if (u == m.n_cross_layers) take(m.lm_head.tiles, matrix_bytes(m.lm_head));
-}
-
-constexpr int kPrefetchAhead = 2;
 
 // ------------------------------------------------------------------ GEMV
 struct GemvJob {
@@ -1294,7 +1219,9 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
   const bool sparse = m.sparse_topk > 0;
 
   if (cta == 0) {
-    for (int i = tid; i < RQ * kMkHistBins; i += kT) a.hist[i] = 0u;
+    // the histogram exists only with a top-k (dense cross attention carves it empty)
+    if (sparse)
+      for (int i = tid; i < RQ * kMkHistBins; i += kT) a.hist[i] = 0u;
     for (int i = tid; i < RQ; i += kT) {
       a.hi_cnt[i] = 0;
       a.cand_cnt[i] = 0;
@@ -1302,7 +1229,6 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     }
   }
   if (cta == 0 && tid == 0) a.trace[0] = gtimer();
-  for (int u = 0; u < kPrefetchAhead; ++u) prefetch_unit(a, u);
   // Each GEMV's first weights (and residual) are loaded between the arrival at
   // the barrier before it and the wait there (GemvPre): they do not depend on
   // the previous phase, so their latency hides behind the barrier.
@@ -1310,7 +1236,6 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
 
   for (int i = 0; i < m.n_self_layers; ++i) {
     const CbSelfLayer& L = m.self_layers[i];
-    prefetch_unit(a, i + kPrefetchAhead);
     GemvJob in{};
     in.W = L.in_proj;
     in.x = a.h;
@@ -1402,7 +1327,6 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     grid_arrive(a, gen);
   }
 
-  prefetch_unit(a, m.n_self_layers + kPrefetchAhead);
   {
     GemvJob sh{};
     sh.W = m.shared_proj;
@@ -1434,7 +1358,6 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
 
   for (int j = 0; j < m.n_cross_layers; ++j) {
     const CbCrossLayer& L = m.cross_layers[j];
-    prefetch_unit(a, m.n_self_layers + 1 + j + kPrefetchAhead);
     GemvJob q{};
     q.W = L.q_gate;
     q.x = j == 0 ? a.h : a.xc;
