@@ -23,6 +23,9 @@ One JSON line on rank 0:
                read + write of one launch from an ncu capture of this workload
   weight_stream  the NVFP4 weight stream alone (every projection of a step,
                M = 1, as separate GEMV launches in one CUDA graph)
+  verify_gemm  the weight stream at M = 2, 4, 8 token rows through the tcgen05
+               verify GEMM and the CUDA-core GEMV
+  batched      step time of B sequences x T tokens (B = 8, 64; T = 1, 5)
   cpu_baseline the oracle restatement of the reference forward on the host
                cores (rank 0, N = 1, a bounded number of 32K-context steps)
 
@@ -50,7 +53,7 @@ METRIC = "decode tok/s (batch 1, τ=1, 32K ctx) per B200 + HBM GB/s vs 8 TB/s; b
 # DRAM bytes (read + write) of one decode_mk_kernel<1> launch at this workload,
 # from `ncu --set full` (dram__bytes_read.sum + dram__bytes_write.sum); see
 # profiles/decode_mk_kernel_step_32k.md for the command
-DECODE_MK_TRAFFIC = 95_655_424 + 4_238_080
+DECODE_MK_TRAFFIC = 95_577_856 + 3_637_504
 PUBLISHED_TOK_S = 1815.0  # reference: decode tok/s at 32K, tau=1 (GB10, measured stream + roofline remainder)
 CTX = 32768
 FLUSH_BYTES = 512 << 20
@@ -401,6 +404,30 @@ def main() -> None:
             del vg
         verify[str(M)] = row
 
+    # ------------------------------------------------ batched steps (B sequences x T tokens)
+    batched = []
+    del graph
+    for Bb, Tb in ((8, 1), (1, 5), (64, 1), (64, 5)):
+        bcache = eng.new_cache(Bb)
+        fill_cache(bcache, CTX, 1)
+        bg = DecodeGraph(eng, bcache, T=Tb, n_logits=Tb, want_logits=False)
+        b_ms = []
+        for i in range(args.warmup + 3):
+            bcache.pos_dev.fill_(CTX - 1)
+            flush.random_(0, 255)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            bg.replay()
+            b.record(stream)
+            b.synchronize()
+            if i >= args.warmup:
+                b_ms.append(a.elapsed_time(b))
+        ms_b = statistics.mean(b_ms)
+        batched.append({"batch": Bb, "T": Tb, "ms_per_step": ms_b, "tokens_per_s": Bb * Tb / (ms_b * 1e-3),
+                        "path": "persistent" if Bb * Tb <= 8 else "one launch per op"})
+        del bg, bcache
+        torch.cuda.empty_cache()
+
     tot = torch.tensor([t_total_ms, e2e_total], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(tot, op=torch.distributed.ReduceOp.MAX)
@@ -432,6 +459,8 @@ def main() -> None:
         "verify_gemm": {"bytes": wbytes, "unit": "GB/s", "note": f"{n_mats} projections per pass, L2 flushed, "
                         "M token rows; tcgen05 = cb_verify_gemm_nvfp4 (bf16 x), cuda_core = cb_gemv_nvfp4",
                         "by_M": verify},
+        "batched": {"note": "per GPU, ctx 32768, L2 flushed, T tokens per sequence per step (T=5: a verify "
+                               "of 1 + 4 draft tokens), device-timed CUDA-graph replay", "steps": batched},
         "e2e": {"value": world * args.steps / (e2e_total * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": 4, "ms_per_step": e2e_total / args.steps},
         "gpu_launches": launches_per_step * args.steps,
@@ -442,7 +471,7 @@ def main() -> None:
         line["cpu_baseline"] = cpu_baseline(cfg, sd, cache, CTX, args.cpu_budget_s, 50)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del graph, wgraph
+    del wgraph
     if world > 1:
         torch.distributed.destroy_process_group()
 
