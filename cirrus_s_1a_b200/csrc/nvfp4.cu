@@ -212,15 +212,19 @@ static int launch_gemv_m(const GemvParams& p, cudaStream_t st) {
 template <int PRE, int EPI>
 static int launch_gemv_pe(GemvParams p, cudaStream_t st) {
   int rc = CB_OK;
-  for (int m0 = 0; m0 < p.m_rows && rc == CB_OK; m0 += 8) {
+  // up to 16 rows per launch (the input rows are staged in shared memory:
+  // 16 x K floats, 128 KB at K = 2048), so a batch reads each matrix M / 16 times
+  const int step = p.K <= 2048 ? 16 : 8;
+  for (int m0 = 0; m0 < p.m_rows && rc == CB_OK; m0 += step) {
     GemvParams q = p;
-    q.m_rows = std::min(8, p.m_rows - m0);
+    q.m_rows = std::min(step, p.m_rows - m0);
     q.x = p.x + (int64_t)m0 * p.ldx;
     q.y = p.y + (int64_t)m0 * p.ldy;
     if (q.m_rows == 1) rc = launch_gemv_m<1, PRE, EPI>(q, st);
     else if (q.m_rows == 2) rc = launch_gemv_m<2, PRE, EPI>(q, st);
     else if (q.m_rows <= 4) rc = launch_gemv_m<4, PRE, EPI>(q, st);
-    else rc = launch_gemv_m<8, PRE, EPI>(q, st);
+    else if (q.m_rows <= 8) rc = launch_gemv_m<8, PRE, EPI>(q, st);
+    else rc = launch_gemv_m<16, PRE, EPI>(q, st);
   }
   return rc;
 }
