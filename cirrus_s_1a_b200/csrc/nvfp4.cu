@@ -86,16 +86,55 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_nvfp4_kernel(GemvParams p) 
     }
     __syncthreads();
   }
-  for (int i = threadIdx.x; i < M * K; i += kGemvThreads) {
-    const int m = i / K, k = i - m * K;
-    float v = 0.0f;
-    if (m < p.m_rows) {
-      const float* xr = p.x + (int64_t)m * p.ldx;
-      if (PRE == PRE_RMSNORM) v = xr[k] * rs[m] * p.norm_w[k];
-      else if (PRE == PRE_SWIGLU) v = silu(xr[k]) * xr[K + k];
-      else v = xr[k];
+  // Stage the inputs: 16-byte vectors, four in flight per thread (a loop of
+  // single loads would wait out one memory latency per element it stages).
+  const bool vec = ((reinterpret_cast<uintptr_t>(p.x) | (uintptr_t)p.ldx * 4u) & 15u) == 0 &&
+                   (PRE != PRE_RMSNORM || (reinterpret_cast<uintptr_t>(p.norm_w) & 15u) == 0);
+  if (vec) {
+    const int K4 = K >> 2, n4 = M * K4;
+    for (int i0 = threadIdx.x; i0 < n4; i0 += 4 * kGemvThreads) {
+      float4 xa[4], xb[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = i0 + j * kGemvThreads, m = i / K4, k4 = i - m * K4;
+        xa[j] = xb[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (i < n4 && m < p.m_rows) {
+          const float4* xr = reinterpret_cast<const float4*>(p.x + (int64_t)m * p.ldx);
+          xa[j] = xr[k4];
+          if (PRE == PRE_SWIGLU) xb[j] = xr[K4 + k4];
+          else if (PRE == PRE_RMSNORM) xb[j] = reinterpret_cast<const float4*>(p.norm_w)[k4];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = i0 + j * kGemvThreads, m = i / K4;
+        if (i < n4) {
+          float4 v = xa[j];
+          if (m < p.m_rows) {
+            const float4 a = xa[j], b = xb[j];
+            if (PRE == PRE_RMSNORM) {
+              const float r = rs[m];
+              v = make_float4(a.x * r * b.x, a.y * r * b.y, a.z * r * b.z, a.w * r * b.w);
+            } else if (PRE == PRE_SWIGLU) {
+              v = make_float4(silu(a.x) * b.x, silu(a.y) * b.y, silu(a.z) * b.z, silu(a.w) * b.w);
+            }
+          }
+          reinterpret_cast<float4*>(xs)[i] = v;
+        }
+      }
     }
-    xs[i] = v;
+  } else {
+    for (int i = threadIdx.x; i < M * K; i += kGemvThreads) {
+      const int m = i / K, k = i - m * K;
+      float v = 0.0f;
+      if (m < p.m_rows) {
+        const float* xr = p.x + (int64_t)m * p.ldx;
+        if (PRE == PRE_RMSNORM) v = xr[k] * rs[m] * p.norm_w[k];
+        else if (PRE == PRE_SWIGLU) v = silu(xr[k]) * xr[K + k];
+        else v = xr[k];
+      }
+      xs[i] = v;
+    }
   }
   __syncthreads();
 
