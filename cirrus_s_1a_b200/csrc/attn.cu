@@ -103,11 +103,35 @@ __global__ void __launch_bounds__(kSwaThreads) swa_attn_kernel(SwaParams p) {
   }
   const uint16_t* kr = p.kring + (int64_t)b * p.seq_stride;
   const uint16_t* vr = p.vring + (int64_t)b * p.seq_stride;
-  for (int i = tid; i < n * hd; i += kSwaThreads) {
-    const int key = i / hd, d = i - key * hd;
-    const int64_t off = ((int64_t)((ks + key) % p.slots) * p.Hkv + g) * hd + d;
-    Ks[key * (hd + 1) + d] = bf16_to_f32(kr[off]);
-    Vs[key * hd + d] = bf16_to_f32(vr[off]);
+  // the split's K/V rows: 16-byte vectors, four of each in flight per thread
+  const int vpk = hd / 8, nv = n * vpk;
+  for (int i0 = tid; i0 < nv; i0 += 4 * kSwaThreads) {
+    uint4 kq[4], vq[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = i0 + j * kSwaThreads;
+      if (i < nv) {
+        const int key = i / vpk, e8 = (i - key * vpk) * 8;
+        const int64_t off = ((int64_t)((ks + key) % p.slots) * p.Hkv + g) * hd + e8;
+        kq[j] = *reinterpret_cast<const uint4*>(kr + off);
+        vq[j] = *reinterpret_cast<const uint4*>(vr + off);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = i0 + j * kSwaThreads;
+      if (i < nv) {
+        const int key = i / vpk, e8 = (i - key * vpk) * 8;
+        const uint32_t kw[4] = {kq[j].x, kq[j].y, kq[j].z, kq[j].w}, vw[4] = {vq[j].x, vq[j].y, vq[j].z, vq[j].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          Ks[key * (hd + 1) + e8 + 2 * e] = bf16_to_f32(kw[e]);
+          Ks[key * (hd + 1) + e8 + 2 * e + 1] = bf16_to_f32(kw[e] >> 16);
+          Vs[key * hd + e8 + 2 * e] = bf16_to_f32(vw[e]);
+          Vs[key * hd + e8 + 2 * e + 1] = bf16_to_f32(vw[e] >> 16);
+        }
+      }
+    }
   }
   __syncthreads();
 
@@ -182,7 +206,7 @@ __global__ void swa_combine_kernel(SwaParams p) {
 }
 
 int launch_swa(const SwaParams& p, int batch, cudaStream_t st) {
-  if (p.hd > kSwaThreads || kSwaThreads % p.hd || p.split_len != kSwaSplit) return CB_ERR_SHAPE;
+  if (p.hd > kSwaThreads || kSwaThreads % p.hd || p.hd % 8 || p.split_len != kSwaSplit) return CB_ERR_SHAPE;
   const size_t smem = sizeof(float) * ((size_t)p.split_len * (2 * p.hd + 1) + p.hd + p.split_len + kSwaThreads);
   static bool set = false;
   if (!set) {
@@ -211,6 +235,9 @@ __global__ void __launch_bounds__(kCrossThreads) cross_attn_kernel(CrossParams p
   extern __shared__ __align__(16) float sm[];
   float* qs = sm;                          // [G][hd]
   float* es = qs + G * hd;                 // [G][kCrossChunk]
+  const int kvld = hd + 8;                 // bf16 row stride of the staged rows (16-byte vector reads spread over banks)
+  uint16_t* Kc = reinterpret_cast<uint16_t*>(es + G * kCrossChunk);  // [kCrossChunk][kvld]
+  uint16_t* Vc = Kc + kCrossChunk * kvld;                             // [kCrossChunk][kvld]
   __shared__ int keys[kCrossChunk];
   __shared__ float red[33];
   __shared__ float mrun[kCrossMaxG], lrun[kCrossMaxG], corr[kCrossMaxG];
@@ -247,9 +274,34 @@ __global__ void __launch_bounds__(kCrossThreads) cross_attn_kernel(CrossParams p
     const int cn = min(kCrossChunk, n - c);
     if (tid < cn) keys[tid] = dense ? c + tid : p.sel_idx[(int64_t)r * p.sel_ld + c + tid];
     __syncthreads();
+    // the chunk's K/V rows into shared memory: 16-byte vectors, four of each in flight per thread
+    const int vpk = hd / 8, nv = cn * vpk;
+    for (int i0 = tid; i0 < nv; i0 += 4 * kCrossThreads) {
+      uint4 kq[4], vq[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = i0 + j * kCrossThreads;
+        if (i < nv) {
+          const int key = i / vpk, e8 = (i - key * vpk) * 8;
+          const int64_t src = ((int64_t)keys[key] * p.Hkv + g) * hd + e8;
+          kq[j] = *reinterpret_cast<const uint4*>(kb + src);
+          vq[j] = *reinterpret_cast<const uint4*>(vb + src);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = i0 + j * kCrossThreads;
+        if (i < nv) {
+          const int key = i / vpk, e8 = (i - key * vpk) * 8;
+          *reinterpret_cast<uint4*>(Kc + key * kvld + e8) = kq[j];
+          *reinterpret_cast<uint4*>(Vc + key * kvld + e8) = vq[j];
+        }
+      }
+    }
+    __syncthreads();
     // scores for this chunk
     for (int i = tid; i < cn; i += kCrossThreads) {
-      const uint16_t* kr = kb + ((int64_t)keys[i] * p.Hkv + g) * hd;
+      const uint16_t* kr = Kc + i * kvld;
       float acc[kCrossMaxG];
 #pragma unroll
       for (int j = 0; j < kCrossMaxG; ++j) acc[j] = 0.0f;
@@ -294,7 +346,7 @@ __global__ void __launch_bounds__(kCrossThreads) cross_attn_kernel(CrossParams p
         const int j = idx / hd, d = idx - j * hd;
         float acc = o_acc[q2] * corr[j];
         const float* ej = es + j * kCrossChunk;
-        for (int i = 0; i < cn; ++i) acc = fmaf(ej[i], bf16_to_f32(vb[((int64_t)keys[i] * p.Hkv + g) * hd + d]), acc);
+        for (int i = 0; i < cn; ++i) acc = fmaf(ej[i], bf16_to_f32(Vc[i * kvld + d]), acc);
         o_acc[q2] = acc;
       }
     }
@@ -315,7 +367,14 @@ __global__ void __launch_bounds__(kCrossThreads) cross_attn_kernel(CrossParams p
 int launch_cross(const CrossParams& p, int rows, cudaStream_t st) {
   const int G = p.Hq / p.Hkv;
   if (G > kCrossMaxG || G * p.hd > 2 * kCrossThreads || p.hd % 8) return CB_ERR_SHAPE;
-  const size_t smem = sizeof(float) * ((size_t)G * p.hd + (size_t)G * kCrossChunk);
+  const size_t smem = sizeof(float) * ((size_t)G * p.hd + (size_t)G * kCrossChunk) +
+                      sizeof(uint16_t) * 2 * kCrossChunk * (size_t)(p.hd + 8);
+  if (smem > 200 * 1024) return CB_ERR_SHAPE;
+  static bool set = false;
+  if (!set) {
+    cudaFuncSetAttribute(cross_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    set = true;
+  }
   cross_attn_kernel<<<dim3(p.Hkv, rows), kCrossThreads, smem, st>>>(p);
   count_launch();
   return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
