@@ -265,6 +265,31 @@ def run_reference(args, rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+def profile_step(B: int, T: int) -> None:
+    """Two eager steps of B sequences x T tokens at ctx 32K (the batched
+    workload), each inside an NVTX range 'step' (`ncu --nvtx --nvtx-include
+    "step/"` lists only their launches)."""
+    import torch
+
+    from cirrus_s_1a_b200 import synthetic
+    from cirrus_s_1a_b200.config import baseline_config
+    from cirrus_s_1a_b200.engine import CirrusB200
+
+    cfg = baseline_config()
+    eng = CirrusB200(cfg, synthetic.random_state_dict(cfg, seed=0), device="cuda:0", max_ctx=CTX + 64)
+    cache = eng.new_cache(B)
+    fill_cache(cache, CTX, 1)
+    ids = torch.randint(0, cfg.vocab_size, (B, T), device="cuda:0")
+    for _ in range(2):
+        cache.pos_dev.fill_(CTX - 1)
+        cache.pos_host = [CTX - 1] * B
+        torch.cuda.nvtx.range_push("step")
+        eng(ids, cache=cache, n_logits=1)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+    print(json.dumps({"profile_step": {"batch": B, "T": T, "ctx": CTX}}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -273,9 +298,15 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--cpu-budget-s", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-step", metavar="BxT", default=None,
+                    help="run two eager batched steps (B sequences x T tokens) inside NVTX ranges named 'step' "
+                         "for a profiler's launch list, then exit")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.profile_step:
+        profile_step(*(int(v) for v in args.profile_step.lower().split("x")))
+        return
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
