@@ -67,6 +67,19 @@ __global__ void pack_tiles_kernel(const uint8_t* __restrict__ codes, const uint8
 constexpr int kGemvThreads = 256;
 constexpr int kGemvUnroll = 4;
 
+template <int EPI>
+__device__ __forceinline__ void gemv_store(const GemvParams& p, int m, int r0, float a0, float a1) {
+  float* yr = p.y + (int64_t)m * p.ldy;
+  if (r0 < p.rows_out) {
+    if (EPI == EPI_ADD) yr[r0] += a0;
+    else yr[r0] = a0;
+  }
+  if (r0 + 1 < p.rows_out) {
+    if (EPI == EPI_ADD) yr[r0 + 1] += a1;
+    else yr[r0 + 1] = a1;
+  }
+}
+
 template <int M, int PRE, int EPI>
 __global__ void __launch_bounds__(kGemvThreads) gemv_nvfp4_kernel(GemvParams p) {
   extern __shared__ __align__(16) float xs[];  // [M][K]
@@ -140,8 +153,16 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_nvfp4_kernel(GemvParams p) 
 
   const int kc = K >> 3;
   const int64_t tb = tile_bytes(K);
-  const int nwarps = gridDim.x * (kGemvThreads / 32);
-  for (int r0 = (blockIdx.x * (kGemvThreads / 32) + warp) * 2; r0 < p.rows; r0 += nwarps * 2) {
+  // S warps share a row pair, each over kc / S of the 8-code chunks; their
+  // partial sums meet in shared memory and are added in part order.
+  const int S = M >= 4 && p.ksplit > 1 ? p.ksplit : 1;  // 1 and 2 row launches compile without the split
+  const int ppc = (kGemvThreads / 32) / S;  // row pairs per CTA pass
+  const int slot = warp % ppc, part = warp / ppc;
+  const int c_lo = part * (kc / S), c_hi = c_lo + kc / S;
+  __shared__ float red[kGemvThreads / 32][2][M];
+  // rows % (2 * ppc) == 0, so every pair of a pass exists and the pass count is CTA-uniform
+  for (int base = blockIdx.x * ppc * 2; base < p.rows; base += gridDim.x * ppc * 2) {
+    const int r0 = base + slot * 2;
     const uint8_t* tile = p.tiles + (int64_t)(r0 >> 4) * tb;
     const int rr = r0 & 15;
     const uint32_t* cw0 = reinterpret_cast<const uint32_t*>(tile + rr * (K / 2));
@@ -152,12 +173,12 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_nvfp4_kernel(GemvParams p) 
 #pragma unroll
     for (int m = 0; m < M; ++m) acc0[m] = acc1[m] = 0.0f;
 
-    for (int cbase = 0; cbase < kc; cbase += 32 * kGemvUnroll) {
+    for (int cbase = c_lo; cbase < c_hi; cbase += 32 * kGemvUnroll) {
       uint32_t w0[kGemvUnroll], w1[kGemvUnroll], s0[kGemvUnroll], s1[kGemvUnroll];
 #pragma unroll
       for (int u = 0; u < kGemvUnroll; ++u) {
         const int c = cbase + u * 32 + lane;
-        const bool ok = c < kc;
+        const bool ok = c < c_hi;
         w0[u] = ok ? __ldg(cw0 + c) : 0u;
         w1[u] = ok ? __ldg(cw1 + c) : 0u;
         s0[u] = ok ? __ldg(sb0 + (c >> 1)) : 0u;
@@ -166,7 +187,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_nvfp4_kernel(GemvParams p) 
 #pragma unroll
       for (int u = 0; u < kGemvUnroll; ++u) {
         const int c = cbase + u * 32 + lane;
-        if (c < kc) {
+        if (c < c_hi) {
           const float sc0 = e4m3_to_f32(s0[u]), sc1 = e4m3_to_f32(s1[u]);
           float2 f0[4], f1[4];
 #pragma unroll
@@ -201,21 +222,34 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_nvfp4_kernel(GemvParams p) 
       }
     }
     const float ts = p.tile_scale[r0 >> 4];
+    if (S == 1) {
 #pragma unroll
-    for (int m = 0; m < M; ++m) {
-      const float a0 = warp_sum(acc0[m]) * ts;
-      const float a1 = warp_sum(acc1[m]) * ts;
-      if (lane == 0 && m < p.m_rows) {
-        float* yr = p.y + (int64_t)m * p.ldy;
-        if (r0 < p.rows_out) {
-          if (EPI == EPI_ADD) yr[r0] += a0;
-          else yr[r0] = a0;
-        }
-        if (r0 + 1 < p.rows_out) {
-          if (EPI == EPI_ADD) yr[r0 + 1] += a1;
-          else yr[r0 + 1] = a1;
+      for (int m = 0; m < M; ++m) {
+        const float a0 = warp_sum(acc0[m]) * ts;
+        const float a1 = warp_sum(acc1[m]) * ts;
+        if (lane == 0 && m < p.m_rows) gemv_store<EPI>(p, m, r0, a0, a1);
+      }
+    } else {
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const float a0 = warp_sum(acc0[m]), a1 = warp_sum(acc1[m]);
+        if (lane == 0) {
+          red[warp][0][m] = a0;
+          red[warp][1][m] = a1;
         }
       }
+      __syncthreads();
+      if (part == 0 && lane == 0) {
+        for (int m = 0; m < p.m_rows; ++m) {
+          float a0 = red[slot][0][m], a1 = red[slot][1][m];
+          for (int q = 1; q < S; ++q) {
+            a0 += red[q * ppc + slot][0][m];
+            a1 += red[q * ppc + slot][1][m];
+          }
+          gemv_store<EPI>(p, m, r0, a0 * ts, a1 * ts);
+        }
+      }
+      __syncthreads();
     }
   }
 }
@@ -232,6 +266,21 @@ int num_sms() {
   return g_num_sms;
 }
 
+// K split of a matrix for launches of 4..16 input rows: doubled (up to 4)
+// while its 16-row tiles leave SMs idle and the split CTAs still fit one wave
+// at 16 input rows.  Launches of 1 or 2 rows keep S = 1: there the shared-
+// memory meeting of the partial sums costs more than the extra CTAs save
+// (74-matrix weight stream at M = 1: 290 us unsplit, 304 us split; at M = 16:
+// 1006 us unsplit, 965 us split).
+static int gemv_ksplit(int rows, int K) {
+  const int kc = K / 8, tiles = rows / 16;
+  const size_t smem16 = (size_t)16 * K * sizeof(float) + 2048;
+  const int per_sm = std::max(1, (int)((size_t)227 * 1024 / smem16));
+  int S = 1;
+  while (S < 4 && tiles * S < num_sms() && tiles * S * 2 <= num_sms() * per_sm && kc % (2 * S) == 0) S *= 2;
+  return S;
+}
+
 template <int M, int PRE, int EPI>
 static int launch_gemv_m(const GemvParams& p, cudaStream_t st) {
   const size_t smem = (size_t)M * p.K * sizeof(float);
@@ -240,10 +289,13 @@ static int launch_gemv_m(const GemvParams& p, cudaStream_t st) {
     cudaFuncSetAttribute(gemv_nvfp4_kernel<M, PRE, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     attr_set = true;
   }
-  const int pairs_per_cta = kGemvThreads / 32;
+  const int S = M >= 4 ? gemv_ksplit(p.rows, p.K) : 1;
+  const int pairs_per_cta = kGemvThreads / 32 / S;
   const int want = ceil_div(p.rows / 2, pairs_per_cta);
   const int grid = std::max(1, std::min(want, num_sms() * 4));
-  gemv_nvfp4_kernel<M, PRE, EPI><<<grid, kGemvThreads, smem, st>>>(p);
+  GemvParams q = p;
+  q.ksplit = S;
+  gemv_nvfp4_kernel<M, PRE, EPI><<<grid, kGemvThreads, smem, st>>>(q);
   count_launch();
   return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
 }

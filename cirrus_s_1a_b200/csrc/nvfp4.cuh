@@ -27,6 +27,7 @@ struct GemvParams {
   float* y;
   int ldy;
   int rows_out;   // rows of y written (<= rows)
+  int ksplit;     // warps sharing a row pair over K (1, 2, 4; set by the launcher, 0 = 1)
 };
 
 int num_sms();
