@@ -23,6 +23,7 @@
 // Every wait is bounded
 // (%globaltimer); on timeout the launch sets CB_ERR_TIMEOUT and all CTAs exit.
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 #include "mk.cuh"
@@ -138,18 +139,20 @@ struct GemvJob {
 
 // One weight row as seen by one lane: the 8-code chunks lane, lane+32, ...
 // (K <= 2048, so at most 8 chunks), code words and scale bytes.
+template <int NU>
 struct RowW {
-  uint32_t w[8];
-  uint32_t s[8];
+  uint32_t w[NU];
+  uint32_t s[NU];
 };
 
-__device__ __forceinline__ void load_row(const CbMatrix& W, int64_t tb, int K, int row, bool valid, RowW& r) {
+template <int NU>
+__device__ __forceinline__ void load_row(const CbMatrix& W, int64_t tb, int K, int row, bool valid, RowW<NU>& r) {
   const int lane = threadIdx.x & 31, kc = K >> 3;
   const uint8_t* t = W.tiles + (int64_t)(row >> 4) * tb;
   const uint32_t* cw = reinterpret_cast<const uint32_t*>(t + (row & 15) * (K / 2));
   const uint8_t* sb = t + kTileRows * (K / 2) + (row & 15) * (K / 16);
 #pragma unroll
-  for (int u = 0; u < 8; ++u) {
+  for (int u = 0; u < NU; ++u) {
     const int c = u * 32 + lane;
     const bool ok = valid && c < kc;
     r.w[u] = ok ? __ldg(cw + c) : 0u;
@@ -157,11 +160,11 @@ __device__ __forceinline__ void load_row(const CbMatrix& W, int64_t tb, int K, i
   }
 }
 
-template <int M>
-__device__ __forceinline__ void dot_row(const RowW& r, int K, const float* xs, float (&acc)[M]) {
+template <int M, int NU>
+__device__ __forceinline__ void dot_row(const RowW<NU>& r, int K, const float* xs, float (&acc)[M]) {
   const int lane = threadIdx.x & 31, kc = K >> 3;
 #pragma unroll
-  for (int u = 0; u < 8; ++u) {
+  for (int u = 0; u < NU; ++u) {
     const int c = u * 32 + lane;
     if (c < kc) {
       const float sc = e4m3_to_f32(r.s[u]);
@@ -242,11 +245,12 @@ __device__ __forceinline__ void pre_copy_row(const CbMatrix& W, int K, int row, 
 }
 
 // The lane's view of a preloaded row (the layout load_row produces).
-__device__ __forceinline__ void pre_read_row(const uint8_t* src, int K, bool valid, RowW& r) {
+template <int NU>
+__device__ __forceinline__ void pre_read_row(const uint8_t* src, int K, bool valid, RowW<NU>& r) {
   const int lane = threadIdx.x & 31, kc = K >> 3;
   const uint32_t* cw = reinterpret_cast<const uint32_t*>(src);
 #pragma unroll
-  for (int u = 0; u < 8; ++u) {
+  for (int u = 0; u < NU; ++u) {
     const int c = u * 32 + lane;
     const bool ok = valid && c < kc;
     r.w[u] = ok ? cw[c] : 0u;
@@ -290,7 +294,6 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
   const int step = g.epi == EPI_ACT_ ? ncta : 2 * ncta;
   auto rows_of = [&](int u, int& ra, int& rb, bool& hb) { gemv_rows(g, units, ncta, u, ra, rb, hb); };
   cp_async_wait_all();  // this warp's preloaded rows (read after the staging barrier)
-  RowW A0, B0;
   float(&resa)[M] = p.resa;
   float(&resb)[M] = p.resb;
   auto load_res = [&](int ra, int rb, bool hb) {
@@ -421,6 +424,10 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
   unsigned long long best[M];
 #pragma unroll
   for (int mr = 0; mr < M; ++mr) best[mr] = 0ull;
+  // the row loop, compiled for K <= 768 (3 chunks of 256 codes per lane) and K <= 2048 (8)
+  auto row_loop = [&](auto nu) {
+  constexpr int NU = decltype(nu)::value;
+  RowW<NU> A0, B0;
   for (int u = cta; u < units; u += step) {
     int ra, rb;
     bool hb;
@@ -464,6 +471,9 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
       }
     }
   }
+  };
+  if (K <= 768) row_loop(std::integral_constant<int, 3>{});
+  else row_loop(std::integral_constant<int, 8>{});
   if (g.argmax) {
     if (lane == 0)
 #pragma unroll
