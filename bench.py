@@ -53,7 +53,7 @@ METRIC = "decode tok/s (batch 1, τ=1, 32K ctx) per B200 + HBM GB/s vs 8 TB/s; b
 # DRAM bytes (read + write) of one decode_mk_kernel<1> launch at this workload,
 # from `ncu --set full` (dram__bytes_read.sum + dram__bytes_write.sum); see
 # profiles/decode_mk_kernel_step_32k.md for the command
-DECODE_MK_TRAFFIC = 95_577_856 + 3_637_504
+DECODE_MK_TRAFFIC = 95_557_120 + 3_375_104
 PUBLISHED_TOK_S = 1815.0  # reference: decode tok/s at 32K, tau=1 (GB10, measured stream + roofline remainder)
 CTX = 32768
 FLUSH_BYTES = 512 << 20
