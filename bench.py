@@ -50,13 +50,38 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s (batch 1, τ=1, 32K ctx) per B200 + HBM GB/s vs 8 TB/s; box tok/s 1/2/4/8"
-# DRAM bytes (read + write) of one decode_mk_kernel<1> launch at this workload,
-# from `ncu --set full` (dram__bytes_read.sum + dram__bytes_write.sum); see
-# profiles/decode_mk_kernel_step_32k.md for the command
-DECODE_MK_TRAFFIC = 95_557_120 + 3_375_104
+# DRAM bytes (read + write) of one persistent-kernel launch at this workload,
+# from an ncu capture (dram__bytes_read.sum + dram__bytes_write.sum), and the
+# SHA-256 prefix of the kernel source it was captured from: a changed source
+# reports traffic null until it is captured again.
+STEP_TRAFFIC = {"bytes": 95_557_120 + 3_375_104, "source": "cirrus_s_1a_b200/csrc/decode_mk.cu",
+                "sha256_16": "545d23fbf5629036"}
+CPU_ARM_WHY = ("the reference is a Python package that cannot travel to the GPU box, so the CPU arm runs the "
+               "oracle: the reference forward restated operation by operation (oracle/model.py), checked against "
+               "fixtures generated from the reference itself (tests/golden), with the B200 storage casts")
 PUBLISHED_TOK_S = 1815.0  # reference: decode tok/s at 32K, tau=1 (GB10, measured stream + roofline remainder)
 CTX = 32768
 FLUSH_BYTES = 512 << 20
+
+
+def workload_config(world: int) -> dict:
+    """The ``config`` of both arms' lines (the same workload)."""
+    return {"workload": "cirrus-s-1a decode step, batch 1, tau=1, ctx 32768 (benchmark shapes, random NVFP4 "
+                        "weights seed 0, synthetic cache)",
+            "batch_per_gpu": 1, "ctx": CTX, "weights": "nvfp4 (e2m1 + e4m3/16 + f32)", "kv": "bf16",
+            "indexer_keys": "e4m3", "l2": "flushed between timed steps (512 MB write)",
+            "parallelism": f"replicas x{world} (independent sequences)"}
+
+
+def step_traffic():
+    """(bytes, note) of the recorded ncu traffic, bytes None when the kernel source changed since."""
+    import hashlib
+
+    path = os.path.join(ROOT, STEP_TRAFFIC["source"])
+    sha = hashlib.sha256(open(path, "rb").read()).hexdigest()[:16] if os.path.exists(path) else ""
+    if sha == STEP_TRAFFIC["sha256_16"]:
+        return STEP_TRAFFIC["bytes"], f"ncu capture of {STEP_TRAFFIC['source']} @ {sha}"
+    return None, f"no ncu capture of the current {STEP_TRAFFIC['source']} ({sha})"
 
 
 def _peaks() -> dict:
@@ -126,23 +151,6 @@ def step_bytes(cfg, weight_bytes: float, ctx: int) -> dict:
         "indexer_keys": ctx * cfg.indexer_dim,
         "topk_kv_gather": min(ctx, cfg.sparse_topk + 1) * 2 * kv_row,
     }
-
-
-def fill_cache(cache, ctx: int, seed: int) -> None:
-    import torch
-
-    g = torch.Generator(device=cache.kv_k.device).manual_seed(seed)
-    cache.gdn_state.normal_(0.0, 0.1, generator=g)
-    cache.gdn_conv.normal_(0.0, 1.0, generator=g)
-    for t in (cache.swa_k, cache.swa_v):
-        t.copy_(torch.randn(t.shape, generator=g, device=t.device).to(torch.bfloat16))
-    for t in (cache.kv_k, cache.kv_v):
-        t[:, :ctx].copy_(torch.randn(t[:, :ctx].shape, generator=g, device=t.device).to(torch.bfloat16))
-    di = cache.model.cfg.indexer_dim
-    ik = torch.randn((cache.batch, ctx, di), generator=g, device=cache.kv_ik.device).to(torch.float8_e4m3fn)
-    cache.kv_ik[:, :ctx, :di].copy_(ik.view(torch.uint8))
-    cache.pos_dev.fill_(ctx - 1)
-    cache.pos_host = [ctx - 1] * cache.batch
 
 
 def weight_stream_graph(eng, M: int = 1, tensor_cores: bool = False):
@@ -255,12 +263,11 @@ def run_reference(args, rank: int) -> None:
             "warmup": args.warmup, "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": value / PUBLISHED_TOK_S, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": "cirrus-s-1a decode step, batch 1, tau=1, ctx 32768 (benchmark shapes, "
-                                   "random NVFP4 fake-quantised weights seed 0, synthetic cache)",
-                       "batch": 1, "ctx": CTX},
+            "config": workload_config(args.gpus),
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
                              "sample": f"{args.steps} oracle decode steps at ctx {CTX} (torch CPU fp32, "
-                                       f"{threads} threads)"},
+                                       f"{threads} threads)",
+                             "why_port": CPU_ARM_WHY},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -278,7 +285,7 @@ def profile_step(B: int, T: int) -> None:
     cfg = baseline_config()
     eng = CirrusB200(cfg, synthetic.random_state_dict(cfg, seed=0), device="cuda:0", max_ctx=CTX + 64)
     cache = eng.new_cache(B)
-    fill_cache(cache, CTX, 1)
+    synthetic.fill_cache(cache, CTX, 1)
     ids = torch.randint(0, cfg.vocab_size, (B, T), device="cuda:0")
     for _ in range(2):
         cache.pos_dev.fill_(CTX - 1)
@@ -332,7 +339,7 @@ def main() -> None:
     sd = synthetic.random_state_dict(cfg, seed=0)
     eng = CirrusB200(cfg, sd, device=dev, max_ctx=CTX + 64)
     cache = eng.new_cache(1)
-    fill_cache(cache, CTX, seed=1 + rank)
+    synthetic.fill_cache(cache, CTX, seed=1 + rank)
 
     L = _lib.lib()
     n0 = L.cb_launch_count()
@@ -440,7 +447,7 @@ def main() -> None:
     del graph
     for Bb, Tb in ((8, 1), (1, 5), (64, 1), (64, 5)):
         bcache = eng.new_cache(Bb)
-        fill_cache(bcache, CTX, 1)
+        synthetic.fill_cache(bcache, CTX, 1)
         bg = DecodeGraph(eng, bcache, T=Tb, n_logits=Tb, want_logits=False)
         b_ms = []
         for i in range(args.warmup + 3):
@@ -469,19 +476,17 @@ def main() -> None:
     step_total = sum(sb.values())
     ms_step = t_total_ms / args.steps
     value = world * args.steps / (t_total_ms * 1e-3)
+    traffic, traffic_note = step_traffic()
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": value / PUBLISHED_TOK_S, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "cirrus-s-1a decode step, batch 1, tau=1, ctx 32768 (benchmark shapes, random "
-                               "NVFP4 weights seed 0, synthetic cache), one CUDA graph per step",
-                   "batch_per_gpu": 1, "ctx": CTX, "weights": "nvfp4 (e2m1 + e4m3/16 + f32)",
-                   "kv": "bf16", "indexer_keys": "e4m3", "l2": "flushed between timed steps (512 MB write)",
-                   "parallelism": f"replicas x{world} (independent sequences)"},
+        "config": workload_config(world),
         "roofline": {"bound": "hbm", "kernel": "decode_mk_kernel<1> (one launch = one decode step)",
                      "achieved": step_total / (ms_step * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": step_total / (ms_step * 1e-3) / 1e9 / peaks["hbm_gbs"],
-                     "traffic": DECODE_MK_TRAFFIC, "bytes": step_total, "parts": sb, "us": ms_step * 1e3,
+                     "traffic": traffic, "traffic_source": traffic_note, "bytes": step_total, "parts": sb,
+                     "us": ms_step * 1e3,
                      "peak_source": peaks["source"]},
         "weight_stream": {"bound": "hbm", "kernel": f"gemv_nvfp4 ({n_mats} launches, M=1, one CUDA graph)",
                           "achieved": wbytes / w_avg_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -500,6 +505,7 @@ def main() -> None:
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(cfg, sd, cache, CTX, args.cpu_budget_s, 50)
+        line["cpu_baseline"]["why_port"] = CPU_ARM_WHY
     if rank == 0:
         print(json.dumps(line), flush=True)
     del wgraph

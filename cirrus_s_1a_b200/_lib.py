@@ -30,7 +30,8 @@ CB_NOALLOC_MAX_SCORES = 1 << 20
 EXPORTS = ("cb_abi_version", "cb_status_string", "cb_nvfp4_quantize", "cb_nvfp4_pack_tiles", "cb_gemv_nvfp4",
            "cb_embed", "cb_argmax", "cb_gdn_step", "cb_indexer_topk", "cb_workspace_bytes", "cb_forward",
            "cb_read_status", "cb_clear_status", "cb_launch_count", "cb_indexer_topk_noalloc", "cb_read_trace",
-           "cb_verify_gemm_nvfp4", "cb_gdn_chunk_prefill")
+           "cb_verify_gemm_nvfp4", "cb_gdn_chunk_prefill", "cb_set_wait_limit",
+           "cb_workspace_layout")
 
 P = C.c_void_p
 I32 = C.c_int32
@@ -78,6 +79,11 @@ class CbCache(C.Structure):
                 ("kv_v", P), ("kv_ik", P)]
 
 
+class CbWorkspaceLayout(C.Structure):
+    _fields_ = [("bytes", C.c_uint64), ("proj", C.c_uint64), ("sel_idx", C.c_uint64), ("sel_cnt", C.c_uint64),
+                ("ld_proj", I32), ("sel_ld", I32)]
+
+
 class CbError(RuntimeError):
     pass
 
@@ -111,6 +117,8 @@ def lib() -> C.CDLL:
         L.cb_forward.argtypes = [C.POINTER(CbModel), C.POINTER(CbCache), P, C.c_size_t, P, I32, I32, P, P, P, P]
         L.cb_read_status.argtypes = [P, C.POINTER(I32), P]
         L.cb_clear_status.argtypes = [P, P]
+        L.cb_set_wait_limit.argtypes = [P, C.c_uint64, I32, P]
+        L.cb_workspace_layout.argtypes = [C.POINTER(CbModel), I32, I32, I32, C.POINTER(CbWorkspaceLayout)]
         L.cb_read_trace.argtypes = [C.POINTER(CbModel), I32, I32, I32, P, P, I32, P]
         L.cb_launch_count.restype = C.c_int64
         L.cb_launch_count.argtypes = []

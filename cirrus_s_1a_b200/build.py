@@ -4,8 +4,9 @@
 
 Every ``csrc/*.cu`` is compiled for ``arch=compute_100a,code=sm_100a`` and
 linked into one position-independent shared library next to this file; the
-library exports the C ABI declared in ``include/cirrus_b200.h``.  Sources are
-rebuilt only when a source or header is newer than the library.
+library exports the C ABI declared in ``include/cirrus_b200.h``.  An object is
+recompiled only when its source or a header is newer than it; objects compile
+in parallel.
 """
 
 from __future__ import annotations
@@ -15,6 +16,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
@@ -35,28 +37,36 @@ def sources() -> list:
     return sorted(glob.glob(os.path.join(HERE, "csrc", "*.cu")))
 
 
-def _stale() -> bool:
-    if not os.path.exists(LIB):
+def _headers() -> list:
+    return glob.glob(os.path.join(HERE, "csrc", "*.cuh")) + glob.glob(os.path.join(ROOT, "include", "*.h"))
+
+
+def _newer(target: str, deps: list) -> bool:
+    """True when ``target`` is missing or older than any of ``deps``."""
+    if not os.path.exists(target):
         return True
-    t = os.path.getmtime(LIB)
-    deps = sources() + glob.glob(os.path.join(HERE, "csrc", "*.cuh")) + glob.glob(os.path.join(ROOT, "include", "*.h"))
+    t = os.path.getmtime(target)
     return any(os.path.getmtime(f) > t for f in deps)
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and not _stale():
+    objdir = os.path.join(ROOT, "_build")
+    objs = [os.path.join(objdir, os.path.basename(s)[:-3] + ".o") for s in sources()]
+    stale = [(s, o) for s, o in zip(sources(), objs) if force or _newer(o, [s, *_headers()])]
+    if not stale and not _newer(LIB, objs):
         return LIB
     nvcc = _nvcc()
-    objdir = os.path.join(ROOT, "_build")
     os.makedirs(objdir, exist_ok=True)
-    objs = []
-    for src in sources():
-        obj = os.path.join(objdir, os.path.basename(src)[:-3] + ".o")
+
+    def compile_one(pair):
+        src, obj = pair
         cmd = [nvcc, *ARCH, *FLAGS, "-I", os.path.join(ROOT, "include"), "-c", src, "-o", obj]
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)
-        objs.append(obj)
+
+    with ThreadPoolExecutor(max_workers=max(1, min(len(stale), os.cpu_count() or 1))) as ex:
+        list(ex.map(compile_one, stale))
     tmp = LIB + ".tmp"
     subprocess.run([nvcc, *ARCH, "-shared", "-Xcompiler", "-fPIC", *objs, "-o", tmp, "-lcudart"], check=True)
     os.replace(tmp, LIB)

@@ -208,11 +208,7 @@ __global__ void swa_combine_kernel(SwaParams p) {
 int launch_swa(const SwaParams& p, int batch, cudaStream_t st) {
   if (p.hd > kSwaThreads || kSwaThreads % p.hd || p.hd % 8 || p.split_len != kSwaSplit) return CB_ERR_SHAPE;
   const size_t smem = sizeof(float) * ((size_t)p.split_len * (2 * p.hd + 1) + p.hd + p.split_len + kSwaThreads);
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(swa_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-    set = true;
-  }
+  if (ensure_smem_attr((const void*)swa_attn_kernel, 160 * 1024) != CB_OK) return CB_ERR_CUDA;
   swa_attn_kernel<<<dim3(p.n_splits, p.Hkv, batch), kSwaThreads, smem, st>>>(p);
   count_launch();
   if (cudaGetLastError() != cudaSuccess) return CB_ERR_CUDA;
@@ -370,11 +366,7 @@ int launch_cross(const CrossParams& p, int rows, cudaStream_t st) {
   const size_t smem = sizeof(float) * ((size_t)G * p.hd + (size_t)G * kCrossChunk) +
                       sizeof(uint16_t) * 2 * kCrossChunk * (size_t)(p.hd + 8);
   if (smem > 200 * 1024) return CB_ERR_SHAPE;
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(cross_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    set = true;
-  }
+  if (ensure_smem_attr((const void*)cross_attn_kernel, 200 * 1024) != CB_OK) return CB_ERR_CUDA;
   cross_attn_kernel<<<dim3(p.Hkv, rows), kCrossThreads, smem, st>>>(p);
   count_launch();
   return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;

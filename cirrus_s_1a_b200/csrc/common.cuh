@@ -15,6 +15,13 @@ namespace cb {
 // Host-side count of kernel launches issued by this library (cb_launch_count).
 void count_launch();
 
+// Per-device launch state (devstate.cu): the dynamic shared-memory opt-in of a
+// kernel on the current device (CB_OK or CB_ERR_CUDA), its resident CTAs per SM
+// at that size, and the current device's SM count.
+int ensure_smem_attr(const void* fn, int bytes);
+int resident_ctas(const void* fn, int threads, int smem_bytes);
+int num_sms();
+
 constexpr int kTileRows = CB_TILE_ROWS;
 constexpr int kWarp = 32;
 

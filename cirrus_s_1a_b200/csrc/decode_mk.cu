@@ -61,13 +61,18 @@ __device__ __forceinline__ unsigned long long gtimer() {
 // Work that does not depend on the other CTAs' writes (the next phase's
 // weight loads) goes between the two.  grid_wait returns false when the launch
 // must stop (this CTA's wait timed out, or another CTA's did).
+// Per-CTA copy of the launch's wait limit and stall hook (thread 0 reads them at start).
+__shared__ unsigned long long s_wait_limit;
+__shared__ unsigned s_stall_barrier;
+
 __device__ __forceinline__ void grid_arrive(const MkArgs& a, unsigned& gen) {
   __syncthreads();
   gen += 1;
   if (threadIdx.x == 0) {
     if (blockIdx.x == 0 && 2 * gen < (unsigned)kMkTrace) a.trace[2 * gen - 1] = gtimer();
     __threadfence();
-    atomicAdd(a.sync, 1u);
+    // the test hook leaves this barrier one arrival short, so every wait on it runs out
+    if (!(blockIdx.x == 0 && gen == s_stall_barrier)) atomicAdd(a.sync, 1u);
   }
 }
 
@@ -83,7 +88,7 @@ __device__ __forceinline__ bool grid_wait(const MkArgs& a, unsigned gen, int* s_
           ok = 0;
           break;
         }
-        if (gtimer() - t0 > a.timeout_ns) {
+        if (gtimer() - t0 > s_wait_limit) {
           atomicExch(a.abort_flag, 1);
           atomicCAS(a.status, 0, CB_ERR_TIMEOUT);
           ok = 0;
@@ -1239,6 +1244,12 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     }
   }
   if (cta == 0 && tid == 0) a.trace[0] = gtimer();
+  if (tid == 0) {
+    const unsigned long long lim = __ldcg(&a.ctl->limit_ns);
+    s_wait_limit = lim ? lim : kDefaultWaitNs;
+    const int stall = __ldcg(&a.ctl->stall_barrier);
+    s_stall_barrier = stall > 0 ? (unsigned)stall : 0u;
+  }
   // Each GEMV's first weights (and residual) are loaded between the arrival at
   // the barrier before it and the wait there (GemvPre): they do not depend on
   // the previous phase, so their latency hides behind the barrier.
@@ -1546,18 +1557,8 @@ int launch_mk(const MkArgs& a, int grid, cudaStream_t st) {
   else if (M <= 2) fn = decode_mk_kernel<2>;
   else if (M <= 4) fn = decode_mk_kernel<4>;
   else fn = decode_mk_kernel<8>;
-  static bool attr[4] = {false, false, false, false};
-  const int slot = M <= 1 ? 0 : (M <= 2 ? 1 : (M <= 4 ? 2 : 3));
-  static int resident[4] = {0, 0, 0, 0};
-  if (!attr[slot]) {
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
-      return CB_ERR_CUDA;
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kMkThreads, kSmem) != cudaSuccess) per_sm = 0;
-    resident[slot] = per_sm;
-    attr[slot] = true;
-  }
-  if (resident[slot] < 1) return CB_ERR_SHAPE;  // the grid could not be co-resident
+  if (ensure_smem_attr((const void*)fn, kSmem) != CB_OK) return CB_ERR_CUDA;
+  if (resident_ctas((const void*)fn, kMkThreads, kSmem) < 1) return CB_ERR_SHAPE;  // the grid could not be co-resident
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kMkThreads);

@@ -12,6 +12,7 @@
 // can be captured once in a CUDA graph and replayed every step.
 #include <algorithm>
 #include <atomic>
+#include <cstddef>
 #include <cstring>
 
 #include "attn.cuh"
@@ -198,7 +199,7 @@ static int launch_persistent(const CbModel& m, const CbCache& c, const Workspace
   a.logits = logits;
   a.hidden = hidden;
   a.argmax = argmax;
-  a.timeout_ns = 200ull * 1000 * 1000;
+  a.ctl = reinterpret_cast<const WaitCtl*>(w.status);
   if (cudaMemsetAsync(w.sync, 0, 256, st) != cudaSuccess) return CB_ERR_CUDA;
   return launch_mk(a, num_sms(), st);
 }
@@ -243,6 +244,21 @@ extern "C" size_t cb_workspace_bytes(const CbModel* m, int32_t batch, int32_t T,
   return carve(*m, batch, T, max_ctx, nullptr).bytes;
 }
 
+extern "C" int cb_workspace_layout(const CbModel* m, int32_t batch, int32_t T, int32_t max_ctx,
+                                   CbWorkspaceLayout* out) {
+  if (!m || !out || batch <= 0 || max_ctx <= 0 || T <= 0) return CB_ERR_ARG;
+  const Workspace w = carve(*m, batch, T, max_ctx, nullptr);
+  const Workspace z = carve(*m, batch, T, max_ctx, reinterpret_cast<char*>(256));  // any non-null base
+  auto off = [&](const void* p) { return (uint64_t)(reinterpret_cast<const char*>(p) - reinterpret_cast<char*>(256)); };
+  out->bytes = w.bytes;
+  out->proj = off(z.proj);
+  out->sel_idx = off(z.sel_idx);
+  out->sel_cnt = off(z.sel_cnt);
+  out->ld_proj = z.ldp;
+  out->sel_ld = z.sel_ld;
+  return CB_OK;
+}
+
 extern "C" int cb_read_status(const void* workspace, int32_t* status, void* stream) {
   if (!workspace || !status) return CB_ERR_ARG;
   if (cudaMemcpyAsync(status, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost, (cudaStream_t)stream) !=
@@ -261,6 +277,19 @@ extern "C" int cb_read_trace(const CbModel* m, int32_t batch, int32_t T, int32_t
     return -CB_ERR_CUDA;
   if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return -CB_ERR_CUDA;
   return cnt;
+}
+
+extern "C" int cb_set_wait_limit(void* workspace, uint64_t limit_ns, int32_t stall_barrier, void* stream) {
+  if (!workspace || stall_barrier < 0) return CB_ERR_ARG;
+  const unsigned long long lim = limit_ns;
+  cudaStream_t st = (cudaStream_t)stream;
+  char* base = static_cast<char*>(workspace);
+  if (cudaMemcpyAsync(base + offsetof(WaitCtl, stall_barrier), &stall_barrier, sizeof(int32_t),
+                      cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(base + offsetof(WaitCtl, limit_ns), &lim, sizeof(lim), cudaMemcpyHostToDevice, st) !=
+          cudaSuccess)
+    return CB_ERR_CUDA;
+  return cudaStreamSynchronize(st) == cudaSuccess ? CB_OK : CB_ERR_CUDA;
 }
 
 extern "C" int cb_clear_status(void* workspace, void* stream) {

@@ -135,11 +135,7 @@ int launch_gdn_step(const GdnParams& p, cudaStream_t st) {
   dim3 grid(p.H, p.batch);
 #define CB_GDN_CASE(K)                                                                                   \
   case K: {                                                                                              \
-    static bool set = false;                                                                             \
-    if (!set) {                                                                                          \
-      cudaFuncSetAttribute(gdn_step_kernel<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024); \
-      set = true;                                                                                        \
-    }                                                                                                    \
+    if (ensure_smem_attr((const void*)gdn_step_kernel<K>, 160 * 1024) != CB_OK) return CB_ERR_CUDA;      \
     gdn_step_kernel<K><<<grid, kGdnThreads, smem, st>>>(p);                                              \
     break;                                                                                               \
   }

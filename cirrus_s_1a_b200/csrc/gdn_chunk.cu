@@ -210,13 +210,7 @@ extern "C" int cb_gdn_chunk_prefill(const float* q, const float* k, const float*
                                     float* state, float* out, void* stream) {
   if (!q || !k || !v || !g || !beta || !state || !out || B < 1 || T < 1 || H < 1) return CB_ERR_ARG;
   if (Dk != kGd || Dv != kGd) return CB_ERR_SHAPE;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(gdn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_chunk_smem()) !=
-        cudaSuccess)
-      return CB_ERR_CUDA;
-    attr = true;
-  }
+  if (ensure_smem_attr((const void*)gdn_chunk_kernel, (int)gdn_chunk_smem()) != CB_OK) return CB_ERR_CUDA;
   GdnChunkParams p{q, k, v, g, beta, state, out, B, T, H, scale};
   gdn_chunk_kernel<<<B * H, kGThreads, gdn_chunk_smem(), (cudaStream_t)stream>>>(p);
   count_launch();

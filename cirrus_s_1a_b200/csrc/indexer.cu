@@ -216,11 +216,7 @@ int launch_indexer_topk(const IndexerParams& p, cudaStream_t st) {
   indexer_score_kernel<<<dim3(blocks_per_row, p.rows), kScoreThreads, 0, st>>>(p);
   count_launch();
   if (cudaGetLastError() != cudaSuccess) return CB_ERR_CUDA;
-  static bool set = false;
-  if (!set) {
-    cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-    set = true;
-  }
+  if (ensure_smem_attr((const void*)topk_kernel, 64 * 1024) != CB_OK) return CB_ERR_CUDA;
   topk_kernel<<<p.rows, kTopkThreads, nsort * sizeof(int), st>>>(p, nsort);
   count_launch();
   return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;

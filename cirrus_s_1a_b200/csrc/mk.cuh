@@ -15,6 +15,15 @@ constexpr int kMkCrossSplit = 64;      // selected keys per cross-attention work
 constexpr int kMkMaxRows = 8;          // batch * T handled by one persistent launch
 constexpr int kMkMaxQ = 24;            // (q heads per KV head) * T per SWA work item
 constexpr int kMkTrace = 512;          // phase timestamps
+constexpr unsigned long long kDefaultWaitNs = 200ull * 1000 * 1000;  // bounded-wait limit when none is set
+
+// The first bytes of a cb_forward workspace: the device status word and the
+// control words that cb_set_wait_limit writes (zero = defaults).
+struct WaitCtl {
+  int32_t status;               // CB_OK or the first device-side error
+  int32_t stall_barrier;        // > 0: CTA 0 skips its arrival at this barrier (fault injection for tests)
+  unsigned long long limit_ns;  // limit of every bounded wait of the persistent kernel; 0 = kDefaultWaitNs
+};
 
 // Everything one persistent launch needs, passed by value (__grid_constant__).
 struct MkArgs {
@@ -50,7 +59,7 @@ struct MkArgs {
   float* logits;     // [RQ][vocab] or null
   float* hidden;     // [RQ][d] or null
   int32_t* argmax;   // [RQ] or null
-  unsigned long long timeout_ns;
+  const WaitCtl* ctl;  // wait limit and test hook (read once per launch)
 };
 
 size_t mk_smem_bytes();

@@ -254,18 +254,6 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_nvfp4_kernel(GemvParams p) 
   }
 }
 
-static int g_num_sms = 0;
-
-int num_sms() {
-  if (g_num_sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (g_num_sms <= 0) g_num_sms = 148;
-  }
-  return g_num_sms;
-}
-
 // K split of a matrix for launches of 4..16 input rows: doubled (up to 4)
 // while its 16-row tiles leave SMs idle and the split CTAs still fit one wave
 // at 16 input rows.  Launches of 1 or 2 rows keep S = 1: there the shared-
@@ -284,11 +272,7 @@ static int gemv_ksplit(int rows, int K) {
 template <int M, int PRE, int EPI>
 static int launch_gemv_m(const GemvParams& p, cudaStream_t st) {
   const size_t smem = (size_t)M * p.K * sizeof(float);
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(gemv_nvfp4_kernel<M, PRE, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr_set = true;
-  }
+  if (ensure_smem_attr((const void*)gemv_nvfp4_kernel<M, PRE, EPI>, 200 * 1024) != CB_OK) return CB_ERR_CUDA;
   const int S = M >= 4 ? gemv_ksplit(p.rows, p.K) : 1;
   const int pairs_per_cta = kGemvThreads / 32 / S;
   const int want = ceil_div(p.rows / 2, pairs_per_cta);

@@ -30,7 +30,6 @@ struct GemvParams {
   int ksplit;     // warps sharing a row pair over K (1, 2, 4; set by the launcher, 0 = 1)
 };
 
-int num_sms();
 int launch_gemv(const GemvParams& p, int pre, int epi, cudaStream_t st);
 int launch_embed(const CbMatrix& tab, int vocab, const int64_t* ids, int64_t ids_ld, int batch, int T, int c0,
                  float* h, int32_t* status, cudaStream_t st);

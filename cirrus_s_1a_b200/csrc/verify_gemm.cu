@@ -312,13 +312,7 @@ extern "C" int cb_verify_gemm_nvfp4(const CbMatrix* w, const uint16_t* x, int32_
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx % 8) || (reinterpret_cast<uintptr_t>(w->tiles) & 15))
     return CB_ERR_ARG;
   const size_t smem = verify_gemm_smem(K);
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(verify_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)verify_gemm_smem(2048)) !=
-        cudaSuccess)
-      return CB_ERR_CUDA;
-    attr = true;
-  }
+  if (ensure_smem_attr((const void*)verify_gemm_kernel, (int)verify_gemm_smem(2048)) != CB_OK) return CB_ERR_CUDA;
   VerifyParams p{};
   p.tiles = w->tiles;
   p.tile_scale = w->tile_scale;
@@ -333,9 +327,7 @@ extern "C" int cb_verify_gemm_nvfp4(const CbMatrix* w, const uint16_t* x, int32_
   p.status = status;
   // split K over a cluster of up to 8 CTAs while the grid stays within two CTAs per SM
   const int tiles = (rows_out + kVgM - 1) / kVgM, nall = K / kVgKc;
-  int sms = 148;
-  int dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = num_sms();
   int S = 1;
   while (S < 8 && tiles * S * 2 <= 2 * sms && S * 2 <= nall) S *= 2;
   cudaLaunchConfig_t cfg{};

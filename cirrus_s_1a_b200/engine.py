@@ -331,6 +331,37 @@ class CirrusB200:
                                    _lib.ptr(argmax), st)
         _lib.check(rc, "cb_forward")
 
+    def intermediates(self, cache: DeviceCache, T: int = 1) -> dict:
+        """Views into the workspace of the last forward on this cache's shape
+        (``cb_workspace_layout``): ``proj`` float32 [batch*Tc, ld] (the shared
+        projection: k | v | idx_k | idx_q | idx_w), ``sel_idx`` int32 [rows, k+1]
+        and ``sel_cnt`` int32 [rows] (the keys each query row selected)."""
+        ws = self.workspace(cache.batch, T, cache.max_ctx)
+        lay = _lib.CbWorkspaceLayout()
+        _lib.check(_lib.lib().cb_workspace_layout(C.byref(self.model.desc), cache.batch, T, cache.max_ctx,
+                                                  C.byref(lay)), "cb_workspace_layout")
+        Tc = min(T, CB_MAX_T)
+        rows = cache.batch * Tc
+
+        def view(off, n, dtype):
+            return ws[off:off + 4 * n].view(dtype)
+
+        return {"proj": view(lay.proj, rows * lay.ld_proj, torch.float32).view(rows, lay.ld_proj),
+                "sel_idx": view(lay.sel_idx, rows * lay.sel_ld, torch.int32).view(rows, lay.sel_ld),
+                "sel_cnt": view(lay.sel_cnt, rows, torch.int32)}
+
+    def set_wait_limit(self, cache: DeviceCache, limit_ns: int, stall_barrier: int = 0, T: int = 1) -> None:
+        """Bounded-wait limit of the persistent kernel on this cache's workspace
+        (``cb_set_wait_limit``; 0 = the default 200 ms).  ``stall_barrier`` > 0
+        makes one barrier of every later launch incomplete (fault injection for tests)."""
+        ws = self.workspace(cache.batch, T, cache.max_ctx)
+        _lib.check(_lib.lib().cb_set_wait_limit(ws.data_ptr(), int(limit_ns), int(stall_barrier),
+                                                _stream_ptr(self.device)), "cb_set_wait_limit")
+
+    def clear_status(self, cache: DeviceCache, T: int = 1) -> None:
+        ws = self.workspace(cache.batch, T, cache.max_ctx)
+        _lib.check(_lib.lib().cb_clear_status(ws.data_ptr(), _stream_ptr(self.device)), "cb_clear_status")
+
     def read_status(self, cache: DeviceCache, T: int = 1) -> int:
         ws = self.workspace(cache.batch, T, cache.max_ctx)
         out = _lib.I32(0)

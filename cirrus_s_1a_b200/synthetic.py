@@ -112,6 +112,45 @@ def random_state_dict(cfg, seed: int = 0, norm_jitter: float = 0.0) -> dict:
     return sd
 
 
+def fill_cache(cache, ctx: int, seed: int, ties: str | None = None) -> None:
+    """Seeded synthetic decode state at context ``ctx`` for every sequence of a
+    ``DeviceCache`` (the stand-in for a real ``ctx``-token prompt): GDN state
+    N(0, 0.1), conv windows N(0, 1), SWA ring and shared K/V bf16 N(0, 1),
+    indexer keys E4M3 of N(0, 1); positions are set to ``ctx - 1``, so the next
+    one-token forward sees ``ctx`` keys.
+
+    ``ties`` makes the indexer scores tie heavily, so that the most-recent-first
+    tie rule decides the selection: ``"repeat"`` keeps 2% of the keys random,
+    zeroes the rest (score exactly 0 after the ReLU) and copies 64 random keys
+    to ctx/8 positions (runs of exactly equal positive scores around the k-th
+    largest); ``"zero"`` keeps 0.5% random and zeroes the rest, so fewer than k
+    keys score above 0 and the threshold falls inside the run of zeros.
+    """
+    g = torch.Generator(device=cache.kv_k.device).manual_seed(seed)
+    dev = cache.kv_k.device
+    cache.gdn_state.normal_(0.0, 0.1, generator=g)
+    cache.gdn_conv.normal_(0.0, 1.0, generator=g)
+    for t in (cache.swa_k, cache.swa_v):
+        t.copy_(torch.randn(t.shape, generator=g, device=dev).to(torch.bfloat16))
+    for t in (cache.kv_k, cache.kv_v):
+        t[:, :ctx].copy_(torch.randn(t[:, :ctx].shape, generator=g, device=dev).to(torch.bfloat16))
+    di = cache.model.cfg.indexer_dim
+    ik = torch.randn((cache.batch, ctx, di), generator=g, device=dev)
+    if ties is not None:
+        if ties not in ("repeat", "zero"):
+            raise ValueError("ties must be None, 'repeat' or 'zero'")
+        keep = torch.rand((cache.batch, ctx, 1), generator=g, device=dev) < (0.02 if ties == "repeat" else 0.005)
+        ik = ik * keep
+        if ties == "repeat":
+            src = torch.randn((cache.batch, 64, di), generator=g, device=dev)
+            for b in range(cache.batch):
+                rows = torch.randint(0, ctx, (ctx // 8,), generator=g, device=dev)
+                ik[b, rows] = src[b, torch.randint(0, 64, (ctx // 8,), generator=g, device=dev)]
+    cache.kv_ik[:, :ctx, :di].copy_(ik.to(torch.float8_e4m3fn).view(torch.uint8))
+    cache.pos_dev.fill_(ctx - 1)
+    cache.pos_host = [ctx - 1] * cache.batch
+
+
 def random_prompt(n: int, vocab: int, seed: int = 0, copy_frac: float = 0.25, span: int = 8) -> list:
     """``n`` token ids: uniform over the vocabulary, except that each 8-token span
     is, with probability ``copy_frac``, a copy of an earlier span."""

@@ -246,10 +246,36 @@ size_t cb_workspace_bytes(const CbModel* m, int32_t batch, int32_t T, int32_t ma
 int cb_forward(const CbModel* m, const CbCache* c, void* workspace, size_t workspace_bytes, const int64_t* ids,
                int32_t T, int32_t n_logits, float* logits, float* hidden, int32_t* argmax, void* stream);
 
+/* Where cb_forward keeps its intermediate results inside a workspace sized for
+ * (batch, T, max_ctx), as byte offsets from the workspace start, for reading
+ * them back after a forward (tests, debugging):
+ *   proj     float32 [batch*Tc][ld_proj], Tc = min(T, CB_MAX_T): the shared
+ *            projection of the last chunk's rows (k | v | idx_k | idx_q | idx_w at
+ *            the CbModel offsets; row b*Tc + t);
+ *   sel_idx  int32 [batch*nq][sel_ld]: the keys each query row of the last chunk
+ *            selected (ascending, sel_cnt[r] of them), nq = query rows per sequence;
+ *   sel_cnt  int32 [batch*nq].
+ * The reference computes these inside CirrusModel.forward (model.py:136-156). */
+typedef struct CbWorkspaceLayout {
+  uint64_t bytes, proj, sel_idx, sel_cnt;
+  int32_t ld_proj, sel_ld;
+} CbWorkspaceLayout;
+int cb_workspace_layout(const CbModel* m, int32_t batch, int32_t T, int32_t max_ctx, CbWorkspaceLayout* out);
+
 /* Copy the workspace's device status word into *status (synchronises on the stream). */
 int cb_read_status(const void* workspace, int32_t* status, void* stream);
 /* Clear the status word (stream-ordered). */
 int cb_clear_status(void* workspace, void* stream);
+
+/* Limit of every bounded wait of the persistent kernel that runs on this
+ * workspace (limit_ns = 0 restores the default, 200 ms): a wait that lasts
+ * longer sets CB_ERR_TIMEOUT in the status word, and every CTA of that launch
+ * returns without advancing the cache.  stall_barrier > 0 is a fault-injection
+ * hook for tests: CTA 0 then skips its arrival at that grid barrier, so the
+ * waits on it run out (0 = off).  Synchronises on the stream.  No reference
+ * counterpart: the reference's grid barrier spins without a limit
+ * (cirrus/perf/bench_kernels.cu:116-117). */
+int cb_set_wait_limit(void* workspace, uint64_t limit_ns, int32_t stall_barrier, void* stream);
 
 /* Number of kernels this library has launched in this process (all entry points). */
 int64_t cb_launch_count(void);

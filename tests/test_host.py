@@ -66,7 +66,7 @@ def test_ctypes_structs_match_c_layout(built_lib):
     if not gcc:
         pytest.skip("no gcc")
     structs = {"CbMatrix": _lib.CbMatrix, "CbSelfLayer": _lib.CbSelfLayer, "CbCrossLayer": _lib.CbCrossLayer,
-               "CbModel": _lib.CbModel, "CbCache": _lib.CbCache}
+               "CbModel": _lib.CbModel, "CbCache": _lib.CbCache, "CbWorkspaceLayout": _lib.CbWorkspaceLayout}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "cirrus_b200.h"', "int main(void){"]
     for name, cls in structs.items():
         lines.append(f'printf("{name} %zu\\n", sizeof({name}));')

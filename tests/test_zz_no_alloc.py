@@ -58,7 +58,9 @@ def test_noalloc_topk_matches_allocating_entry_point():
 
     L = _lib.lib()
     Hi, Di, k = 4, 64, 512
-    for seed, (rows, max_ctx) in ((1, (6, 32768)), (2, (9, 20000))):  # two calls in a row
+    # calls in a row; the last one fills the static scratch exactly (32 * 32768 = 2^20 scores)
+    for seed, (rows, max_ctx) in ((1, (6, 32768)), (2, (9, 20000)), (3, (32, 32768))):
+        assert rows * max_ctx <= _lib.CB_NOALLOC_MAX_SCORES
         case = _case(seed, rows, Hi, Di, max_ctx, k)
         sel_a, cnt_a = _run(L, False, *case, Hi, Di, max_ctx, k, rows)
         sel_b, cnt_b = _run(L, True, *case, Hi, Di, max_ctx, k, rows)
