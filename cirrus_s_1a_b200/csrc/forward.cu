@@ -415,8 +415,10 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
     }
 
     // ------------------------------------------------ shared KV (YOCO)
-    const int lds = m.shared_proj.rows;
-    CB_TRY(gemv(m.shared_proj, w.h, d, R, m.shared_norm, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.proj, lds, lds, st));
+    // row stride w.ldp, as in the persistent kernel (cb_workspace_layout reports it)
+    const int lds = w.ldp;
+    CB_TRY(gemv(m.shared_proj, w.h, d, R, m.shared_norm, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.proj, lds,
+                m.shared_proj.rows, st));
     {
       HeadPrepParams hp{};
       hp.proj = w.proj;

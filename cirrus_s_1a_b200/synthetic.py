@@ -120,11 +120,12 @@ def fill_cache(cache, ctx: int, seed: int, ties: str | None = None) -> None:
     one-token forward sees ``ctx`` keys.
 
     ``ties`` makes the indexer scores tie heavily, so that the most-recent-first
-    tie rule decides the selection: ``"repeat"`` keeps 2% of the keys random,
-    zeroes the rest (score exactly 0 after the ReLU) and copies 64 random keys
-    to ctx/8 positions (runs of exactly equal positive scores around the k-th
-    largest); ``"zero"`` keeps 0.5% random and zeroes the rest, so fewer than k
-    keys score above 0 and the threshold falls inside the run of zeros.
+    tie rule decides the selection: ``"repeat"`` zeroes every key (score exactly
+    0 after the ReLU) and then copies 64 random keys to ctx/8 positions, so every
+    nonzero score belongs to a run of about 64 exactly equal scores and the k-th
+    largest is always tied; ``"zero"`` keeps 0.5% of the keys random and zeroes
+    the rest, so fewer than k keys score above 0 and the threshold falls inside
+    the run of zeros.
     """
     g = torch.Generator(device=cache.kv_k.device).manual_seed(seed)
     dev = cache.kv_k.device
@@ -139,7 +140,7 @@ def fill_cache(cache, ctx: int, seed: int, ties: str | None = None) -> None:
     if ties is not None:
         if ties not in ("repeat", "zero"):
             raise ValueError("ties must be None, 'repeat' or 'zero'")
-        keep = torch.rand((cache.batch, ctx, 1), generator=g, device=dev) < (0.02 if ties == "repeat" else 0.005)
+        keep = torch.rand((cache.batch, ctx, 1), generator=g, device=dev) < (0.0 if ties == "repeat" else 0.005)
         ik = ik * keep
         if ties == "repeat":
             src = torch.randn((cache.batch, 64, di), generator=g, device=dev)
