@@ -31,7 +31,8 @@ EXPORTS = ("cb_abi_version", "cb_status_string", "cb_nvfp4_quantize", "cb_nvfp4_
            "cb_embed", "cb_argmax", "cb_gdn_step", "cb_indexer_topk", "cb_workspace_bytes", "cb_forward",
            "cb_read_status", "cb_clear_status", "cb_launch_count", "cb_indexer_topk_noalloc", "cb_read_trace",
            "cb_verify_gemm_nvfp4", "cb_gdn_chunk_prefill", "cb_set_wait_limit",
-           "cb_workspace_layout")
+           "cb_workspace_layout", "cb_nvfp4_slice_bytes", "cb_nvfp4_pack_slices", "cb_prompt_lookup_draft",
+           "cb_spec_accept", "cb_mtp_workspace_bytes", "cb_mtp_draft")
 
 P = C.c_void_p
 I32 = C.c_int32
@@ -41,15 +42,20 @@ class CbMatrix(C.Structure):
     _fields_ = [("tiles", P), ("tile_scale", P), ("rows", I32), ("k", I32)]
 
 
+class CbSliced(C.Structure):
+    _fields_ = [("data", P), ("tensor_scale", P), ("rows", I32), ("k", I32), ("width", I32)]
+
+
 class CbSelfLayer(C.Structure):
     _fields_ = [("kind", I32), ("slot", I32), ("norm1", P), ("norm2", P), ("in_proj", CbMatrix),
                 ("o_proj", CbMatrix), ("gate_up", CbMatrix), ("down", CbMatrix), ("conv_w", P), ("A_log", P),
-                ("dt_bias", P), ("o_norm", P), ("q_norm", P), ("k_norm", P)]
+                ("dt_bias", P), ("o_norm", P), ("q_norm", P), ("k_norm", P), ("o_proj_ks", CbSliced),
+                ("down_ks", CbSliced)]
 
 
 class CbCrossLayer(C.Structure):
     _fields_ = [("norm1", P), ("norm2", P), ("q_gate", CbMatrix), ("o_proj", CbMatrix), ("gate_up", CbMatrix),
-                ("down", CbMatrix), ("q_norm", P)]
+                ("down", CbMatrix), ("q_norm", P), ("down_ks", CbSliced)]
 
 
 class CbModel(C.Structure):
@@ -73,10 +79,15 @@ class CbModel(C.Structure):
     ]
 
 
+class CbMtp(C.Structure):
+    _fields_ = [("norm_h", P), ("norm_e", P), ("ffn_norm", P), ("proj", CbMatrix), ("gate_up", CbMatrix),
+                ("down", CbMatrix), ("draft_head", CbMatrix), ("draft_ids", P), ("n_draft", I32)]
+
+
 class CbCache(C.Structure):
     _fields_ = [("batch", I32), ("max_ctx", I32), ("swa_slots", I32), ("n_gdn", I32), ("n_swa", I32),
                 ("pos", P), ("gdn_state", P), ("gdn_conv", P), ("swa_k", P), ("swa_v", P), ("kv_k", P),
-                ("kv_v", P), ("kv_ik", P)]
+                ("kv_v", P), ("kv_ik", P), ("snap_state", P), ("snap_conv", P)]
 
 
 class CbWorkspaceLayout(C.Structure):
@@ -104,6 +115,9 @@ def lib() -> C.CDLL:
         L.cb_status_string.argtypes = [C.c_int]
         L.cb_nvfp4_quantize.argtypes = [P, I32, I32, C.c_float, P, P, P]
         L.cb_nvfp4_pack_tiles.argtypes = [P, P, I32, I32, P, P]
+        L.cb_nvfp4_slice_bytes.restype = C.c_int64
+        L.cb_nvfp4_slice_bytes.argtypes = [I32, I32]
+        L.cb_nvfp4_pack_slices.argtypes = [P, P, I32, I32, I32, P, P]
         L.cb_gemv_nvfp4.argtypes = [C.POINTER(CbMatrix), P, I32, I32, P, I32, I32, P]
         L.cb_verify_gemm_nvfp4.argtypes = [C.POINTER(CbMatrix), P, I32, I32, P, I32, I32, P, P]
         L.cb_gdn_chunk_prefill.argtypes = [P, P, P, P, P, I32, I32, I32, I32, I32, C.c_float, P, P, P]
@@ -116,6 +130,11 @@ def lib() -> C.CDLL:
         L.cb_workspace_bytes.argtypes = [C.POINTER(CbModel), I32, I32, I32]
         L.cb_forward.argtypes = [C.POINTER(CbModel), C.POINTER(CbCache), P, C.c_size_t, P, I32, I32, P, P, P, P]
         L.cb_read_status.argtypes = [P, C.POINTER(I32), P]
+        L.cb_mtp_workspace_bytes.restype = C.c_size_t
+        L.cb_mtp_workspace_bytes.argtypes = [C.POINTER(CbModel), C.POINTER(CbMtp)]
+        L.cb_mtp_draft.argtypes = [C.POINTER(CbModel), C.POINTER(CbMtp), P, P, I32, P, P, C.c_size_t, P]
+        L.cb_prompt_lookup_draft.argtypes = [P, I32, P, P, I32, I32, I32, I32, P, I32, P, P]
+        L.cb_spec_accept.argtypes = [C.POINTER(CbModel), C.POINTER(CbCache), P, P, P, I32, P, I32, P, P, P, P]
         L.cb_clear_status.argtypes = [P, P]
         L.cb_set_wait_limit.argtypes = [P, C.c_uint64, I32, P]
         L.cb_workspace_layout.argtypes = [C.POINTER(CbModel), I32, I32, I32, C.POINTER(CbWorkspaceLayout)]
@@ -123,9 +142,10 @@ def lib() -> C.CDLL:
         L.cb_launch_count.restype = C.c_int64
         L.cb_launch_count.argtypes = []
         for name in EXPORTS:
-            if name not in ("cb_status_string", "cb_workspace_bytes", "cb_launch_count"):
+            if name not in ("cb_status_string", "cb_workspace_bytes", "cb_launch_count", "cb_nvfp4_slice_bytes",
+                            "cb_mtp_workspace_bytes"):
                 getattr(L, name).restype = C.c_int
-        if L.cb_abi_version() != 2:
+        if L.cb_abi_version() != 3:
             raise CbError("libcirrus_b200.so ABI version mismatch")
         _lib = L
     return _lib

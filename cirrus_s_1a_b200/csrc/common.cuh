@@ -21,6 +21,13 @@ void count_launch();
 int ensure_smem_attr(const void* fn, int bytes);
 int resident_ctas(const void* fn, int threads, int smem_bytes);
 int num_sms();
+// Clusters of `cluster` CTAs of a kernel that fit on the current device at once
+// (cudaOccupancyMaxActiveClusters, cached per kernel and device; 0 on error).
+int resident_clusters(const void* fn, int threads, int smem_bytes, int cluster);
+// Whether a cooperative launch may carry a cluster dimension on the current
+// device (true until a launch of that form has been refused there).
+bool cooperative_clusters_ok();
+void note_cooperative_clusters_refused();
 
 constexpr int kTileRows = CB_TILE_ROWS;
 constexpr int kWarp = 32;

@@ -1,27 +1,38 @@
-// Persistent decode kernel: one cooperative launch runs a whole forward chunk
-// of M = batch * T <= 8 rows (a tau=1 decode step, or a verify of 1 + draft
-// tokens) with every CTA resident, walking the model layer by layer.
+// Persistent decode kernel: one launch runs a whole forward chunk of
+// M = batch * T <= 8 rows (a tau=1 decode step, or a verify of 1 + draft
+// tokens), with every CTA resident, walking the model phase by phase.
 //
-// Phases (each followed by a grid barrier):
-//   self layer:  in-proj GEMV (norm1 fused; layer 0 gathers the embedding)
-//                -> GDN heads | SWA (q/k norm + RoPE + ring append + split
-//                   attention partials)
-//                -> o-proj GEMV (+ residual; after SWA its input staging merges
-//                   the split partials and applies the output gate)
-//                -> gate_up GEMV producing silu(g)*u
-//                -> down GEMV (+ residual)
-//   shared KV:   projection GEMV -> K/V/indexer-key append + indexer scores with
-//                a 2048-bin histogram of the score keys -> threshold bin and
-//                compaction -> exact selection (one CTA per query row, run
-//                alongside the first cross layer's q GEMV)
-//   cross layer: q|gate GEMV -> selected-key attention (split partials)
-//                -> o-proj (merging the partials) -> gate_up -> down
-//   head:        LM-head GEMV (final norm fused) with a per-row argmax
-// Each GEMV's first weight rows are copied to shared memory between the
-// arrival at the barrier before it and the wait there; there is no separate
-// L2 prefetch (measured: it costs more in issue and queueing than it saves).
-// Every wait is bounded
-// (%globaltimer); on timeout the launch sets CB_ERR_TIMEOUT and all CTAs exit.
+// The grid is a set of 8-CTA thread-block clusters.  Phases, each ended by a
+// grid barrier (bounded waits on one monotonic counter):
+//   GDN layer:  [mixer]  one cluster per head: in-projection rows of the head
+//                        (2 tiles per CTA) -> distributed shared memory ->
+//                        short conv, L2 norms, decay / beta -> the recurrence on
+//                        the CTA's Dv/8 value columns -> gated RMSNorm (sums of
+//                        squares exchanged in the cluster) -> split-K o-projection
+//                        on the CTA's columns -> partials summed in the cluster
+//                        -> added to the residual stream
+//               [FFN]    split K: each CTA one 16-wide slice of the hidden layer
+//                        (its gate and up tiles, SwiGLU, the matching 16 columns
+//                        of the down projection) -> partials summed in the cluster
+//                        -> added to the residual stream
+//   SWA layer:  in-projection GEMV -> split attention over the window ring ->
+//               o-projection (merging the split partials) -> FFN
+//   shared KV:  projection GEMV -> K/V/indexer-key append + indexer scores with a
+//               2048-bin histogram -> threshold bin + compaction -> exact
+//               selection (one CTA per query row, beside the first q GEMV)
+//   cross layer: q|gate GEMV -> selected-key attention -> o-projection -> FFN
+//   head:       LM-head GEMV (final norm fused) with a per-row argmax
+//
+// The residual streams are kept in 64-bit fixed point (value * 2^32) and every
+// update is an integer atomic add, so the split-K sums are exact and the
+// result does not depend on the order in which CTAs finish.  Each phase's
+// weights are staged into one of two shared-memory slots by bulk copies
+// (cp.async.bulk, completion on an mbarrier) issued one phase ahead.
+//
+// Every wait is bounded (%globaltimer): on timeout a CTA sets CB_ERR_TIMEOUT and
+// an abort bit in the barrier counter; from then on every CTA skips the work
+// but still takes its cluster barriers, so no CTA is left waiting for a
+// cluster peer, and the launch ends without advancing the cache.
 #include <algorithm>
 #include <type_traits>
 
@@ -33,22 +44,43 @@ namespace cb {
 namespace {
 
 constexpr int kT = kMkThreads;
-constexpr int kW = kMkThreads / 32;
-constexpr int kSmem = 160 * 1024;
+constexpr int kW = kMkThreads / 32;   // 16 warps: one per row of a weight tile
+constexpr int kCl = kMkCluster;
+constexpr int kSlot = kMkSlotBytes;
+constexpr int kWork = kMkWorkBytes;
+// Parameter region at the end of the work area: each phase's small operands
+// (norm vector, tile and tensor scales, gate constants, conv taps and windows)
+// are copied here between the arrival at the barrier before the phase and the
+// wait there.  No other CTA writes it, and no phase that needs parameters
+// uses it as scratch.
+constexpr int kPreOff = kWork - 21 * 1024;
+constexpr int kParNorm = 0;                      // [kMkMaxD] norm vector
+constexpr int kParSmall = kMkMaxD;               // [64] scales and constants
+constexpr int kParConv = kMkMaxD + 80;           // conv taps [NC][4], then windows [B][3][NC]
+constexpr int kParTs = 48;                       // tile scales held for the first 48 units of a GEMV
+enum { PS_A_LOG = 48, PS_DT_BIAS = 49, PS_TSCALE = 50, PS_O_NORM = 52 };  // indices in the small block (80)
+constexpr int kMarkBase = 256;                   // trace entries kMarkBase + 4 p + i: sub-phase marks of CTA 0
+constexpr int kSmem = 2 * kSlot + kWork;
 constexpr int kMaxSort = 4096;
 constexpr int kMkBitmapWords = 4096;  // selection bitmap: up to 131072 keys
+constexpr int kMaxPhases = 4 * CB_MAX_SELF + 4 * CB_MAX_CROSS + 8;
+constexpr unsigned kAbortBit = 1u << 30;
+constexpr float kFix = 4294967296.0f;              // 2^32
+constexpr float kFixInv = 2.3283064365386963e-10f;  // 2^-32
 
 enum { PRE_NONE_ = 0, PRE_RMS_ = 1, PRE_EMBED_ = 2, PRE_COMBINE_ = 3 };
-enum { EPI_STORE_ = 0, EPI_ADD_ = 1, EPI_ACT_ = 2 };
+enum { EPI_STORE_ = 0, EPI_RED_ = 1 };
+enum : int {
+  PH_GDN = 0, PH_FFN_SELF, PH_SWA_IN, PH_SWA_ATT, PH_SWA_O, PH_SH_PROJ, PH_SH_SCORE, PH_SH_COMPACT, PH_CR_Q,
+  PH_CR_ATT, PH_CR_O, PH_FFN_CROSS, PH_LM_HEAD
+};
 
-// ------------------------------------------------------------------ sync
+// ------------------------------------------------------------------ timers, sync
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-
-__device__ __forceinline__ int ld_volatile_i32(const int32_t* p) { return *(volatile const int32_t*)p; }
 
 __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
@@ -56,15 +88,27 @@ __device__ __forceinline__ unsigned long long gtimer() {
   return t;
 }
 
-// Grid barrier on a monotonic arrival counter, split in two: grid_arrive
-// publishes this CTA's writes and counts it in; grid_wait waits for every CTA.
-// Work that does not depend on the other CTAs' writes (the next phase's
-// weight loads) goes between the two.  grid_wait returns false when the launch
-// must stop (this CTA's wait timed out, or another CTA's did).
 // Per-CTA copy of the launch's wait limit and stall hook (thread 0 reads them at start).
 __shared__ unsigned long long s_wait_limit;
 __shared__ unsigned s_stall_barrier;
 
+__shared__ int s_mark_base;  // trace entry of this phase's first sub-phase mark
+
+// %globaltimer at a point inside the current phase (CTA 0 only; i < 4).
+__device__ __forceinline__ void mark(const MkArgs& a, int i) {
+  if (blockIdx.x == 0 && threadIdx.x == 0 && s_mark_base + i < kMkTrace) a.trace[s_mark_base + i] = gtimer();
+}
+
+__device__ __forceinline__ void raise_abort(const MkArgs& a) {
+  atomicOr(a.sync, kAbortBit);
+  atomicCAS(a.status, 0, CB_ERR_TIMEOUT);
+}
+
+// Grid barrier on a monotonic arrival counter, split in two: grid_arrive
+// publishes this CTA's writes and counts it in; grid_wait waits for every CTA.
+// Work that does not depend on the other CTAs' writes (the next phase's weight
+// copies, recurrent state) goes between the two.  The abort bit in the counter
+// ends every wait at once; grid_wait returns false when the launch is aborted.
 __device__ __forceinline__ void grid_arrive(const MkArgs& a, unsigned& gen) {
   __syncthreads();
   gen += 1;
@@ -82,18 +126,17 @@ __device__ __forceinline__ bool grid_wait(const MkArgs& a, unsigned gen, int* s_
     int ok = 1;
     const unsigned long long t0 = gtimer();
     unsigned spin = 0;
-    while (ld_acquire_u32(a.sync) < target) {
-      if ((++spin & 127) == 0) {
-        if (ld_volatile_i32(a.abort_flag)) {
-          ok = 0;
-          break;
-        }
-        if (gtimer() - t0 > s_wait_limit) {
-          atomicExch(a.abort_flag, 1);
-          atomicCAS(a.status, 0, CB_ERR_TIMEOUT);
-          ok = 0;
-          break;
-        }
+    for (;;) {
+      const unsigned v = ld_acquire_u32(a.sync);
+      if (v & kAbortBit) {
+        ok = 0;
+        break;
+      }
+      if (v >= target) break;
+      if ((++spin & 63) == 0 && gtimer() - t0 > s_wait_limit) {
+        raise_abort(a);
+        ok = 0;
+        break;
       }
     }
     if (blockIdx.x == 0 && 2 * gen < (unsigned)kMkTrace) a.trace[2 * gen] = gtimer();
@@ -103,45 +146,85 @@ __device__ __forceinline__ bool grid_wait(const MkArgs& a, unsigned gen, int* s_
   return *s_ok != 0;
 }
 
-__device__ __forceinline__ bool grid_sync(const MkArgs& a, unsigned& gen, int* s_ok) {
-  grid_arrive(a, gen);
-  return grid_wait(a, gen, s_ok);
+// ------------------------------------------------------------------ clusters
+__device__ __forceinline__ unsigned cluster_rank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ unsigned cluster_index() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+// Cluster barrier: orders this CTA's shared-memory stores to the cluster's CTAs
+// before every CTA's later reads.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+// Address of the same shared-memory location in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t dsmem(const void* p, unsigned rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_dsmem(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 
-// Asynchronous global -> shared copies (no registers held while they fly)
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+// ------------------------------------------------------------------ bulk copies
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_arrive(unsigned long long* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(unsigned long long* bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for an mbarrier phase (every thread waits, so every thread sees the copied bytes).
+__device__ __forceinline__ bool mbar_wait(unsigned long long* bar, unsigned parity) {
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long t0 = gtimer();
+  while (!mbar_try(bar, parity))
+    if (gtimer() - t0 > s_wait_limit) return false;
+  return true;
+}
+// Global -> this CTA's shared memory, completion counted on `bar` (16-byte aligned, size % 16 == 0).
+__device__ __forceinline__ void bulk_copy(void* dst, const void* src, unsigned bytes, unsigned long long* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
 }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Asynchronous global -> shared copies of small pieces (no registers held while they fly)
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
 __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
-               : "memory");
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
 
-// ------------------------------------------------------------------ GEMV
-struct GemvJob {
-  CbMatrix W;
-  const float* x;
-  int ldx;
-  int xmap_nq, xmap_T, xmap_off;  // x row of m = (m / nq) * T + off + m % nq when xmap_nq > 0
-  int pre;
-  const float* norm_w;
-  float* y;
-  int ldy, rows_out, epi;
-  float* copy_x;                  // local CTA 0 stores the raw input rows here ([m][K])
-  bool argmax;
-  // PRE_COMBINE: the input is the gated merge of split-softmax attention
-  // partials, part[((m * H + h) * S + s) * (hd + 2)] = (max, sum, o[hd]), with
-  // the output gate sigmoid(gate_x[m * gate_ld + gate_off + h])
-  const float* part;
-  int S, hd;
-  const float* gate_x;
-  int gate_ld, gate_off;
-};
+// ------------------------------------------------------------------ fixed point
+__device__ __forceinline__ float from_fix(long long q) { return __ll2float_rn(q) * kFixInv; }
+__device__ __forceinline__ void red_fix(long long* p, float v) {
+  const unsigned long long q = (unsigned long long)__float2ll_rn(v * kFix);
+  asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(q) : "memory");
+}
 
+// ------------------------------------------------------------------ weight rows
 // One weight row as seen by one lane: the 8-code chunks lane, lane+32, ...
 // (K <= 2048, so at most 8 chunks), code words and scale bytes.
 template <int NU>
@@ -150,18 +233,24 @@ struct RowW {
   uint32_t s[NU];
 };
 
+// Row `w` of a 16-row tile (codes of the 16 rows, then their scales), in shared
+// or global memory.
 template <int NU>
-__device__ __forceinline__ void load_row(const CbMatrix& W, int64_t tb, int K, int row, bool valid, RowW<NU>& r) {
+__device__ __forceinline__ void tile_row(const uint8_t* tile, int K, int w, bool valid, bool global, RowW<NU>& r) {
   const int lane = threadIdx.x & 31, kc = K >> 3;
-  const uint8_t* t = W.tiles + (int64_t)(row >> 4) * tb;
-  const uint32_t* cw = reinterpret_cast<const uint32_t*>(t + (row & 15) * (K / 2));
-  const uint8_t* sb = t + kTileRows * (K / 2) + (row & 15) * (K / 16);
+  const uint32_t* cw = reinterpret_cast<const uint32_t*>(tile + w * (K / 2));
+  const uint8_t* sb = tile + kTileRows * (K / 2) + w * (K / 16);
 #pragma unroll
   for (int u = 0; u < NU; ++u) {
     const int c = u * 32 + lane;
     const bool ok = valid && c < kc;
-    r.w[u] = ok ? __ldg(cw + c) : 0u;
-    r.s[u] = ok ? (uint32_t)__ldg(sb + (c >> 1)) : 0u;
+    if (global) {
+      r.w[u] = ok ? __ldg(cw + c) : 0u;
+      r.s[u] = ok ? (uint32_t)__ldg(sb + (c >> 1)) : 0u;
+    } else {
+      r.w[u] = ok ? cw[c] : 0u;
+      r.s[u] = ok ? (uint32_t)sb[c >> 1] : 0u;
+    }
   }
 }
 
@@ -194,171 +283,160 @@ __device__ __forceinline__ void dot_row(const RowW<NU>& r, int K, const float* x
   }
 }
 
+// Dot products of one tile row with the M staged input rows: acc[m] holds the
+// warp-reduced sum on every lane.
+template <int M>
+__device__ __forceinline__ void row_dot(const uint8_t* tile, int K, int w, bool valid, bool global, const float* xs,
+                                        float (&acc)[M]) {
+#pragma unroll
+  for (int m = 0; m < M; ++m) acc[m] = 0.0f;
+  if (K <= 768) {
+    RowW<3> r;
+    tile_row<3>(tile, K, w, valid, global, r);
+    dot_row<M, 3>(r, K, xs, acc);
+  } else {
+    RowW<8> r;
+    tile_row<8>(tile, K, w, valid, global, r);
+    dot_row<M, 8>(r, K, xs, acc);
+  }
+#pragma unroll
+  for (int m = 0; m < M; ++m) acc[m] = warp_sum(acc[m]);
+}
+
 __device__ __forceinline__ unsigned long long pack_argmax(float v, int idx) {
   return ((unsigned long long)score_key(v) << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)idx);
 }
 
-// Rows of unit u for this warp: ACT pairs gate row ra with up row rb; the
-// other epilogues pair units u and u + ncta (rb valid when hb).
-__device__ __forceinline__ void gemv_rows(const GemvJob& g, int units, int ncta, int u, int& ra, int& rb, bool& hb) {
-  const int warp = threadIdx.x >> 5;
-  if (g.epi == EPI_ACT_) {
-    ra = u * kTileRows + warp;
-    rb = g.W.rows / 2 + u * kTileRows + warp;
-    hb = true;
-  } else {
-    const int ub = u + ncta;
-    ra = u * kTileRows + warp;
-    hb = ub < units;
-    rb = ub * kTileRows + warp;
-  }
-}
-
-__device__ __forceinline__ int gemv_units(const GemvJob& g) {
-  return g.epi == EPI_ACT_ ? g.W.rows / 32 : g.W.rows / kTileRows;
-}
-
-// The first unit's weights and, for a residual add, the old outputs: they do
-// not depend on the previous phase, so they are fetched between the arrival at
-// its barrier and the wait there.  The weight rows go by asynchronous copies
-// into a per-warp shared-memory slot at kPreOff (two rows of codes + scales),
-// so no registers stay live across the barrier; the residuals are registers.
-constexpr int kPreOff = 96 * 1024;
-__host__ __device__ constexpr int pre_row_bytes(int K) { return ((9 * K / 16) + 15) & ~15; }
-static_assert(kPreOff + kW * 2 * pre_row_bytes(2048) <= kSmem, "preload slots exceed the scratch");
-
+// ------------------------------------------------------------------ RMSNorm staging
+// xs[m][k] = x[m][k] * norm_w[k] for m < m_rows (zeros above); rn[m] receives
+// the RMSNorm factor of each row (1 when norm_w is null).  x comes from a
+// fixed-point residual row (xq, row rowmap[m]), float rows (x) or the token
+// embeddings (embed_from).  The sums of squares are reduced in a fixed order.
 template <int M>
-struct GemvPre {
-  float resa[M], resb[M];
-};
-
-// The copies move 16-byte code chunks and 4-byte scale chunks: K % 64 == 0.
-// Other K load the first unit directly after the barrier.
-__device__ __forceinline__ bool pre_staged(int K) { return K % 64 == 0; }
-
-__device__ __forceinline__ uint8_t* pre_slot(float* smem, int K) {
-  return reinterpret_cast<uint8_t*>(smem) + kPreOff + (threadIdx.x >> 5) * 2 * pre_row_bytes(K);
-}
-
-__device__ __forceinline__ void pre_copy_row(const CbMatrix& W, int K, int row, uint8_t* dst) {
-  const int lane = threadIdx.x & 31;
-  const uint8_t* t = W.tiles + (int64_t)(row >> 4) * tile_bytes(K);
-  const uint8_t* codes = t + (row & 15) * (K / 2);
-  const uint8_t* sc = t + kTileRows * (K / 2) + (row & 15) * (K / 16);
-  for (int i = lane; i < K / 32; i += 32) cp_async16(dst + 16 * i, codes + 16 * i);
-  for (int i = lane; i < K / 64; i += 32) cp_async4(dst + K / 2 + 4 * i, sc + 4 * i);
-}
-
-// The lane's view of a preloaded row (the layout load_row produces).
-template <int NU>
-__device__ __forceinline__ void pre_read_row(const uint8_t* src, int K, bool valid, RowW<NU>& r) {
-  const int lane = threadIdx.x & 31, kc = K >> 3;
-  const uint32_t* cw = reinterpret_cast<const uint32_t*>(src);
-#pragma unroll
-  for (int u = 0; u < NU; ++u) {
-    const int c = u * 32 + lane;
-    const bool ok = valid && c < kc;
-    r.w[u] = ok ? cw[c] : 0u;
-    r.s[u] = ok ? (uint32_t)src[K / 2 + (c >> 1)] : 0u;
-  }
-}
-
-template <int M>
-__device__ __forceinline__ void gemv_pre(const GemvJob& g, int m_rows, int cta, int ncta, float* smem,
-                                         GemvPre<M>& p) {
-  const int units = gemv_units(g);
-  if (cta < 0 || cta >= units || ncta <= 0) return;
-  const int K = g.W.k, lane = threadIdx.x & 31;
-  int ra, rb;
-  bool hb;
-  gemv_rows(g, units, ncta, cta, ra, rb, hb);
-  if (pre_staged(K)) {
-    uint8_t* slot = pre_slot(smem, K);
-    pre_copy_row(g.W, K, ra, slot);
-    if (hb) pre_copy_row(g.W, K, rb, slot + pre_row_bytes(K));
-  }
-#pragma unroll
-  for (int mr = 0; mr < M; ++mr) {
-    p.resa[mr] = p.resb[mr] = 0.0f;
-    if (g.epi == EPI_ADD_ && lane == 0 && mr < m_rows) {
-      if (ra < g.rows_out) p.resa[mr] = __ldcg(g.y + (int64_t)mr * g.ldy + ra);
-      if (hb && rb < g.rows_out) p.resb[mr] = __ldcg(g.y + (int64_t)mr * g.ldy + rb);
-    }
-  }
-}
-
-template <int M>
-__device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int cta, int ncta, float* smem,
-                           GemvPre<M>& p) {
-  const int units = gemv_units(g);
-  if (cta < 0 || cta >= units || ncta <= 0) return;
-  const int K = g.W.k, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float* xs = smem;  // [M][K]
-  __shared__ unsigned long long s_best[kMkMaxRows];
-  const int64_t tb = tile_bytes(K);
-  const int step = g.epi == EPI_ACT_ ? ncta : 2 * ncta;
-  auto rows_of = [&](int u, int& ra, int& rb, bool& hb) { gemv_rows(g, units, ncta, u, ra, rb, hb); };
-  cp_async_wait_all();  // this warp's preloaded rows (read after the staging barrier)
-  float(&resa)[M] = p.resa;
-  float(&resb)[M] = p.resb;
-  auto load_res = [&](int ra, int rb, bool hb) {
-#pragma unroll
-    for (int mr = 0; mr < M; ++mr) {
-      resa[mr] = resb[mr] = 0.0f;
-      if (g.epi == EPI_ADD_ && lane == 0 && mr < m_rows) {
-        if (ra < g.rows_out) resa[mr] = __ldcg(g.y + (int64_t)mr * g.ldy + ra);
-        if (hb && rb < g.rows_out) resb[mr] = __ldcg(g.y + (int64_t)mr * g.ldy + rb);
-      }
-    }
-  };
-
-  // Stage pre(x) = x * norm_w (RMSNorm's per-row scale is applied to the dot
-  // products at the end); the sum of squares of each row is reduced on the way.
-  __shared__ float wsq[kW][kMkMaxRows];  // per-warp partial sums of squares (summed in a fixed order)
-  if (g.argmax && tid < kMkMaxRows) s_best[tid] = 0ull;
-  __syncthreads();
-  const bool norm = g.pre == PRE_RMS_ || g.pre == PRE_EMBED_;
-  const bool copy = g.copy_x != nullptr && cta == 0;
+__device__ void stage_rows(const long long* xq, const float* x, int ldx, const int* rowmap, int m_rows, int K,
+                           const float* norm_w, float eps, float* xs, float (&rn)[M], long long* copy_q,
+                           long long* embed_add, const MkArgs* embed_from) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  __shared__ float wsq[kW][kMkMaxRows];
   float sq[M];
 #pragma unroll
-  for (int mr = 0; mr < M; ++mr) sq[mr] = 0.0f;
-  if (g.pre == PRE_EMBED_) {
-    const CbMatrix& E = a.m.lm_head;
-    const int64_t etb = tile_bytes(K);
-    for (int i = tid; i < M * (K / 2); i += kT) {
-      const int mr = i / (K / 2), j = i - mr * (K / 2);
-      float v0 = 0.0f, v1 = 0.0f;
-      if (mr < m_rows) {
+  for (int m = 0; m < M; ++m) sq[m] = 0.0f;
+  const bool norm = norm_w != nullptr;
+  for (int i = tid; i < M * K; i += kT) {
+    const int mr = i / K, k = i - mr * K;
+    float v = 0.0f;
+    if (mr < m_rows) {
+      if (embed_from) {  // the token's embedding row (tied with the LM head, gathered from its tiles)
+        const MkArgs& a = *embed_from;
+        const CbMatrix& E = a.m.lm_head;
         const int b = mr / a.T, t = mr - b * a.T;
         const int64_t id = a.ids[(int64_t)b * a.ids_ld + a.c0 + t];
         if (id >= 0 && id < a.m.vocab_size) {
-          const uint8_t* tile = E.tiles + (id >> 4) * etb;
+          const uint8_t* tile = E.tiles + (id >> 4) * tile_bytes(K);
           const int rr = (int)(id & 15);
-          const float2 f = e2m1x2_to_f32x2(tile[rr * (K / 2) + j]);
-          const float s = e4m3_to_f32(tile[kTileRows * (K / 2) + rr * (K / 16) + (j >> 3)]);
-          const float ts = E.tile_scale[id >> 4];
-          v0 = (f.x * s) * ts;
-          v1 = (f.y * s) * ts;
-        } else if (j == 0) {
+          const float2 f = e2m1x2_to_f32x2(tile[rr * (K / 2) + (k >> 1)]);
+          const float s = e4m3_to_f32(tile[kTileRows * (K / 2) + rr * (K / 16) + (k >> 4)]);
+          v = ((k & 1 ? f.y : f.x) * s) * E.tile_scale[id >> 4];
+        } else if (k == 0) {
           set_status(a.status, CB_ERR_TOKEN);
         }
+        if (embed_add) red_fix(embed_add + (int64_t)mr * K + k, v);
+      } else {
+        const int xr = rowmap ? rowmap[mr] : mr;
+        if (xq) {
+          const long long q = __ldcg(xq + (int64_t)xr * ldx + k);
+          v = from_fix(q);
+          if (copy_q) copy_q[(int64_t)mr * ldx + k] = q;
+        } else {
+          v = __ldcg(x + (int64_t)xr * ldx + k);
+        }
       }
-      if (copy && mr < m_rows) {
-        g.copy_x[mr * K + 2 * j] = v0;
-        g.copy_x[mr * K + 2 * j + 1] = v1;
-      }
+    }
+    if (norm) {
 #pragma unroll
       for (int q = 0; q < M; ++q)
-        if (q == mr) sq[q] += v0 * v0 + v1 * v1;
-      xs[mr * K + 2 * j] = v0 * g.norm_w[2 * j];
-      xs[mr * K + 2 * j + 1] = v1 * g.norm_w[2 * j + 1];
+        if (q == mr) sq[q] += v * v;
+      v *= norm_w[k];
     }
-  } else if (g.pre == PRE_COMBINE_) {
+    xs[i] = v;
+  }
+  if (norm) {
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const float t = warp_sum(sq[m]);
+      if (lane == 0) wsq[warp][m] = t;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    rn[m] = 1.0f;
+    if (norm) {
+      float t = 0.0f;
+      for (int w = 0; w < kW; ++w) t += wsq[w][m];
+      rn[m] = rsqrtf(t / (float)K + eps);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ GEMV over tiles
+struct GemvJob {
+  CbMatrix W;
+  const long long* xq;  // fixed-point input rows (or null)
+  const float* x;       // float input rows (when xq is null)
+  int ldx;
+  int xmap_nq, xmap_T, xmap_off;  // input row of m = (m / nq) * T + off + m % nq when xmap_nq > 0
+  int pre;
+  const float* norm_w;
+  float* y;             // EPI_STORE_
+  long long* yq;        // EPI_RED_: y is added to this fixed-point stream
+  int ldy, rows_out, epi;
+  long long* copy_q;    // the first CTA of the phase copies the (mapped) fixed-point input rows here
+  bool argmax;
+  // PRE_COMBINE_: the input is the gated merge of split-softmax attention
+  // partials, part[((m * H + h) * S + s) * (hd + 2)] = (max, sum, o[hd]), with
+  // the output gate sigmoid(gate_x[m * gate_ld + gate_off + h])
+  const float* part;
+  int S, hd;
+  const float* gate_x;
+  int gate_ld, gate_off;
+  int ucta, uncta;      // this CTA's index among the phase's CTAs and their count (units ucta + i * uncta)
+};
+
+__device__ __forceinline__ int gemv_mine(const GemvJob& g) {
+  const int units = g.W.rows / kTileRows;
+  if (g.ucta < 0 || g.ucta >= units || g.uncta <= 0) return 0;
+  return (units - 1 - g.ucta) / g.uncta + 1;
+}
+__device__ __forceinline__ int gemv_staged(const GemvJob& g) {
+  return min(gemv_mine(g), (int)(kSlot / tile_bytes(g.W.k)));
+}
+
+__device__ __forceinline__ float* par_norm(float* work) { return work + kPreOff / 4 + kParNorm; }
+__device__ __forceinline__ float* par_small(float* work) { return work + kPreOff / 4 + kParSmall; }
+
+template <int M>
+__device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, const uint8_t* slot, float* work) {
+  const int n_mine = gemv_mine(g);
+  if (n_mine == 0) return;
+  const float* ps = par_small(work);
+  const int K = g.W.k, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t tb = tile_bytes(K);
+  const int nst = gemv_staged(g);
+  float* xs = work;  // [M][K]
+  __shared__ unsigned long long s_best[kMkMaxRows];
+  __shared__ int s_rowmap[kMkMaxRows];
+  if (g.argmax && tid < kMkMaxRows) s_best[tid] = 0ull;
+  if (tid < kMkMaxRows)
+    s_rowmap[tid] = g.xmap_nq > 0 ? (tid / g.xmap_nq) * g.xmap_T + g.xmap_off + tid % g.xmap_nq : tid;
+  __syncthreads();
+  float rn[M];
+  if (g.pre == PRE_COMBINE_) {
     // Merge the S <= 32 split partials of every (row, head): a warp per pair,
     // a lane per split: w_s = exp(m_s - max m), coef_s = w_s * gate / sum_s w_s l_s;
     // then x = sum_s coef_s o_s with the loads of 8 splits in flight at a time.
     const int hd = g.hd, H = K / hd, S = g.S, per = hd + 2;
-    float* coef = smem + M * K;  // [M][H][32]
+    float* coef = work + M * K;  // [M][H][32]
     for (int i = warp; i < m_rows * H; i += kW) {
       const int mr = i / H, h = i - mr * H;
       const float* pb = g.part + (int64_t)i * S * per + lane * per;
@@ -375,10 +453,10 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
       const int mr = i / K, k = i - mr * K;
       float v = 0.0f;
       if (mr < m_rows) {
-        const int h = k / hd, d = k - h * hd;
-        const float* pb = g.part + (int64_t)(mr * H + h) * S * per + 2 + d;
+        const int h = k / hd, dd = k - h * hd;
+        const float* pb = g.part + (int64_t)(mr * H + h) * S * per + 2 + dd;
         const float* cf = coef + (mr * H + h) * 32;
-        for (int s0 = 0; s0 < S; s0 += 8) {  // 8 loads in flight per batch
+        for (int s0 = 0; s0 < S; s0 += 8) {
           float o[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) o[e] = s0 + e < S ? __ldcg(pb + (s0 + e) * per) : 0.0f;
@@ -388,97 +466,53 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
       }
       xs[i] = v;
     }
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < M; ++m) rn[m] = 1.0f;
   } else {
-#pragma unroll 4
-    for (int i = tid; i < M * K; i += kT) {
-      const int mr = i / K, k = i - mr * K;
-      float v = 0.0f;
-      if (mr < m_rows) {
-        const int xr = g.xmap_nq > 0 ? (mr / g.xmap_nq) * g.xmap_T + g.xmap_off + mr % g.xmap_nq : mr;
-        v = __ldcg(g.x + (int64_t)xr * g.ldx + k);
-        if (copy) g.copy_x[mr * K + k] = v;
-      }
-      if (norm) {
-#pragma unroll
-        for (int q = 0; q < M; ++q)
-          if (q == mr) sq[q] += v * v;
-        v *= g.norm_w[k];
-      }
-      xs[i] = v;
-    }
+    const bool first = g.ucta == 0;
+    stage_rows<M>(g.xq, g.x, g.ldx, s_rowmap, m_rows, K, g.pre == PRE_NONE_ ? nullptr : par_norm(work), a.m.norm_eps,
+                  xs, rn, first ? g.copy_q : nullptr, (g.pre == PRE_EMBED_ && first) ? a.hq : nullptr,
+                  g.pre == PRE_EMBED_ ? &a : nullptr);
   }
-  if (norm) {
-#pragma unroll
-    for (int mr = 0; mr < M; ++mr) {
-      const float t = warp_sum(sq[mr]);
-      if (lane == 0) wsq[warp][mr] = t;
-    }
-  }
-  __syncthreads();
-  float rn[M];
-#pragma unroll
-  for (int mr = 0; mr < M; ++mr) {
-    rn[mr] = 1.0f;
-    if (norm) {
-      float t = 0.0f;
-      for (int w = 0; w < kW; ++w) t += wsq[w][mr];
-      rn[mr] = rsqrtf(t / (float)K + a.m.norm_eps);
-    }
-  }
+  mark(a, 0);
 
   unsigned long long best[M];
 #pragma unroll
   for (int mr = 0; mr < M; ++mr) best[mr] = 0ull;
-  // the row loop, compiled for K <= 768 (3 chunks of 256 codes per lane) and K <= 2048 (8)
-  auto row_loop = [&](auto nu) {
-  constexpr int NU = decltype(nu)::value;
-  RowW<NU> A0, B0;
-  for (int u = cta; u < units; u += step) {
-    int ra, rb;
-    bool hb;
-    rows_of(u, ra, rb, hb);
-    if (u != cta || !pre_staged(K)) {
-      load_row(g.W, tb, K, ra, true, A0);
-      load_row(g.W, tb, K, rb, hb, B0);
-      if (u != cta) load_res(ra, rb, hb);
-    } else {  // the first unit's rows were copied to shared memory before the barrier
-      const uint8_t* slot = pre_slot(smem, K);
-      pre_read_row(slot, K, true, A0);
-      pre_read_row(slot + pre_row_bytes(K), K, hb, B0);
-    }
+  for (int i = 0; i < n_mine; i += 2) {
+    const int ua = g.ucta + i * g.uncta, ub = ua + g.uncta;
+    const bool hb = i + 1 < n_mine;
+    const int ra = ua * kTileRows + warp, rb = ub * kTileRows + warp;
+    const bool ga = i >= nst, gb = i + 1 >= nst;
+    const uint8_t* ta = ga ? g.W.tiles + ua * tb : slot + i * tb;
+    const uint8_t* tbb = gb ? g.W.tiles + ub * tb : slot + (i + 1) * tb;
     float aa[M], ab[M];
-#pragma unroll
-    for (int mr = 0; mr < M; ++mr) aa[mr] = ab[mr] = 0.0f;
-    dot_row<M>(A0, K, xs, aa);
-    if (hb) dot_row<M>(B0, K, xs, ab);
-    const float tsa = g.W.tile_scale[ra >> 4];
-    const float tsb = hb ? g.W.tile_scale[rb >> 4] : 0.0f;
+    row_dot<M>(ta, K, warp, true, ga, xs, aa);
+    if (hb) row_dot<M>(tbb, K, warp, true, gb, xs, ab);
+    const float tsa = i < kParTs ? ps[i] : g.W.tile_scale[ua];
+    const float tsb = hb ? (i + 1 < kParTs ? ps[i + 1] : g.W.tile_scale[ub]) : 0.0f;
 #pragma unroll
     for (int mr = 0; mr < M; ++mr) {
-      const float va = warp_sum(aa[mr]) * tsa * rn[mr];
-      const float vb = hb ? warp_sum(ab[mr]) * tsb * rn[mr] : 0.0f;
-      if (lane == 0 && mr < m_rows) {
-        float* yr = g.y + (int64_t)mr * g.ldy;
-        if (g.epi == EPI_ACT_) {
-          if (ra < g.rows_out) yr[ra] = silu(va) * vb;
+      const float va = aa[mr] * tsa * rn[mr];
+      const float vb = hb ? ab[mr] * tsb * rn[mr] : 0.0f;
+      if (g.argmax) {
+        if (ra < g.rows_out) best[mr] = max(best[mr], pack_argmax(va, ra));
+        if (hb && rb < g.rows_out) best[mr] = max(best[mr], pack_argmax(vb, rb));
+      }
+      if (lane == mr && mr < m_rows) {  // one lane per input row writes
+        if (g.epi == EPI_RED_) {
+          long long* yr = g.yq + (int64_t)mr * g.ldy;
+          if (ra < g.rows_out) red_fix(yr + ra, va);
+          if (hb && rb < g.rows_out) red_fix(yr + rb, vb);
         } else {
-          if (ra < g.rows_out) {
-            if (g.epi == EPI_ADD_) yr[ra] = resa[mr] + va;
-            else yr[ra] = va;
-            if (g.argmax) best[mr] = max(best[mr], pack_argmax(va, ra));
-          }
-          if (hb && rb < g.rows_out) {
-            if (g.epi == EPI_ADD_) yr[rb] = resb[mr] + vb;
-            else yr[rb] = vb;
-            if (g.argmax) best[mr] = max(best[mr], pack_argmax(vb, rb));
-          }
+          float* yr = g.y + (int64_t)mr * g.ldy;
+          if (ra < g.rows_out) yr[ra] = va;
+          if (hb && rb < g.rows_out) yr[rb] = vb;
         }
       }
     }
   }
-  };
-  if (K <= 768) row_loop(std::integral_constant<int, 3>{});
-  else row_loop(std::integral_constant<int, 8>{});
   if (g.argmax) {
     if (lane == 0)
 #pragma unroll
@@ -486,6 +520,505 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, int ct
         if (mr < m_rows) atomicMax(&s_best[mr], best[mr]);
     __syncthreads();
     if (tid < m_rows) atomicMax(&a.amax[tid], s_best[tid]);
+  }
+}
+
+// ------------------------------------------------------------------ GDN (cluster per head)
+struct GdnGeo {
+  int H, Dk, Dv, vpr, v0, HP, ntile, NC, RC, d;
+};
+
+__device__ __forceinline__ GdnGeo gdn_geo(const CbModel& m, int rank) {
+  GdnGeo g;
+  g.H = m.gdn_heads;
+  g.Dk = m.gdn_dk;
+  g.Dv = m.gdn_dv;
+  g.vpr = g.Dv / kCl;
+  g.v0 = rank * g.vpr;
+  g.HP = 2 * g.Dk + 2 * g.Dv + 2;
+  g.ntile = (2 * g.Dk + 2 * g.Dv) / kTileRows;
+  g.NC = 2 * g.Dk + g.vpr;
+  g.RC = m.d_model / kCl;
+  g.d = m.d_model;
+  return g;
+}
+
+// In-projection tile of entry j of head h's tile list (q tiles, k tiles, v tiles,
+// gate tiles), and the offset of its first row in the head's output vector.
+__device__ __forceinline__ int gdn_head_tile(const CbModel& m, const GdnGeo& g, int h, int j, int& hp_off) {
+  const int qt = g.Dk / kTileRows, vt = g.Dv / kTileRows;
+  if (j < qt) {
+    hp_off = j * kTileRows;
+    return (h * g.Dk) / kTileRows + j;
+  }
+  j -= qt;
+  if (j < qt) {
+    hp_off = g.Dk + j * kTileRows;
+    return (g.H * g.Dk + h * g.Dk) / kTileRows + j;
+  }
+  j -= qt;
+  if (j < vt) {
+    hp_off = 2 * g.Dk + j * kTileRows;
+    return (2 * g.H * g.Dk + h * g.Dv) / kTileRows + j;
+  }
+  j -= vt;
+  hp_off = 2 * g.Dk + g.Dv + j * kTileRows;
+  return (m.gdn_off_gate + h * g.Dv) / kTileRows + j;
+}
+
+// Global channel of conv channel c of this rank (q: Dk, k: Dk, v: the rank's vpr columns).
+__device__ __forceinline__ int gdn_channel(const GdnGeo& g, int h, int c) {
+  if (c < g.Dk) return h * g.Dk + c;
+  if (c < 2 * g.Dk) return g.H * g.Dk + h * g.Dk + (c - g.Dk);
+  return 2 * g.H * g.Dk + h * g.Dv + g.v0 + (c - 2 * g.Dk);
+}
+
+// Shared-memory plan of the GDN phase inside the work area (hp, ssq and red
+// are written by the cluster's CTAs; the preload region is written only by
+// this CTA, before the barrier that starts the phase).
+struct GdnSmem {
+  float *hp, *ssq, *red, *xs, *qk, *vv, *og, *rs, *pv, *gb, *pconv_w, *pconv_s;
+};
+__device__ __forceinline__ int pad4(int n) { return (n + 3) & ~3; }  // floats to a 16-byte multiple
+
+template <int M>
+__device__ __forceinline__ GdnSmem gdn_smem(float* work, const GdnGeo& g) {
+  GdnSmem s;  // every array starts on a 16-byte boundary (xs is read as float4)
+  s.xs = work;                          // [M][d]
+  s.hp = s.xs + pad4(M * g.d);          // [M][HP]
+  s.ssq = s.hp + pad4(M * g.HP);        // [kCl][M]
+  s.red = s.ssq + pad4(kCl * M);        // [kCl][M][RC]
+  s.qk = s.red + pad4(kCl * M * g.RC);  // [M][2 Dk]
+  s.vv = s.qk + pad4(M * 2 * g.Dk);     // [M][vpr]
+  s.og = s.vv + pad4(M * g.vpr);        // [M][vpr]
+  s.rs = s.og + pad4(M * g.vpr);        // [kT] reduction scratch
+  s.pv = s.rs + kT;                     // [kW]
+  s.gb = s.pv + kW;                     // [M][2] decay log, beta
+  s.pconv_w = work + kPreOff / 4 + kParConv;  // [NC][4] conv taps (parameter region)
+  s.pconv_s = s.pconv_w + g.NC * 4;     // [B][3][NC] conv window
+  return s;
+}
+
+// Before the barrier: this rank's state columns into registers and its conv
+// taps / conv window into the preload region (they do not depend on the step).
+template <int M>
+__device__ __forceinline__ void gdn_preload(const MkArgs& a, const CbSelfLayer& L, int h, int rank, float (&st)[M],
+                            float* work) {
+  const CbModel& m = a.m;
+  const GdnGeo g = gdn_geo(m, rank);
+  const GdnSmem s = gdn_smem<M>(work, g);
+  const int tid = threadIdx.x, C = 2 * g.H * g.Dk + g.H * g.Dv;
+  const bool holds = tid < g.Dk * g.vpr;
+  const int k = tid / g.vpr, v = tid - k * g.vpr;
+#pragma unroll
+  for (int b = 0; b < M; ++b) {
+    st[b] = 0.0f;
+    if (b < a.B && holds) {
+      const int64_t slot = (int64_t)b * a.c.n_gdn + L.slot;
+      st[b] = __ldcg(a.c.gdn_state + ((slot * g.H + h) * g.Dk + k) * g.Dv + g.v0 + v);
+    }
+  }
+  // norm vector, tile scales of this rank's tiles, gate constants, tensor scale, o_norm columns
+  float* pn = par_norm(work);
+  float* ps = par_small(work);
+  for (int i = tid; i < m.d_model / 4; i += kT) cp_async16(pn + 4 * i, L.norm1 + 4 * i);
+  if (tid == 0) {
+    int q = 0;
+    for (int j = rank; j < g.ntile; j += kCl, ++q) {
+      int hp_off;
+      cp_async4(ps + q, L.in_proj.tile_scale + gdn_head_tile(m, g, h, j, hp_off));
+    }
+    if (rank == kCl - 1) {
+      cp_async4(ps + 16, L.in_proj.tile_scale + (m.gdn_off_a + h) / kTileRows);
+      cp_async4(ps + 17, L.in_proj.tile_scale + (m.gdn_off_b + h) / kTileRows);
+    }
+    cp_async4(ps + PS_A_LOG, L.A_log + h);
+    cp_async4(ps + PS_DT_BIAS, L.dt_bias + h);
+    cp_async4(ps + PS_TSCALE, L.o_proj_ks.tensor_scale);
+  }
+  for (int v2 = tid; v2 < g.vpr; v2 += kT) cp_async4(ps + PS_O_NORM + v2, L.o_norm + g.v0 + v2);
+  for (int c = tid; c < g.NC; c += kT) cp_async16(s.pconv_w + c * 4, L.conv_w + (int64_t)gdn_channel(g, h, c) * 4);
+  for (int i = tid; i < a.B * 3 * g.NC; i += kT) {
+    const int b = i / (3 * g.NC), r = i - b * 3 * g.NC, j = r / g.NC, c = r - j * g.NC;
+    const int64_t slot = (int64_t)b * a.c.n_gdn + L.slot;
+    cp_async4(s.pconv_s + i, a.c.gdn_conv + (slot * 3 + j) * C + gdn_channel(g, h, c));
+  }
+}
+
+__device__ __forceinline__ int64_t slice_bytes(const CbSliced& S) {
+  return ((int64_t)S.rows * (S.width / 2 + 1) + 15) / 16 * 16;
+}
+
+// Weight chunks of the GDN phase for cluster rank `rank` of head h: the rank's
+// in-projection tiles (entries rank, rank + 8, ... of the head's list), the a
+// and b tiles on the last rank, then the rank's o-projection slice.  Returns
+// the chunk count; *oslice receives the slot offset of the o-projection slice.
+template <typename F>
+__device__ __forceinline__ int gdn_chunks(const CbSelfLayer& L, const CbModel& m, int h, int rank, F&& f,
+                                          int* oslice = nullptr) {
+  const GdnGeo g = gdn_geo(m, rank);
+  const int64_t tb = tile_bytes(L.in_proj.k);
+  int n = 0, off = 0;
+  for (int j = rank; j < g.ntile; j += kCl) {
+    int hp_off;
+    const int t = gdn_head_tile(m, g, h, j, hp_off);
+    f(n++, L.in_proj.tiles + t * tb, (unsigned)tb, off);
+    off += (int)tb;
+  }
+  if (rank == kCl - 1) {
+    f(n++, L.in_proj.tiles + ((m.gdn_off_a + h) / kTileRows) * tb, (unsigned)tb, off);
+    off += (int)tb;
+    f(n++, L.in_proj.tiles + ((m.gdn_off_b + h) / kTileRows) * tb, (unsigned)tb, off);
+    off += (int)tb;
+  }
+  if (oslice) *oslice = off;
+  const int64_t sb = slice_bytes(L.o_proj_ks);
+  f(n++, L.o_proj_ks.data + (int64_t)(h * kCl + rank) * sb, (unsigned)sb, off);
+  return n;
+}
+
+// One cluster per head: in-projection -> conv -> recurrence -> gated norm -> o-projection.
+template <int M>
+__device__ __forceinline__ void gdn_phase(const MkArgs& a, const CbSelfLayer& L, bool first, bool live, int h, int rank,
+                          float (&st)[M], const uint8_t* slot, float* work) {
+  const CbModel& m = a.m;
+  const GdnGeo g = gdn_geo(m, rank);
+  const GdnSmem s = gdn_smem<M>(work, g);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int B = a.B, T = a.T, Mr = B * T, d = g.d, K = L.in_proj.k, C = 2 * g.H * g.Dk + g.H * g.Dv;
+  const int64_t tb = tile_bytes(K);
+  const bool snap = a.c.snap_state != nullptr && a.c.snap_conv != nullptr && T > 1;
+  if (live) {
+    __shared__ int s_rows[kMkMaxRows];
+    if (tid < kMkMaxRows) s_rows[tid] = tid;
+    __syncthreads();
+    float rn[M];
+    stage_rows<M>(a.hq, nullptr, d, s_rows, Mr, K, par_norm(work), m.norm_eps, s.xs, rn, nullptr,
+                  (first && h == 0 && rank == 0) ? a.hq : nullptr, first ? &a : nullptr);
+    mark(a, 0);
+    const float* ps = par_small(work);
+    // this rank's rows: tiles rank, rank + 8, ... then (last rank) the a and b rows;
+    // lane r < 8 of each warp sends the row's values to cluster rank r
+    int off = 0, q = 0;
+    for (int j = rank; j < g.ntile; j += kCl, ++q) {
+      int hp_off;
+      gdn_head_tile(m, g, h, j, hp_off);
+      float acc[M];
+      row_dot<M>(slot + off, K, warp, true, false, s.xs, acc);
+      off += (int)tb;
+      const float ts = ps[q];
+      if (lane < kCl)
+#pragma unroll
+        for (int mr = 0; mr < M; ++mr)
+          if (mr < Mr) st_dsmem(dsmem(s.hp + mr * g.HP + hp_off + warp, lane), acc[mr] * ts * rn[mr]);
+    }
+    if (rank == kCl - 1) {
+      for (int e = 0; e < 2; ++e) {
+        const int row = (e == 0 ? m.gdn_off_a : m.gdn_off_b) + h;
+        if (warp == (row & 15)) {
+          float acc[M];
+          row_dot<M>(slot + off, K, warp, true, false, s.xs, acc);
+          const float ts = ps[16 + e];
+          if (lane < kCl)
+#pragma unroll
+            for (int mr = 0; mr < M; ++mr)
+              if (mr < Mr) st_dsmem(dsmem(s.hp + mr * g.HP + 2 * g.Dk + 2 * g.Dv + e, lane), acc[mr] * ts * rn[mr]);
+        }
+        off += (int)tb;
+      }
+    }
+  }
+  cluster_sync();  // every rank's in-projection rows are in every rank's hp
+  mark(a, 1);
+  if (live) {
+    const float* ps = par_small(work);
+    // short conv (4 taps) on q, k and this rank's v channels; the new window goes back to the cache
+    for (int c = tid; c < g.NC; c += kT) {
+      const float w0 = s.pconv_w[c * 4], w1 = s.pconv_w[c * 4 + 1], w2 = s.pconv_w[c * 4 + 2],
+                  w3 = s.pconv_w[c * 4 + 3];
+      const int hpi = c < 2 * g.Dk ? c : 2 * g.Dk + g.v0 + (c - 2 * g.Dk);
+      const bool own = c >= 2 * g.Dk || (c % kCl) == rank;
+      for (int b = 0; b < B; ++b) {
+        float c0 = s.pconv_s[(b * 3 + 0) * g.NC + c], c1 = s.pconv_s[(b * 3 + 1) * g.NC + c],
+              c2 = s.pconv_s[(b * 3 + 2) * g.NC + c];
+        for (int t = 0; t < T; ++t) {
+          const int mr = b * T + t;
+          const float x = s.hp[mr * g.HP + hpi];
+          float y = c0 * w0;
+          y += c1 * w1;
+          y += c2 * w2;
+          y += x * w3;
+          const float o = silu(y);
+          if (c < 2 * g.Dk) s.qk[mr * 2 * g.Dk + c] = o;
+          else s.vv[mr * g.vpr + (c - 2 * g.Dk)] = o;
+          c0 = c1;
+          c1 = c2;
+          c2 = x;
+          if (snap && own && t < T - 1) {  // the window after token t (verify rewind)
+            float* sw = a.c.snap_conv + (int64_t)t * B * a.c.n_gdn * 3 * C +
+                        ((int64_t)b * a.c.n_gdn + L.slot) * 3 * C + gdn_channel(g, h, c);
+            sw[0] = c0;
+            sw[C] = c1;
+            sw[2 * (int64_t)C] = c2;
+          }
+        }
+        if (own) {
+          const int64_t slot_i = (int64_t)b * a.c.n_gdn + L.slot;
+          float* cw = a.c.gdn_conv + slot_i * 3 * C + gdn_channel(g, h, c);
+          cw[0] = c0;
+          cw[C] = c1;
+          cw[2 * (int64_t)C] = c2;
+        }
+      }
+    }
+    if (tid < Mr) {
+      const float av = s.hp[tid * g.HP + 2 * g.Dk + 2 * g.Dv], bv = s.hp[tid * g.HP + 2 * g.Dk + 2 * g.Dv + 1];
+      s.gb[tid * 2] = -expf(ps[PS_A_LOG]) * softplus(av + ps[PS_DT_BIAS]);
+      s.gb[tid * 2 + 1] = sigmoid(bv);
+    }
+    __syncthreads();
+    for (int job = warp; job < 2 * Mr; job += kW) {  // L2 norms of q and k
+      float* x = s.qk + (job >> 1) * 2 * g.Dk + (job & 1) * g.Dk;
+      float ss = 0.0f;
+      for (int i = lane; i < g.Dk; i += 32) ss += x[i] * x[i];
+      ss = warp_sum(ss);
+      const float inv = 1.0f / fmaxf(sqrtf(ss), 1e-12f);
+      for (int i = lane; i < g.Dk; i += 32) x[i] *= inv;
+    }
+    __syncthreads();
+  }
+  // the recurrence on this rank's columns: thread (k, v) holds S[k][v0 + v] of every sequence
+  const bool holds = tid < g.Dk * g.vpr;
+  const int k = tid / g.vpr, v = tid - k * g.vpr;
+  if (live) {
+    const float scale = rsqrtf((float)g.Dk);
+    auto reduce_k = [&](float part, float* out, float mul) {  // out[v] = mul * sum_k part(k, v), fixed order
+      s.rs[tid] = part;
+      __syncthreads();
+      if (warp < g.vpr) {
+        float t = 0.0f;
+        for (int kk = lane; kk < g.Dk; kk += 32) t += s.rs[kk * g.vpr + warp];
+        t = warp_sum(t);
+        if (lane == 0) out[warp] = t * mul;
+      }
+      __syncthreads();
+    };
+#pragma unroll
+    for (int b = 0; b < M; ++b) {
+      if (b < B) {
+        for (int t = 0; t < T; ++t) {
+          const int mr = b * T + t;
+          const float* qq = s.qk + mr * 2 * g.Dk;
+          const float* kk = qq + g.Dk;
+          const float decay = expf(s.gb[mr * 2]), beta = s.gb[mr * 2 + 1];
+          float part = 0.0f;
+          if (holds) {
+            st[b] *= decay;
+            part = st[b] * kk[k];
+          }
+          reduce_k(part, s.pv, 1.0f);
+          part = 0.0f;
+          if (holds) {
+            const float delta = beta * (s.vv[mr * g.vpr + v] - s.pv[v]);
+            st[b] = fmaf(kk[k], delta, st[b]);
+            part = st[b] * qq[k];
+          }
+          reduce_k(part, s.og + mr * g.vpr, scale);
+          if (snap && holds && t < T - 1)  // the state after token t (verify rewind)
+            a.c.snap_state[(int64_t)t * B * a.c.n_gdn * g.H * g.Dk * g.Dv +
+                           ((((int64_t)b * a.c.n_gdn + L.slot) * g.H + h) * g.Dk + k) * g.Dv + g.v0 + v] = st[b];
+        }
+        if (holds) {
+          const int64_t slot_i = (int64_t)b * a.c.n_gdn + L.slot;
+          a.c.gdn_state[((slot_i * g.H + h) * g.Dk + k) * g.Dv + g.v0 + v] = st[b];
+        }
+      }
+    }
+    // this rank's part of each row's sum of squares, to every rank
+    if (tid < Mr) {
+      float ss = 0.0f;
+      for (int vv = 0; vv < g.vpr; ++vv) ss += s.og[tid * g.vpr + vv] * s.og[tid * g.vpr + vv];
+      for (int r = 0; r < kCl; ++r) st_dsmem(dsmem(s.ssq + rank * M + tid, r), ss);
+    }
+  }
+  cluster_sync();
+  mark(a, 2);
+  if (live) {
+    const float* ps = par_small(work);
+    for (int i = tid; i < Mr * g.vpr; i += kT) {
+      const int mr = i / g.vpr, vc = i - mr * g.vpr;
+      float ss = 0.0f;
+      for (int r = 0; r < kCl; ++r) ss += s.ssq[r * M + mr];
+      const float rr = rsqrtf(ss / (float)g.Dv + m.norm_eps);
+      const float gate = s.hp[mr * g.HP + 2 * g.Dk + g.Dv + g.v0 + vc];
+      s.og[i] = s.og[i] * rr * ps[PS_O_NORM + vc] * silu(gate);
+    }
+    __syncthreads();
+    // split-K o-projection on this rank's columns; the partial of output n goes to rank n / RC
+    int soff = 0;
+    gdn_chunks(L, m, h, rank, [](int, const uint8_t*, unsigned, int) {}, &soff);
+    const uint8_t* sl = slot + soff;
+    const int cbytes = g.vpr / 2;
+    const float ts = ps[PS_TSCALE];
+    for (int n = tid; n < d; n += kT) {
+      const float sc = e4m3_to_f32(sl[(int64_t)d * cbytes + n]) * ts;
+      float acc[M];
+#pragma unroll
+      for (int mr = 0; mr < M; ++mr) acc[mr] = 0.0f;
+      for (int j = 0; j < cbytes; ++j) {
+        const float2 w = e2m1x2_to_f32x2(sl[n * cbytes + j]);
+#pragma unroll
+        for (int mr = 0; mr < M; ++mr)
+          acc[mr] = fmaf(w.y, s.og[mr * g.vpr + 2 * j + 1], fmaf(w.x, s.og[mr * g.vpr + 2 * j], acc[mr]));
+      }
+      const int q = n / g.RC, nl = n - q * g.RC;
+#pragma unroll
+      for (int mr = 0; mr < M; ++mr)
+        if (mr < Mr) st_dsmem(dsmem(s.red + (rank * M + mr) * g.RC + nl, q), acc[mr] * sc);
+    }
+  }
+  cluster_sync();
+  mark(a, 3);
+  if (live) {
+    for (int i = tid; i < Mr * g.RC; i += kT) {
+      const int mr = i / g.RC, nl = i - mr * g.RC;
+      float t = 0.0f;
+      for (int r = 0; r < kCl; ++r) t += s.red[(r * M + mr) * g.RC + nl];
+      red_fix(a.hq + (int64_t)mr * d + rank * g.RC + nl, t);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ FFN (split K)
+// Slices of 16 hidden units: slice j = the gate tile j, the up tile F/16 + j and
+// the 16 columns j of the down projection.  CTA c owns slices c, c + ncta, ...
+__device__ __forceinline__ int ffn_mine(int F, int cta, int ncta) {
+  const int nsl = F / kTileRows;
+  return cta < nsl ? (nsl - 1 - cta) / ncta + 1 : 0;
+}
+__device__ __forceinline__ int ffn_staged(const CbMatrix& GU, const CbSliced& D, int F, int cta, int ncta) {
+  const int64_t per = 2 * tile_bytes(GU.k) + slice_bytes(D);
+  return min(ffn_mine(F, cta, ncta), (int)(kSlot / per));
+}
+
+template <typename F>
+__device__ __forceinline__ int ffn_chunks(const CbMatrix& GU, const CbSliced& D, int Fh, int cta, int ncta, F&& f) {
+  const int64_t tb = tile_bytes(GU.k), dsb = slice_bytes(D);
+  const int nst = ffn_staged(GU, D, Fh, cta, ncta);
+  int n = 0, off = 0;
+  for (int i = 0; i < nst; ++i) {
+    const int j = cta + i * ncta;
+    f(n++, GU.tiles + j * tb, (unsigned)tb, off);
+    off += (int)tb;
+    f(n++, GU.tiles + (Fh / kTileRows + j) * tb, (unsigned)tb, off);
+    off += (int)tb;
+    f(n++, D.data + j * dsb, (unsigned)dsb, off);
+    off += (int)dsb;
+  }
+  return n;
+}
+
+template <int M>
+__device__ void ffn_phase(const MkArgs& a, const CbMatrix& GU, const CbSliced& D, const float* norm2, long long* resid,
+                          int Mr, bool live, int rank, int cid, const uint8_t* slot, float* work) {
+  const CbModel& m = a.m;
+  const int d = m.d_model, Fh = m.ffn_hidden, RC = d / kCl, K = GU.k;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, cta = blockIdx.x, ncta = gridDim.x;
+  float* red = work;                   // [kCl][M][RC]  (written by the cluster's CTAs)
+  float* xs = red + kCl * M * RC;      // [M][d]
+  float* act = xs + M * d;             // [M][16]
+  constexpr int kNE = (kMkMaxD + kT - 1) / kT;  // outputs per thread
+  float acc[kNE][M];
+#pragma unroll
+  for (int e = 0; e < kNE; ++e)
+#pragma unroll
+    for (int mr = 0; mr < M; ++mr) acc[e][mr] = 0.0f;
+  const int n_mine = ffn_mine(Fh, cta, ncta);
+  // a cluster adds its sums only when one of its CTAs owns a slice (cluster-uniform)
+  const bool cluster_has = cid * kCl < Fh / kTileRows;
+  if (live && n_mine > 0) {
+    __shared__ int s_rows[kMkMaxRows];
+    if (tid < kMkMaxRows) s_rows[tid] = tid;
+    __syncthreads();
+    float rn[M];
+    stage_rows<M>(resid, nullptr, d, s_rows, Mr, K, par_norm(work), m.norm_eps, xs, rn, nullptr, nullptr, nullptr);
+    mark(a, 0);
+    const float* ps = par_small(work);
+    const int64_t tb = tile_bytes(K), dsb = slice_bytes(D);
+    const int nst = ffn_staged(GU, D, Fh, cta, ncta);
+    const float ts_d = ps[PS_TSCALE];
+    for (int i = 0; i < n_mine; ++i) {
+      const int j = cta + i * ncta;
+      const bool glob = i >= nst;
+      const uint8_t* tg = glob ? GU.tiles + j * tb : slot + i * (2 * tb + dsb);
+      const uint8_t* tu = glob ? GU.tiles + (Fh / kTileRows + j) * tb : tg + tb;
+      const uint8_t* ds = glob ? D.data + j * dsb : tg + 2 * tb;
+      float gv[M], uv[M];
+      row_dot<M>(tg, K, warp, true, glob, xs, gv);
+      row_dot<M>(tu, K, warp, true, glob, xs, uv);
+      const float tsg = i < 16 ? ps[i] : GU.tile_scale[j];
+      const float tsu = i < 16 ? ps[16 + i] : GU.tile_scale[Fh / kTileRows + j];
+      if (lane < M && lane < Mr) {
+        float g0 = 0.0f, u0 = 0.0f;
+#pragma unroll
+        for (int mr = 0; mr < M; ++mr)
+          if (mr == lane) {
+            g0 = gv[mr] * tsg * rn[mr];
+            u0 = uv[mr] * tsu * rn[mr];
+          }
+        act[lane * kTileRows + warp] = silu(g0) * u0;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int e = 0; e < kNE; ++e) {
+        const int n = tid + e * kT;
+        if (n < d) {
+          const uint2 cw = glob ? __ldg(reinterpret_cast<const uint2*>(ds + (int64_t)n * 8))
+                                : *reinterpret_cast<const uint2*>(ds + (int64_t)n * 8);
+          const float sc = e4m3_to_f32(glob ? __ldg(ds + (int64_t)d * 8 + n) : ds[(int64_t)d * 8 + n]) * ts_d;
+          float w[16];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 lo = e2m1x2_to_f32x2(cw.x >> (8 * q)), hi = e2m1x2_to_f32x2(cw.y >> (8 * q));
+            w[2 * q] = lo.x;
+            w[2 * q + 1] = lo.y;
+            w[8 + 2 * q] = hi.x;
+            w[8 + 2 * q + 1] = hi.y;
+          }
+#pragma unroll
+          for (int mr = 0; mr < M; ++mr) {
+            float p = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) p = fmaf(w[c], act[mr * kTileRows + c], p);
+            acc[e][mr] = fmaf(p, sc, acc[e][mr]);
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  if (live && cluster_has) {
+#pragma unroll
+    for (int e = 0; e < kNE; ++e) {
+      const int n = tid + e * kT;
+      if (n < d) {
+        const int q = n / RC, nl = n - q * RC;
+#pragma unroll
+        for (int mr = 0; mr < M; ++mr)
+          if (mr < Mr) st_dsmem(dsmem(red + (rank * M + mr) * RC + nl, q), acc[e][mr]);
+      }
+    }
+  }
+  mark(a, 1);
+  cluster_sync();
+  mark(a, 2);
+  if (live && cluster_has) {
+    for (int i = tid; i < Mr * RC; i += kT) {
+      const int mr = i / RC, nl = i - mr * RC;
+      float t = 0.0f;
+      for (int r = 0; r < kCl; ++r) t += red[(r * M + mr) * RC + nl];
+      red_fix(resid + (int64_t)mr * d + rank * RC + nl, t);
+    }
   }
 }
 
@@ -521,149 +1054,6 @@ __device__ void norm_rope_warp(const float* x, const float* w, int hd, int rot2,
   }
 }
 
-// ------------------------------------------------------------------- GDN
-template <int KPT>
-__device__ void gdn_item(const MkArgs& a, const CbSelfLayer& L, int h, int b, float* smem) {
-  const CbModel& m = a.m;
-  const int H = m.gdn_heads, Dk = m.gdn_dk, Dv = m.gdn_dv, T = a.T, KC = m.conv_size;
-  const int C = 2 * H * Dk + H * Dv;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n_kg = Dk / KPT;  // thread groups that hold state rows
-  const int v = tid % Dv, kg = tid / Dv;
-  const bool holds = kg < n_kg;
-  float* qs = smem;                  // [8][Dk]
-  float* ks = qs + kMkMaxRows * Dk;  // [8][Dk]
-  float* vs = ks + kMkMaxRows * Dk;  // [8][Dv]
-  float* red = vs + kMkMaxRows * Dv; // [kT]
-  float* os = red + kT;              // [8][Dv]
-  __shared__ float gs[kMkMaxRows], bs[kMkMaxRows], scratch[33];
-  const int64_t slot = (int64_t)b * a.c.n_gdn + L.slot;
-  float* conv = a.c.gdn_conv + slot * (KC - 1) * C;
-  float* S = a.c.gdn_state + slot * H * Dk * Dv + (int64_t)h * Dk * Dv;
-  const float* proj = a.proj + (int64_t)b * T * a.ldp;
-  float s[KPT];  // state rows of this thread, loaded first (they do not depend on the step's input)
-  if (holds) {
-#pragma unroll
-    for (int i = 0; i < KPT; ++i) s[i] = S[(int64_t)(kg * KPT + i) * Dv + v];
-  }
-
-  for (int c = tid; c < 2 * Dk + Dv; c += kT) {
-    int ch, di;
-    float* dst;
-    int dstride;
-    if (c < Dk) { ch = h * Dk + c; dst = qs; dstride = Dk; di = c; }
-    else if (c < 2 * Dk) { ch = H * Dk + h * Dk + (c - Dk); dst = ks; dstride = Dk; di = c - Dk; }
-    else { ch = 2 * H * Dk + h * Dv + (c - 2 * Dk); dst = vs; dstride = Dv; di = c - 2 * Dk; }
-    // causal conv with 4 taps (the persistent path requires conv_size == 4): y_t = sum_j w[j] * xx[t + j]
-    float w0 = L.conv_w[(int64_t)ch * 4 + 0], w1 = L.conv_w[(int64_t)ch * 4 + 1];
-    float w2 = L.conv_w[(int64_t)ch * 4 + 2], w3 = L.conv_w[(int64_t)ch * 4 + 3];
-    float c0 = conv[ch], c1 = conv[(int64_t)C + ch], c2 = conv[(int64_t)2 * C + ch];
-    float xin[kMkMaxRows];
-#pragma unroll
-    for (int t = 0; t < kMkMaxRows; ++t) xin[t] = t < T ? __ldcg(proj + (int64_t)t * a.ldp + ch) : 0.0f;
-#pragma unroll
-    for (int t = 0; t < kMkMaxRows; ++t) {
-      if (t < T) {
-        const float x = xin[t];
-        float y = c0 * w0;
-        y += c1 * w1;
-        y += c2 * w2;
-        y += x * w3;
-        dst[t * dstride + di] = silu(y);
-        c0 = c1;
-        c1 = c2;
-        c2 = x;
-      }
-    }
-    conv[ch] = c0;
-    conv[(int64_t)C + ch] = c1;
-    conv[(int64_t)2 * C + ch] = c2;
-  }
-  if (tid < T) {
-    const float av = __ldcg(proj + (int64_t)tid * a.ldp + m.gdn_off_a + h);
-    const float bv = __ldcg(proj + (int64_t)tid * a.ldp + m.gdn_off_b + h);
-    gs[tid] = -expf(L.A_log[h]) * softplus(av + L.dt_bias[h]);
-    bs[tid] = sigmoid(bv);
-  }
-  __syncthreads();
-  for (int job = warp; job < 2 * T; job += kW) {
-    float* x = (job < T ? qs : ks) + (job % T) * Dk;
-    float ss = 0.0f;
-    for (int i = lane; i < Dk; i += 32) ss += x[i] * x[i];
-    ss = warp_sum(ss);
-    const float inv = 1.0f / fmaxf(sqrtf(ss), 1e-12f);
-    for (int i = lane; i < Dk; i += 32) x[i] *= inv;
-  }
-  __syncthreads();
-  const float scale = rsqrtf((float)Dk);
-  for (int t = 0; t < T; ++t) {
-    const float decay = expf(gs[t]);
-    float part = 0.0f;
-    if (holds) {
-      const float* kt = ks + t * Dk + kg * KPT;
-#pragma unroll
-      for (int i = 0; i < KPT; ++i) {
-        s[i] *= decay;
-        part = fmaf(s[i], kt[i], part);
-      }
-    }
-    red[tid] = part;
-    __syncthreads();
-    float pred = 0.0f;
-    for (int g2 = 0; g2 < n_kg; ++g2) pred += red[g2 * Dv + v];
-    __syncthreads();
-    const float delta = bs[t] * (vs[t * Dv + v] - pred);
-    part = 0.0f;
-    if (holds) {
-      const float* kt = ks + t * Dk + kg * KPT;
-      const float* qt = qs + t * Dk + kg * KPT;
-#pragma unroll
-      for (int i = 0; i < KPT; ++i) {
-        s[i] = fmaf(kt[i], delta, s[i]);
-        part = fmaf(s[i], qt[i], part);
-      }
-    }
-    red[tid] = part;
-    __syncthreads();
-    if (kg == 0) {
-      float o = 0.0f;
-      for (int g2 = 0; g2 < n_kg; ++g2) o += red[g2 * Dv + v];
-      os[t * Dv + v] = o * scale;
-    }
-    __syncthreads();
-  }
-  if (holds) {
-#pragma unroll
-    for (int i = 0; i < KPT; ++i) S[(int64_t)(kg * KPT + i) * Dv + v] = s[i];
-  }
-  for (int t = 0; t < T; ++t) {
-    const float o = tid < Dv ? os[t * Dv + tid] : 0.0f;
-    const float ss = block_sum(o * o, scratch);
-    if (tid < Dv) {
-      const float r = rsqrtf(ss / (float)Dv + m.norm_eps);
-      const float gate = __ldcg(proj + (int64_t)t * a.ldp + m.gdn_off_gate + h * Dv + tid);
-      a.attn[((int64_t)b * T + t) * a.att_ld + h * Dv + tid] = o * r * L.o_norm[tid] * silu(gate);
-    }
-  }
-  __syncthreads();
-}
-
-__device__ void gdn_phase(const MkArgs& a, const CbSelfLayer& L, int cta, int ncta, float* smem) {
-  const int H = a.m.gdn_heads;
-  const int kpt = max(1, a.m.gdn_dk * a.m.gdn_dv / kT);
-  for (int it = cta; it < H * a.B; it += ncta) {
-    const int h = it % H, b = it / H;
-    switch (kpt) {
-      case 1: gdn_item<1>(a, L, h, b, smem); break;
-      case 2: gdn_item<2>(a, L, h, b, smem); break;
-      case 4: gdn_item<4>(a, L, h, b, smem); break;
-      case 8: gdn_item<8>(a, L, h, b, smem); break;
-      case 16: gdn_item<16>(a, L, h, b, smem); break;
-      default: gdn_item<32>(a, L, h, b, smem); break;
-    }
-  }
-}
-
 // ------------------------------------------- attention helpers (split softmax)
 // Scores of nq queries (Qs [nq][hd]) against n keys (Ks [n][hd+1]) into Sc [nq][ldsc],
 // masked entries -inf; then per query max / exp / sum (qm, ql) and o += e V into oacc.
@@ -684,11 +1074,11 @@ __device__ void attend_chunk(const float* Qs, const float* Ks, const float* Vs, 
       const float* kk = Ks + key * (hd + 1);
       float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
 #pragma unroll 2
-      for (int d = 0; d < hd; d += 4) {
-        a0 = fmaf(qq[d], kk[d], a0);
-        a1 = fmaf(qq[d + 1], kk[d + 1], a1);
-        a2 = fmaf(qq[d + 2], kk[d + 2], a2);
-        a3 = fmaf(qq[d + 3], kk[d + 3], a3);
+      for (int dd = 0; dd < hd; dd += 4) {
+        a0 = fmaf(qq[dd], kk[dd], a0);
+        a1 = fmaf(qq[dd + 1], kk[dd + 1], a1);
+        a2 = fmaf(qq[dd + 2], kk[dd + 2], a2);
+        a3 = fmaf(qq[dd + 3], kk[dd + 3], a3);
       }
       sc = ((a0 + a1) + (a2 + a3)) * scale;
     }
@@ -717,18 +1107,18 @@ __device__ void attend_chunk(const float* Qs, const float* Ks, const float* Vs, 
   }
   __syncthreads();
   for (int i = tid; i < nq * hd; i += kT) {
-    const int q = i / hd, d = i - q * hd;
+    const int q = i / hd, dd = i - q * hd;
     const float* e = Sc + q * ldsc;
     float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;  // keys mod 4, summed in a fixed order
     int key = 0;
 #pragma unroll 2
     for (; key + 4 <= n; key += 4) {
-      o0 = fmaf(e[key], Vs[key * hd + d], o0);
-      o1 = fmaf(e[key + 1], Vs[(key + 1) * hd + d], o1);
-      o2 = fmaf(e[key + 2], Vs[(key + 2) * hd + d], o2);
-      o3 = fmaf(e[key + 3], Vs[(key + 3) * hd + d], o3);
+      o0 = fmaf(e[key], Vs[key * hd + dd], o0);
+      o1 = fmaf(e[key + 1], Vs[(key + 1) * hd + dd], o1);
+      o2 = fmaf(e[key + 2], Vs[(key + 2) * hd + dd], o2);
+      o3 = fmaf(e[key + 3], Vs[(key + 3) * hd + dd], o3);
     }
-    for (; key < n; ++key) o0 = fmaf(e[key], Vs[key * hd + d], o0);
+    for (; key < n; ++key) o0 = fmaf(e[key], Vs[key * hd + dd], o0);
     oacc[i] = fmaf(oacc[i], corr[q], (o0 + o1) + (o2 + o3));
   }
   __syncthreads();
@@ -781,10 +1171,10 @@ __device__ void swa_item(const MkArgs& a, const CbSelfLayer& L, int b, int g, in
     norm_rope_warp(row + m.swa_off_kv + g * hd, L.k_norm, hd, m.rot_dim / 2, kp, m.inv_freq, m.norm_eps,
                    Ks + idx * (hd + 1), true, kr + off);
     const int lane = tid & 31;
-    for (int d = lane; d < hd; d += 32) {
-      const uint16_t bits = f32_to_bf16(__ldcg(row + m.swa_off_kv + Hkv * hd + g * hd + d));
-      vr[off + d] = bits;
-      Vs[idx * hd + d] = bf16_to_f32(bits);
+    for (int dd = lane; dd < hd; dd += 32) {
+      const uint16_t bits = f32_to_bf16(__ldcg(row + m.swa_off_kv + Hkv * hd + g * hd + dd));
+      vr[off + dd] = bits;
+      Vs[idx * hd + dd] = bf16_to_f32(bits);
     }
   }
   cp_async_wait_all();
@@ -820,12 +1210,13 @@ __device__ void swa_item(const MkArgs& a, const CbSelfLayer& L, int b, int g, in
     float* pp = a.part + ((((int64_t)b * T + t) * Hq + g * G + j) * S + s) * (hd + 2);
     pp[e] = e == 0 ? qm[q] : (e == 1 ? ql[q] : oacc[q * hd + e - 2]);
   }
+  __syncthreads();
   // the o projection merges the partials (PRE_COMBINE)
 }
 
-__device__ void swa_phase(const MkArgs& a, const CbSelfLayer& L, int cta, int ncta, float* smem) {
+__device__ void swa_phase(const MkArgs& a, const CbSelfLayer& L, float* smem) {
   const int Hkv = a.m.n_kv_heads, S = a.swa_splits;
-  for (int it = cta; it < a.B * Hkv * S; it += ncta) {
+  for (int it = blockIdx.x; it < a.B * Hkv * S; it += gridDim.x) {
     const int s = it % S, g = (it / S) % Hkv, b = it / (S * Hkv);
     swa_item(a, L, b, g, s, smem);
   }
@@ -894,12 +1285,13 @@ __device__ void cross_item(const MkArgs& a, const CbCrossLayer& L, int r, int g,
     float* pp = a.part2 + (((int64_t)r * Hq + g * G + j) * S + s) * (hd + 2);
     pp[e] = e == 0 ? qm[j] : (e == 1 ? ql[j] : oacc[j * hd + e - 2]);
   }
+  __syncthreads();
   // the o projection merges the partials (PRE_COMBINE)
 }
 
-__device__ void cross_phase(const MkArgs& a, const CbCrossLayer& L, int cta, int ncta, float* smem) {
+__device__ void cross_phase(const MkArgs& a, const CbCrossLayer& L, float* smem) {
   const int Hkv = a.m.n_kv_heads, S = a.cross_splits, RQ = a.B * a.nq;
-  for (int it = cta; it < RQ * Hkv * S; it += ncta) {
+  for (int it = blockIdx.x; it < RQ * Hkv * S; it += gridDim.x) {
     const int s = it % S, g = (it / S) % Hkv, r = it / (S * Hkv);
     cross_item(a, L, r, g, s, smem);
   }
@@ -914,12 +1306,12 @@ __device__ __forceinline__ void query_row(const MkArgs& a, int r, int& b, int& t
 }
 
 // New rows of the shared cache: k = RoPE(RMSNorm(k)), v, indexer key (E4M3).
-__device__ void shared_append(const MkArgs& a, int cta, int ncta, float* smem) {
+__device__ void shared_append(const MkArgs& a, float* smem) {
   const CbModel& m = a.m;
   const CbCache& c = a.c;
   const int Mrows = a.B * a.T, hd = m.head_dim, Hkv = m.n_kv_heads;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int mr = cta; mr < Mrows; mr += ncta) {
+  for (int mr = blockIdx.x; mr < Mrows; mr += gridDim.x) {
     const int b = mr / a.T, t = mr - b * a.T, p = c.pos[b] + a.c0 + t;
     if (p < 0 || p >= c.max_ctx) {
       if (threadIdx.x == 0) set_status(a.status, CB_ERR_CTX_FULL);
@@ -935,10 +1327,11 @@ __device__ void shared_append(const MkArgs& a, int cta, int ncta, float* smem) {
                        c.kv_k + base + it * hd);
       } else if (it < 2 * Hkv) {
         const int hh = it - Hkv;
-        for (int d = lane; d < hd; d += 32) c.kv_v[base + hh * hd + d] = f32_to_bf16(__ldcg(row + Hkv * hd + hh * hd + d));
+        for (int dd = lane; dd < hd; dd += 32)
+          c.kv_v[base + hh * hd + dd] = f32_to_bf16(__ldcg(row + Hkv * hd + hh * hd + dd));
       } else {
         uint8_t* ik = c.kv_ik + ((int64_t)b * c.max_ctx + p) * m.indexer_dim;
-        for (int d = lane; d < m.indexer_dim; d += 32) ik[d] = f32_to_e4m3(__ldcg(row + m.sh_off_ik + d));
+        for (int dd = lane; dd < m.indexer_dim; dd += 32) ik[dd] = f32_to_e4m3(__ldcg(row + m.sh_off_ik + dd));
       }
     }
     __syncthreads();
@@ -960,9 +1353,9 @@ __device__ __forceinline__ float indexer_score_bytes(const uint8_t* kr, const fl
         pr[rr] = i == 0 ? prod : __fadd_rn(pr[rr], prod);
       }
     }
-    const float d = __fadd_rn(__fadd_rn(__fadd_rn(pr[0], pr[1]), __fadd_rn(pr[2], pr[3])),
-                              __fadd_rn(__fadd_rn(pr[4], pr[5]), __fadd_rn(pr[6], pr[7])));
-    const float rl = d > 0.0f ? d : 0.0f;
+    const float dsum = __fadd_rn(__fadd_rn(__fadd_rn(pr[0], pr[1]), __fadd_rn(pr[2], pr[3])),
+                                 __fadd_rn(__fadd_rn(pr[4], pr[5]), __fadd_rn(pr[6], pr[7])));
+    const float rl = dsum > 0.0f ? dsum : 0.0f;
     const float term = __fmul_rn(rl, w[h]);
     score = h == 0 ? term : __fadd_rn(score, term);
   }
@@ -976,11 +1369,11 @@ __device__ __forceinline__ void key_range(int n, int cta, int ncta, int& js, int
 }
 
 // Scores of this CTA's key range for every query row + histogram of the top 11 key bits.
-__device__ void score_phase(const MkArgs& a, int cta, int ncta, float* smem) {
+__device__ void score_phase(const MkArgs& a, float* smem) {
   const CbModel& m = a.m;
   const CbCache& c = a.c;
   const int RQ = a.B * a.nq, Hi = m.indexer_heads, Di = m.indexer_dim, k = m.sparse_topk;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, cta = blockIdx.x, ncta = gridDim.x;
   unsigned* hist = reinterpret_cast<unsigned*>(smem);             // [2048]
   float* q = smem + kMkHistBins;                                   // [Hi*Di]
   float* w = q + Hi * Di;                                          // [Hi]
@@ -997,8 +1390,8 @@ __device__ void score_phase(const MkArgs& a, int cta, int ncta, float* smem) {
     for (int i = tid; i < Hi * Di; i += kT) q[i] = __ldcg(qrow + m.sh_off_iq + i);
     for (int i = tid; i < Hi; i += kT) w[i] = __ldcg(qrow + m.sh_off_iw + i);
     for (int i = tid; i < a.T * Di; i += kT) {
-      const int t2 = i / Di, d = i - t2 * Di;
-      newk[i] = f32_to_e4m3(__ldcg(a.proj + ((int64_t)b * a.T + t2) * a.ldp + m.sh_off_ik + d));
+      const int t2 = i / Di, dd = i - t2 * Di;
+      newk[i] = f32_to_e4m3(__ldcg(a.proj + ((int64_t)b * a.T + t2) * a.ldp + m.sh_off_ik + dd));
     }
     for (int i = tid; i < kMkHistBins; i += kT) hist[i] = 0u;
     __syncthreads();
@@ -1045,11 +1438,11 @@ __device__ unsigned block_excl_scan(unsigned v, unsigned* wsum, unsigned* total)
 }
 
 // Threshold bin of the k-th largest key, then this CTA's keys above it to hi_list and in it to cand.
-__device__ void compact_phase(const MkArgs& a, int cta, int ncta, float* smem) {
+__device__ void compact_phase(const MkArgs& a) {
   const CbModel& m = a.m;
   const CbCache& c = a.c;
   const int RQ = a.B * a.nq, k = m.sparse_topk;
-  const int tid = threadIdx.x, lane = tid & 31;
+  const int tid = threadIdx.x, lane = tid & 31, cta = blockIdx.x, ncta = gridDim.x;
   __shared__ unsigned wsum[32], s_total;
   __shared__ int s_b1;
   for (int r = 0; r < RQ; ++r) {
@@ -1126,7 +1519,7 @@ __device__ void resolve_row(const MkArgs& a, int r, float* smem) {
   __shared__ int s_digit, s_rem;
   unsigned* bits = reinterpret_cast<unsigned*>(smem);  // [kMkBitmapWords]
   unsigned long long* cs = reinterpret_cast<unsigned long long*>(smem) + kMkBitmapWords / 2;
-  const int cap = (kSmem - kMkBitmapWords * (int)sizeof(unsigned)) / (int)sizeof(unsigned long long);
+  const int cap = (kPreOff - kMkBitmapWords * (int)sizeof(unsigned)) / (int)sizeof(unsigned long long);
   const int nw = (n + 31) / 32;
   const int above = min(max(__ldcg(a.hi_cnt + r), 0), k - 1);
   const int nc = min(max(__ldcg(a.cand_cnt + r), 0), c.max_ctx);
@@ -1147,12 +1540,10 @@ __device__ void resolve_row(const MkArgs& a, int r, float* smem) {
   }
   unsigned long long prefix = 0ull, pmask = 0ull;
   int remaining = need;
-  const int shifts[7] = {45, 37, 29, 21, 13, 5, 0};
-  const unsigned widths[7] = {0xFF, 0xFF, 0xFF, 0xFF, 0xFF, 0xFF, 0x1F};
 #pragma unroll 1
-  for (int ps = 0; ps < 7; ++ps) {
-    const int shift = shifts[ps];
-    const unsigned dm = widths[ps];
+  for (int ps = 0; ps < 7; ++ps) {  // digits of 8 bits from bit 45 down, then the low 5 bits
+    const int shift = ps < 6 ? 45 - 8 * ps : 0;
+    const unsigned dm = ps < 6 ? 0xFFu : 0x1Fu;
     for (int i = tid; i < 256; i += kT) hist256[i] = 0u;
     __syncthreads();
     for (int i = tid; i < nc; i += kT) {
@@ -1222,335 +1613,404 @@ __device__ void resolve_row(const MkArgs& a, int r, float* smem) {
   __syncthreads();
 }
 
+// ------------------------------------------------------------------ phase plan
+__device__ int build_plan(const CbModel& m, uint16_t* plan) {
+  int n = 0;
+  auto push = [&](int kind, int layer) { plan[n++] = (uint16_t)((kind << 8) | layer); };
+  for (int i = 0; i < m.n_self_layers; ++i) {
+    if (m.self_layers[i].kind == CB_LAYER_GDN) {
+      push(PH_GDN, i);
+    } else {
+      push(PH_SWA_IN, i);
+      push(PH_SWA_ATT, i);
+      push(PH_SWA_O, i);
+    }
+    push(PH_FFN_SELF, i);
+  }
+  push(PH_SH_PROJ, 0);
+  push(PH_SH_SCORE, 0);
+  if (m.sparse_topk > 0) push(PH_SH_COMPACT, 0);
+  for (int j = 0; j < m.n_cross_layers; ++j) {
+    push(PH_CR_Q, j);
+    push(PH_CR_ATT, j);
+    push(PH_CR_O, j);
+    push(PH_FFN_CROSS, j);
+  }
+  push(PH_LM_HEAD, 0);
+  return n;
+}
+
+// The GEMV of a GEMV phase (input, output, this CTA's units).
+__device__ GemvJob gemv_job(const MkArgs& a, int kind, int layer) {
+  const CbModel& m = a.m;
+  const int d = m.d_model, RQ = a.B * a.nq;
+  GemvJob g{};
+  g.ucta = blockIdx.x;
+  g.uncta = gridDim.x;
+  g.ldx = d;
+  g.epi = EPI_STORE_;
+  switch (kind) {
+    case PH_SWA_IN: {
+      const CbSelfLayer& L = m.self_layers[layer];
+      g.W = L.in_proj;
+      g.xq = a.hq;
+      g.pre = layer == 0 ? PRE_EMBED_ : PRE_RMS_;
+      g.norm_w = L.norm1;
+      g.y = a.proj;
+      g.ldy = a.ldp;
+      g.rows_out = L.in_proj.rows;
+      break;
+    }
+    case PH_SWA_O: {
+      const CbSelfLayer& L = m.self_layers[layer];
+      g.W = L.o_proj;
+      g.pre = PRE_COMBINE_;
+      g.part = a.part;
+      g.S = a.swa_splits;
+      g.hd = m.head_dim;
+      g.gate_x = a.proj;
+      g.gate_ld = a.ldp;
+      g.gate_off = m.swa_off_gate;
+      g.yq = a.hq;
+      g.ldy = d;
+      g.rows_out = d;
+      g.epi = EPI_RED_;
+      break;
+    }
+    case PH_SH_PROJ:
+      g.W = m.shared_proj;
+      g.xq = a.hq;
+      g.pre = PRE_RMS_;
+      g.norm_w = m.shared_norm;
+      g.y = a.proj;
+      g.ldy = a.ldp;
+      g.rows_out = m.shared_proj.rows;
+      break;
+    case PH_CR_Q: {
+      const CbCrossLayer& L = m.cross_layers[layer];
+      g.W = L.q_gate;
+      g.xq = layer == 0 ? a.hq : a.xq;
+      if (layer == 0) {  // the query rows of the self-decoder's output start the cross residual stream
+        g.xmap_nq = a.nq;
+        g.xmap_T = a.T;
+        g.xmap_off = a.T - a.nq;
+        g.copy_q = a.xq;
+        if (m.sparse_topk > 0) {  // the first RQ CTAs resolve the selections beside this GEMV
+          g.ucta = (int)blockIdx.x - RQ;
+          g.uncta = (int)gridDim.x - RQ;
+        }
+      }
+      g.pre = PRE_RMS_;
+      g.norm_w = L.norm1;
+      g.y = a.cproj;
+      g.ldy = a.cr_ld;
+      g.rows_out = L.q_gate.rows;
+      break;
+    }
+    case PH_CR_O: {
+      const CbCrossLayer& L = m.cross_layers[layer];
+      g.W = L.o_proj;
+      g.pre = PRE_COMBINE_;
+      g.part = a.part2;
+      g.S = a.cross_splits;
+      g.hd = m.head_dim;
+      g.gate_x = a.cproj;
+      g.gate_ld = a.cr_ld;
+      g.gate_off = m.cr_off_gate;
+      g.yq = a.xq;
+      g.ldy = d;
+      g.rows_out = d;
+      g.epi = EPI_RED_;
+      break;
+    }
+    default:  // PH_LM_HEAD
+      g.W = m.lm_head;
+      g.xq = a.xq;
+      g.pre = PRE_RMS_;
+      g.norm_w = m.final_norm;
+      g.y = a.logits ? a.logits : a.ws_logits;
+      g.ldy = m.vocab_size;
+      g.rows_out = m.vocab_size;
+      g.argmax = true;
+      break;
+  }
+  return g;
+}
+
+__device__ __forceinline__ bool is_gemv(int kind) {
+  return kind == PH_SWA_IN || kind == PH_SWA_O || kind == PH_SH_PROJ || kind == PH_CR_Q || kind == PH_CR_O ||
+         kind == PH_LM_HEAD;
+}
+
+// Weight chunks of phase (kind, layer) for this CTA, in slot order: f(i, src, bytes, slot offset).
+template <typename F>
+__device__ int phase_chunks(const MkArgs& a, int kind, int layer, F&& f) {
+  const CbModel& m = a.m;
+  if (is_gemv(kind)) {
+    const GemvJob g = gemv_job(a, kind, layer);
+    const int nst = gemv_staged(g);
+    const int64_t tb = tile_bytes(g.W.k);
+    for (int i = 0; i < nst; ++i) f(i, g.W.tiles + (int64_t)(g.ucta + i * g.uncta) * tb, (unsigned)tb, (int)(i * tb));
+    return nst;
+  }
+  if (kind == PH_GDN) {
+    const int cid = (int)cluster_index();
+    if (cid >= m.gdn_heads) return 0;
+    return gdn_chunks(m.self_layers[layer], m, cid, (int)cluster_rank(), f);
+  }
+  if (kind == PH_FFN_SELF) {
+    const CbSelfLayer& L = m.self_layers[layer];
+    return ffn_chunks(L.gate_up, L.down_ks, m.ffn_hidden, blockIdx.x, gridDim.x, f);
+  }
+  if (kind == PH_FFN_CROSS) {
+    const CbCrossLayer& L = m.cross_layers[layer];
+    return ffn_chunks(L.gate_up, L.down_ks, m.ffn_hidden, blockIdx.x, gridDim.x, f);
+  }
+  return 0;
+}
+
+// Between the arrival at the barrier before a GEMV or FFN phase and the wait
+// there: the phase's norm vector, tile scales and tensor scale into the
+// parameter region (cp.async; completed after the wait).  The GDN phase has
+// its own (gdn_preload).
+__device__ void phase_params(const MkArgs& a, int kind, int layer, float* work) {
+  const CbModel& m = a.m;
+  const int tid = threadIdx.x;
+  float* pn = par_norm(work);
+  float* ps = par_small(work);
+  if (is_gemv(kind)) {
+    const GemvJob g = gemv_job(a, kind, layer);
+    const int n = min(gemv_mine(g), kParTs);
+    if (n == 0) return;
+    if (g.pre == PRE_RMS_ || g.pre == PRE_EMBED_)
+      for (int i = tid; i < g.W.k / 4; i += kT) cp_async16(pn + 4 * i, g.norm_w + 4 * i);
+    for (int i = tid; i < n; i += kT) cp_async4(ps + i, g.W.tile_scale + g.ucta + i * g.uncta);
+  } else if (kind == PH_FFN_SELF || kind == PH_FFN_CROSS) {
+    const bool self = kind == PH_FFN_SELF;
+    const CbMatrix& GU = self ? m.self_layers[layer].gate_up : m.cross_layers[layer].gate_up;
+    const CbSliced& D = self ? m.self_layers[layer].down_ks : m.cross_layers[layer].down_ks;
+    const float* norm2 = self ? m.self_layers[layer].norm2 : m.cross_layers[layer].norm2;
+    const int n = min(ffn_mine(m.ffn_hidden, blockIdx.x, gridDim.x), 16);
+    if (n == 0) return;
+    for (int i = tid; i < m.d_model / 4; i += kT) cp_async16(pn + 4 * i, norm2 + 4 * i);
+    for (int i = tid; i < n; i += kT) {
+      const int j = blockIdx.x + i * gridDim.x;
+      cp_async4(ps + i, GU.tile_scale + j);
+      cp_async4(ps + 16 + i, GU.tile_scale + m.ffn_hidden / kTileRows + j);
+    }
+    if (tid == 0) cp_async4(ps + PS_TSCALE, D.tensor_scale);
+  }
+}
+
+// Warp 0: arm the slot's mbarrier with the phase's byte count and start its copies.
+__device__ void stage_issue(const MkArgs& a, int kind, int layer, uint8_t* slot, unsigned long long* bar) {
+  const int lane = threadIdx.x & 31;
+  unsigned total = 0;
+  phase_chunks(a, kind, layer, [&](int, const uint8_t*, unsigned bytes, int) { total += bytes; });
+  if (lane == 0) {
+    fence_proxy_async();  // the slot's previous contents were read by ordinary loads
+    mbar_expect_arrive(bar, total);
+  }
+  __syncwarp();
+  phase_chunks(a, kind, layer, [&](int i, const uint8_t* src, unsigned bytes, int off) {
+    if ((i & 31) == lane) bulk_copy(slot + off, src, bytes, bar);
+  });
+}
+
 // ------------------------------------------------------------------ kernel
 template <int M>
 __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_constant__ MkArgs a) {
-  extern __shared__ __align__(16) float smem[];
-  __shared__ int s_ok;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) unsigned long long s_bar[2];
+  __shared__ uint16_t s_plan[kMaxPhases];
+  __shared__ int s_np, s_ok, s_live;
+  float* work = reinterpret_cast<float*>(smem + 2 * kSlot);
   unsigned gen = 0;
-  const int cta = blockIdx.x, ncta = gridDim.x, tid = threadIdx.x;
+  const int cta = blockIdx.x, ncta = gridDim.x, tid = threadIdx.x, warp = tid >> 5;
+  const int rank = (int)cluster_rank(), cid = (int)cluster_index();
   const CbModel& m = a.m;
-  const int d = m.d_model, Mrows = a.B * a.T, RQ = a.B * a.nq, F = m.ffn_hidden;
-  const bool sparse = m.sparse_topk > 0;
+  const int d = m.d_model, Mrows = a.B * a.T, RQ = a.B * a.nq;
 
+  if (tid == 0) {
+    s_np = build_plan(m, s_plan);
+    mbar_init(&s_bar[0], 1);
+    mbar_init(&s_bar[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    const unsigned long long lim = __ldcg(&a.ctl->limit_ns);
+    s_wait_limit = lim ? lim : kDefaultWaitNs;
+    const int stall = __ldcg(&a.ctl->stall_barrier);
+    s_stall_barrier = stall > 0 ? (unsigned)stall : 0u;
+    s_live = 1;
+    if (cta == 0) a.trace[0] = gtimer();
+  }
   if (cta == 0) {
     // the histogram exists only with a top-k (dense cross attention carves it empty)
-    if (sparse)
+    if (m.sparse_topk > 0)
       for (int i = tid; i < RQ * kMkHistBins; i += kT) a.hist[i] = 0u;
     for (int i = tid; i < RQ; i += kT) {
       a.hi_cnt[i] = 0;
       a.cand_cnt[i] = 0;
       a.amax[i] = 0ull;
     }
+    for (int i = tid; i < Mrows * d; i += kT) a.hq[i] = 0;  // the embedding is added in the first phase
   }
-  if (cta == 0 && tid == 0) a.trace[0] = gtimer();
-  if (tid == 0) {
-    const unsigned long long lim = __ldcg(&a.ctl->limit_ns);
-    s_wait_limit = lim ? lim : kDefaultWaitNs;
-    const int stall = __ldcg(&a.ctl->stall_barrier);
-    s_stall_barrier = stall > 0 ? (unsigned)stall : 0u;
-  }
-  // Each GEMV's first weights (and residual) are loaded between the arrival at
-  // the barrier before it and the wait there (GemvPre): they do not depend on
-  // the previous phase, so their latency hides behind the barrier.
+  __syncthreads();
+  // bulk-copy phases issued and waited per slot (uniform in the CTA)
+  unsigned issued0 = 0u, issued1 = 0u, waited0 = 0u, waited1 = 0u;
+  const int P = s_np;
+  if (warp == 0) stage_issue(a, s_plan[0] >> 8, s_plan[0] & 0xFF, smem, &s_bar[0]);
+  issued0 = 1;
   grid_arrive(a, gen);
+  bool live = true;
 
-  for (int i = 0; i < m.n_self_layers; ++i) {
-    const CbSelfLayer& L = m.self_layers[i];
-    GemvJob in{};
-    in.W = L.in_proj;
-    in.x = a.h;
-    in.ldx = d;
-    in.pre = i == 0 ? PRE_EMBED_ : PRE_RMS_;
-    in.norm_w = L.norm1;
-    in.y = a.proj;
-    in.ldy = a.ldp;
-    in.rows_out = L.in_proj.rows;
-    in.epi = EPI_STORE_;
-    in.copy_x = i == 0 ? a.h : nullptr;
-    {
-      GemvPre<M> p;
-      gemv_pre<M>(in, Mrows, cta, ncta, smem, p);
-      if (!grid_wait(a, gen, &s_ok)) {
-        cp_async_wait_all();
-        return;
-      }
-      gemv_phase<M>(a, in, Mrows, cta, ncta, smem, p);
+  for (int p = 0; p < P; ++p) {
+    const int kind = s_plan[p] >> 8, layer = s_plan[p] & 0xFF, sl = p & 1;
+    if (live && p + 1 < P) {  // the next phase's weights, into the other slot
+      if (warp == 0) stage_issue(a, s_plan[p + 1] >> 8, s_plan[p + 1] & 0xFF, smem + (sl ^ 1) * kSlot, &s_bar[sl ^ 1]);
+      if (sl) issued0 += 1;
+      else issued1 += 1;
     }
-    if (!grid_sync(a, gen, &s_ok)) return;
-    if (L.kind == CB_LAYER_GDN) gdn_phase(a, L, cta, ncta, smem);
-    else swa_phase(a, L, cta, ncta, smem);
-    grid_arrive(a, gen);
-    GemvJob o{};
-    o.W = L.o_proj;
-    o.x = a.attn;
-    o.ldx = a.att_ld;
-    if (L.kind == CB_LAYER_SWA) {
-      o.pre = PRE_COMBINE_;
-      o.part = a.part;
-      o.S = a.swa_splits;
-      o.hd = m.head_dim;
-      o.gate_x = a.proj;
-      o.gate_ld = a.ldp;
-      o.gate_off = m.swa_off_gate;
+    float st[M];  // the recurrent state of this thread's GDN columns, one value per sequence
+    const bool gdn_here = kind == PH_GDN && cid < m.gdn_heads;
+    if (tid == 0) s_mark_base = kMarkBase + 4 * p;
+    if (live) {
+      if (gdn_here) gdn_preload<M>(a, m.self_layers[layer], cid, rank, st, work);
+      else phase_params(a, kind, layer, work);
     }
-    o.y = a.h;
-    o.ldy = d;
-    o.rows_out = d;
-    o.epi = EPI_ADD_;
-    {
-      GemvPre<M> p;
-      gemv_pre<M>(o, Mrows, cta, ncta, smem, p);
-      if (!grid_wait(a, gen, &s_ok)) {
-        cp_async_wait_all();
-        return;
+    live = grid_wait(a, gen, &s_ok) && live;
+    cp_async_wait_all();  // this phase's parameters
+    __syncthreads();
+    const unsigned iss = sl ? issued1 : issued0, wtd = sl ? waited1 : waited0;
+    if (live && iss > wtd) {
+      const bool ok = mbar_wait(&s_bar[sl], wtd & 1u);
+      if (sl) waited1 += 1;
+      else waited0 += 1;
+      if (!ok && tid == 0) {
+        raise_abort(a);
+        s_live = 0;
       }
-      gemv_phase<M>(a, o, Mrows, cta, ncta, smem, p);
+      __syncthreads();
+      live = s_live != 0;
     }
-    grid_arrive(a, gen);
-    GemvJob gu{};
-    gu.W = L.gate_up;
-    gu.x = a.h;
-    gu.ldx = d;
-    gu.pre = PRE_RMS_;
-    gu.norm_w = L.norm2;
-    gu.y = a.act;
-    gu.ldy = F;
-    gu.rows_out = F;
-    gu.epi = EPI_ACT_;
-    {
-      GemvPre<M> p;
-      gemv_pre<M>(gu, Mrows, cta, ncta, smem, p);
-      if (!grid_wait(a, gen, &s_ok)) {
-        cp_async_wait_all();
-        return;
+    const uint8_t* slot = smem + sl * kSlot;
+    switch (kind) {
+      case PH_GDN:
+        if (gdn_here) gdn_phase<M>(a, m.self_layers[layer], layer == 0, live, cid, rank, st, slot, work);
+        break;
+      case PH_FFN_SELF: {
+        const CbSelfLayer& L = m.self_layers[layer];
+        ffn_phase<M>(a, L.gate_up, L.down_ks, L.norm2, a.hq, Mrows, live, rank, cid, slot, work);
+        break;
       }
-      gemv_phase<M>(a, gu, Mrows, cta, ncta, smem, p);
-    }
-    grid_arrive(a, gen);
-    GemvJob dn{};
-    dn.W = L.down;
-    dn.x = a.act;
-    dn.ldx = F;
-    dn.y = a.h;
-    dn.ldy = d;
-    dn.rows_out = d;
-    dn.epi = EPI_ADD_;
-    {
-      GemvPre<M> p;
-      gemv_pre<M>(dn, Mrows, cta, ncta, smem, p);
-      if (!grid_wait(a, gen, &s_ok)) {
-        cp_async_wait_all();
-        return;
+      case PH_FFN_CROSS: {
+        const CbCrossLayer& L = m.cross_layers[layer];
+        ffn_phase<M>(a, L.gate_up, L.down_ks, L.norm2, a.xq, RQ, live, rank, cid, slot, work);
+        break;
       }
-      gemv_phase<M>(a, dn, Mrows, cta, ncta, smem, p);
+      case PH_SWA_ATT:
+        if (live) swa_phase(a, m.self_layers[layer], work);
+        break;
+      case PH_SH_SCORE:
+        if (live) {
+          shared_append(a, work);
+          if (m.sparse_topk > 0) score_phase(a, work);
+        }
+        break;
+      case PH_SH_COMPACT:
+        if (live) compact_phase(a);
+        break;
+      case PH_CR_ATT:
+        if (live) cross_phase(a, m.cross_layers[layer], work);
+        break;
+      default: {  // GEMV phases
+        if (!live) break;
+        const GemvJob g = gemv_job(a, kind, layer);
+        const int rows = (kind == PH_CR_Q || kind == PH_CR_O || kind == PH_LM_HEAD) ? RQ : Mrows;
+        if (kind == PH_CR_Q && layer == 0 && m.sparse_topk > 0 && cta < RQ) resolve_row(a, cta, work);
+        else gemv_phase<M>(a, g, rows, slot, work);
+        if (kind == PH_LM_HEAD && a.hidden != nullptr && cta == ncta - 1)
+          for (int i = tid; i < RQ * d; i += kT) a.hidden[i] = from_fix(__ldcg(a.xq + i));
+        break;
+      }
     }
     grid_arrive(a, gen);
   }
-
-  {
-    GemvJob sh{};
-    sh.W = m.shared_proj;
-    sh.x = a.h;
-    sh.ldx = d;
-    sh.pre = PRE_RMS_;
-    sh.norm_w = m.shared_norm;
-    sh.y = a.proj;
-    sh.ldy = a.ldp;
-    sh.rows_out = m.shared_proj.rows;
-    sh.epi = EPI_STORE_;
-    GemvPre<M> p;
-    gemv_pre<M>(sh, Mrows, cta, ncta, smem, p);
-    if (!grid_wait(a, gen, &s_ok)) {
-      cp_async_wait_all();
-      return;
-    }
-    gemv_phase<M>(a, sh, Mrows, cta, ncta, smem, p);
-  }
-  if (!grid_sync(a, gen, &s_ok)) return;
-  shared_append(a, cta, ncta, smem);
-  if (sparse) score_phase(a, cta, ncta, smem);
-  grid_arrive(a, gen);
-  if (sparse) {
-    if (!grid_wait(a, gen, &s_ok)) return;
-    compact_phase(a, cta, ncta, smem);
-    grid_arrive(a, gen);
-  }
-
-  for (int j = 0; j < m.n_cross_layers; ++j) {
-    const CbCrossLayer& L = m.cross_layers[j];
-    GemvJob q{};
-    q.W = L.q_gate;
-    q.x = j == 0 ? a.h : a.xc;
-    q.ldx = d;
-    if (j == 0) {
-      q.xmap_nq = a.nq;
-      q.xmap_T = a.T;
-      q.xmap_off = a.T - a.nq;
-      q.copy_x = a.xc;
-    }
-    q.pre = PRE_RMS_;
-    q.norm_w = L.norm1;
-    q.y = a.cproj;
-    q.ldy = a.cr_ld;
-    q.rows_out = L.q_gate.rows;
-    q.epi = EPI_STORE_;
-    {
-      // the exact selection of each query row runs beside the first q projection
-      const bool beside = j == 0 && sparse;
-      const int qc = beside ? cta - RQ : cta, qn = beside ? ncta - RQ : ncta;
-      GemvPre<M> p;
-      gemv_pre<M>(q, RQ, qc, qn, smem, p);
-      if (!grid_wait(a, gen, &s_ok)) {
-        cp_async_wait_all();
-        return;
-      }
-      if (beside && cta < RQ) resolve_row(a, cta, smem);
-      else gemv_phase<M>(a, q, RQ, qc, qn, smem, p);
-    }
-    if (!grid_sync(a, gen, &s_ok)) return;
-    cross_phase(a, L, cta, ncta, smem);
-    grid_arrive(a, gen);
-    GemvJob o{};
-    o.W = L.o_proj;
-    o.x = a.attn;
-    o.ldx = a.att_ld;
-    o.pre = PRE_COMBINE_;
-    o.part = a.part2;
-    o.S = a.cross_splits;
-    o.hd = m.head_dim;
-    o.gate_x = a.cproj;
-    o.gate_ld = a.cr_ld;
-    o.gate_off = m.cr_off_gate;
-    o.y = a.xc;
-    o.ldy = d;
-    o.rows_out = d;
-    o.epi = EPI_ADD_;
-    {
-      GemvPre<M> p;
-      gemv_pre<M>(o, RQ, cta, ncta, smem, p);
-      if (!grid_wait(a, gen, &s_ok)) {
-        cp_async_wait_all();
-        return;
-      }
-      gemv_phase<M>(a, o, RQ, cta, ncta, smem, p);
-    }
-    grid_arrive(a, gen);
-    GemvJob gu{};
-    gu.W = L.gate_up;
-    gu.x = a.xc;
-    gu.ldx = d;
-    gu.pre = PRE_RMS_;
-    gu.norm_w = L.norm2;
-    gu.y = a.act;
-    gu.ldy = F;
-    gu.rows_out = F;
-    gu.epi = EPI_ACT_;
-    {
-      GemvPre<M> p;
-      gemv_pre<M>(gu, RQ, cta, ncta, smem, p);
-      if (!grid_wait(a, gen, &s_ok)) {
-        cp_async_wait_all();
-        return;
-      }
-      gemv_phase<M>(a, gu, RQ, cta, ncta, smem, p);
-    }
-    grid_arrive(a, gen);
-    GemvJob dn{};
-    dn.W = L.down;
-    dn.x = a.act;
-    dn.ldx = F;
-    dn.y = a.xc;
-    dn.ldy = d;
-    dn.rows_out = d;
-    dn.epi = EPI_ADD_;
-    {
-      GemvPre<M> p;
-      gemv_pre<M>(dn, RQ, cta, ncta, smem, p);
-      if (!grid_wait(a, gen, &s_ok)) {
-        cp_async_wait_all();
-        return;
-      }
-      gemv_phase<M>(a, dn, RQ, cta, ncta, smem, p);
-    }
-    grid_arrive(a, gen);
-  }
-
-  {
-    GemvJob hd{};
-    hd.W = m.lm_head;
-    hd.x = a.xc;
-    hd.ldx = d;
-    hd.pre = PRE_RMS_;
-    hd.norm_w = m.final_norm;
-    hd.y = a.logits ? a.logits : a.ws_logits;
-    hd.ldy = m.vocab_size;
-    hd.rows_out = m.vocab_size;
-    hd.epi = EPI_STORE_;
-    hd.argmax = true;
-    GemvPre<M> p;
-    gemv_pre<M>(hd, RQ, cta, ncta, smem, p);
-    if (!grid_wait(a, gen, &s_ok)) {
-      cp_async_wait_all();
-      return;
-    }
-    gemv_phase<M>(a, hd, RQ, cta, ncta, smem, p);
-    if (a.hidden != nullptr && cta == ncta - 1)
-      for (int i = tid; i < RQ * d; i += kT) a.hidden[i] = __ldcg(a.xc + i);
-  }
-  if (!grid_sync(a, gen, &s_ok)) return;
-  if (cta == 0) {
+  live = grid_wait(a, gen, &s_ok) && live;
+  if (live && cta == 0) {
     if (a.argmax != nullptr)
       for (int r = tid; r < RQ; r += kT)
         a.argmax[r] = (int32_t)(0xFFFFFFFFu - (unsigned)(__ldcg(a.amax + r) & 0xFFFFFFFFull));
     for (int b = tid; b < a.B; b += kT) a.c.pos[b] += a.T;
   }
+  // copies still in flight after an abort land before the CTA exits (bounded)
+  for (; waited0 < issued0; ++waited0) mbar_wait(&s_bar[0], waited0 & 1u);
+  for (; waited1 < issued1; ++waited1) mbar_wait(&s_bar[1], waited1 & 1u);
 }
 
 }  // namespace
 
 size_t mk_smem_bytes() { return kSmem; }
 
+int mk_swa_splits(const CbModel& m) { return ceil_div(m.swa_window + CB_MAX_T, kMkSwaSplit); }
+
+static bool sliced_ok(const CbSliced& s, int rows, int k, int width) {
+  return s.data != nullptr && s.tensor_scale != nullptr && s.rows == rows && s.k == k && s.width == width &&
+         (reinterpret_cast<uintptr_t>(s.data) & 15) == 0;
+}
+
 bool mk_supported(const CbModel& m, const CbCache& c, int T, int nq) {
-  const int G = m.n_q_heads / m.n_kv_heads;
+  const int G = m.n_q_heads / m.n_kv_heads, d = m.d_model;
   if (c.batch * T > kMkMaxRows || T > CB_MAX_T || nq < 1 || nq > T) return false;
   if (m.head_dim > 128 || m.head_dim % 8 || G * T > kMkMaxQ) return false;
-  if (m.gdn_dv > kMkThreads || kMkThreads % m.gdn_dv || m.gdn_dk * m.gdn_dv / kMkThreads > 32) return false;
-  if ((m.gdn_dk * m.gdn_dv) % kMkThreads && m.gdn_dk * m.gdn_dv > kMkThreads) return false;
+  if (d > kMkMaxD || d % 16 || m.ffn_hidden % kTileRows || m.ffn_hidden > 2048) return false;
+  if (m.n_q_heads * m.head_dim > kMkMaxD) return false;
   if (m.conv_size != 4) return false;
-  if (m.d_model > 2048 || m.ffn_hidden > 2048 || m.d_model % 16 || m.ffn_hidden % 16) return false;
   if (m.sparse_topk > 0 && c.max_ctx > kMkBitmapWords * 32) return false;
   if (m.sparse_topk > 0 && (m.sparse_topk + 1 > kMaxSort || m.indexer_dim % 8 || m.indexer_dim > 256 ||
                             m.indexer_heads > 16 || (m.indexer_heads * m.indexer_dim + 16 + kMkHistBins) * 4 +
-                            CB_MAX_T * m.indexer_dim > kSmem))
+                            CB_MAX_T * m.indexer_dim > kWork))
     return false;
   const size_t att = sizeof(float) * ((size_t)kMkSwaSplit * (2 * m.head_dim + 1) + (size_t)kMkMaxQ * m.head_dim * 2 +
                                       (size_t)kMkMaxQ * kMkSwaSplit) +
                      sizeof(uint16_t) * 2 * kMkSwaSplit * m.head_dim;
-  if (att > (size_t)kSmem) return false;
-  if ((size_t)kMkMaxRows * 2048 * sizeof(float) > (size_t)kSmem) return false;
-  {  // GEMV staging ([M][K] inputs, K <= 2048) stays below the preload slots at kPreOff
-    int kmax = std::max(m.lm_head.k, m.shared_proj.k);
-    for (int i = 0; i < m.n_self_layers; ++i) {
-      const CbSelfLayer& L = m.self_layers[i];
-      kmax = std::max({kmax, L.in_proj.k, L.o_proj.k, L.gate_up.k, L.down.k});
+  if (att > (size_t)kWork) return false;
+  if (mk_swa_splits(m) > 32) return false;
+  if (m.sparse_topk > 0 && ceil_div(m.sparse_topk + 1, kMkCrossSplit) > 32) return false;
+  // GEMV staging: [M][K] inputs (+ [M][H][32] split weights for the o projections)
+  if ((size_t)kMkMaxRows * (kMkMaxD + m.n_q_heads * 32) * sizeof(float) > (size_t)kPreOff) return false;
+  // FFN: [8][M][d/8] partials + [M][d] inputs + [M][16]
+  if ((size_t)kMkMaxRows * (2 * d + 16) * sizeof(float) > (size_t)kPreOff) return false;
+  const int64_t tb = tile_bytes(d);
+  for (int i = 0; i < m.n_self_layers; ++i) {
+    const CbSelfLayer& L = m.self_layers[i];
+    if (L.in_proj.k != d || L.gate_up.k != d || L.o_proj.rows < d || L.down.rows < d) return false;
+    if (!sliced_ok(L.down_ks, d, m.ffn_hidden, 16)) return false;
+    if (L.kind == CB_LAYER_GDN) {
+      const int Dk = m.gdn_dk, Dv = m.gdn_dv, vpr = Dv / kCl;
+      if (Dk % 16 || Dv % 16 || Dk > 64 || Dk * vpr > kMkThreads || vpr > kW) return false;
+      if (m.gdn_off_gate % 16 || m.gdn_off_a % 16 || m.gdn_off_b % 16) return false;
+      if (!sliced_ok(L.o_proj_ks, d, m.gdn_heads * Dv, vpr)) return false;
+      const int ntile = (2 * Dk + 2 * Dv) / kTileRows;
+      const int64_t slice = ((int64_t)d * (vpr / 2 + 1) + 15) / 16 * 16;
+      if ((int64_t)(ceil_div(ntile, kCl) + 2) * tb + slice > kSlot) return false;
+      // GDN working memory before the preload region; conv taps and windows after it
+      const size_t w = sizeof(float) * ((size_t)kMkMaxRows * (2 * Dk + 2 * Dv + 2) + kCl * kMkMaxRows +
+                                        (size_t)kMkMaxRows * 2 * d + (size_t)kMkMaxRows * (2 * Dk + 2 * vpr) +
+                                        kT + kW + 2 * kMkMaxRows + 32);  // + 16-byte padding of each array
+      const size_t pre = sizeof(float) * ((size_t)kParConv + (size_t)(2 * Dk + vpr) * (4 + 3 * c.batch));
+      if (w > (size_t)kPreOff || pre > (size_t)(kWork - kPreOff) || vpr > 16) return false;
     }
-    for (int j = 0; j < m.n_cross_layers; ++j) {
-      const CbCrossLayer& L = m.cross_layers[j];
-      kmax = std::max({kmax, L.q_gate.k, L.o_proj.k, L.gate_up.k, L.down.k});
-    }
-    if (kmax > 2048 || (size_t)kMkMaxRows * (kmax + m.n_q_heads * 32) * sizeof(float) > (size_t)kPreOff) return false;
   }
-  {  // o projection staging with the split merge: [M][K] inputs + [M][H][32] weights, S <= 32 splits
-    const int sw = ceil_div(m.swa_window + CB_MAX_T, kMkSwaSplit);
-    const int sc = m.sparse_topk > 0 ? ceil_div(m.sparse_topk + 1, kMkCrossSplit) : 32;
-    const size_t need = (size_t)kMkMaxRows * m.n_q_heads * (m.head_dim + 32) * sizeof(float);
-    if (need > (size_t)kSmem || sw > 32 || sc > 32) return false;
+  for (int j = 0; j < m.n_cross_layers; ++j) {
+    const CbCrossLayer& L = m.cross_layers[j];
+    if (L.q_gate.k != d || L.gate_up.k != d) return false;
+    if (!sliced_ok(L.down_ks, d, m.ffn_hidden, 16)) return false;
   }
+  if (m.lm_head.k != d || m.shared_proj.k != d) return false;
   return true;
 }
 
-int launch_mk(const MkArgs& a, int grid, cudaStream_t st) {
+int launch_mk(const MkArgs& a, cudaStream_t st) {
   const int M = a.B * a.T;
   void (*fn)(MkArgs);
   if (M <= 1) fn = decode_mk_kernel<1>;
@@ -1558,18 +2018,35 @@ int launch_mk(const MkArgs& a, int grid, cudaStream_t st) {
   else if (M <= 4) fn = decode_mk_kernel<4>;
   else fn = decode_mk_kernel<8>;
   if (ensure_smem_attr((const void*)fn, kSmem) != CB_OK) return CB_ERR_CUDA;
-  if (resident_ctas((const void*)fn, kMkThreads, kSmem) < 1) return CB_ERR_SHAPE;  // the grid could not be co-resident
+  const int ncl = std::min(resident_clusters((const void*)fn, kMkThreads, kSmem, kCl), kMkMaxClusters);
+  // every GDN head needs a cluster, and the first cross layer needs CTAs beyond the query rows
+  if (ncl < a.m.gdn_heads || ncl * kCl <= a.B * a.nq) return CB_ERR_SHAPE;
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = dim3(ncl * kCl);
   cfg.blockDim = dim3(kMkThreads);
   cfg.dynamicSmemBytes = kSmem;
   cfg.stream = st;
-  cudaLaunchAttribute attrs[1];
-  attrs[0].id = cudaLaunchAttributeCooperative;
-  attrs[0].val.cooperative = 1;
+  cudaLaunchAttribute attrs[2];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = kCl;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  attrs[1].id = cudaLaunchAttributeCooperative;
+  attrs[1].val.cooperative = 1;
   cfg.attrs = attrs;
-  cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, a);
+  // A cooperative launch guarantees co-residency.  Where the runtime does not
+  // combine it with clusters, the plain cluster launch runs the same grid: every
+  // cluster fits at once (the count comes from the occupancy query), and the
+  // bounded waits end a launch whose CTAs are not all resident.
+  const bool coop = cooperative_clusters_ok();
+  cfg.numAttrs = coop ? 2 : 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fn, a);
+  if (e != cudaSuccess && coop) {
+    (void)cudaGetLastError();
+    note_cooperative_clusters_refused();
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, fn, a);
+  }
   count_launch();
   return e == cudaSuccess ? CB_OK : CB_ERR_CUDA;
 }

@@ -28,6 +28,8 @@ void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 struct Workspace {
   int32_t* status;
+  long long* hq;   // persistent kernel: fixed-point residual streams
+  long long* xq;
   float* h;
   float* proj;
   float* attn;
@@ -70,7 +72,7 @@ static Workspace carve(const CbModel& m, int batch, int T, int max_ctx, char* ba
   w.ldp = ldp;
   w.att_ld = std::max(m.gdn_heads * m.gdn_dv, m.n_q_heads * m.head_dim);
   w.cr_ld = m.n_cross_layers > 0 ? m.cross_layers[0].q_gate.rows : 16;
-  w.n_splits = swa_splits(m);
+  w.n_splits = std::max(swa_splits(m), mk_swa_splits(m));  // the larger of the two paths' split counts
   w.sel_ld = std::max(m.sparse_topk, 1) + 1;
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -79,6 +81,8 @@ static Workspace carve(const CbModel& m, int batch, int T, int max_ctx, char* ba
     return base ? base + o : nullptr;
   };
   w.status = (int32_t*)take(256);
+  w.hq = (long long*)take(sizeof(long long) * R * m.d_model);
+  w.xq = (long long*)take(sizeof(long long) * R * m.d_model);
   w.h = (float*)take(sizeof(float) * R * m.d_model);
   w.proj = (float*)take(sizeof(float) * R * ldp);
   w.attn = (float*)take(sizeof(float) * R * w.att_ld);
@@ -162,11 +166,10 @@ static int launch_persistent(const CbModel& m, const CbCache& c, const Workspace
   MkArgs a{};
   a.m = m;
   a.c = c;
-  a.h = w.h;
+  a.hq = w.hq;
+  a.xq = w.xq;
   a.proj = w.proj;
-  a.attn = w.attn;
   a.act = w.gu;
-  a.xc = w.xc;
   a.cproj = w.cproj;
   a.part = w.part;
   a.part2 = w.part2;
@@ -182,13 +185,12 @@ static int launch_persistent(const CbModel& m, const CbCache& c, const Workspace
   a.amax = w.amax64;
   a.sync = w.sync;
   a.trace = w.trace;
-  a.abort_flag = reinterpret_cast<int32_t*>(w.sync + 32);
   a.status = w.status;
   a.ldp = w.ldp;
   a.att_ld = w.att_ld;
   a.cr_ld = w.cr_ld;
   a.sel_ld = w.sel_ld;
-  a.swa_splits = ceil_div(m.swa_window + CB_MAX_T, kMkSwaSplit);
+  a.swa_splits = mk_swa_splits(m);
   a.cross_splits = w.cross_splits;
   a.ids = ids;
   a.ids_ld = T;
@@ -201,7 +203,7 @@ static int launch_persistent(const CbModel& m, const CbCache& c, const Workspace
   a.argmax = argmax;
   a.ctl = reinterpret_cast<const WaitCtl*>(w.status);
   if (cudaMemsetAsync(w.sync, 0, 256, st) != cudaSuccess) return CB_ERR_CUDA;
-  return launch_mk(a, num_sms(), st);
+  return launch_mk(a, st);
 }
 
 static int validate(const CbModel& m, const CbCache& c) {
@@ -349,6 +351,12 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
         g.conv_stride = (int64_t)c.n_gdn * gdn_conv_layer;
         g.out = w.attn;
         g.ldo = w.att_ld;
+        if (c.snap_state && c.snap_conv && tc > 1 && T <= CB_MAX_T) {
+          g.snap_state = c.snap_state + (int64_t)L.slot * gdn_S_layer;
+          g.snap_state_t = (int64_t)B * c.n_gdn * gdn_S_layer;
+          g.snap_conv = c.snap_conv + (int64_t)L.slot * gdn_conv_layer;
+          g.snap_conv_t = (int64_t)B * c.n_gdn * gdn_conv_layer;
+        }
         g.batch = B;
         g.T = tc;
         g.H = H;

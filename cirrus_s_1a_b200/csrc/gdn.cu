@@ -48,6 +48,9 @@ __global__ void __launch_bounds__(kGdnThreads) gdn_step_kernel(GdnParams p) {
       for (int j = 0; j < KC; ++j) y += win[j] * w[j];
       dst[t * dstride + di] = silu(y);
       for (int j = 0; j < KC - 1; ++j) win[j] = win[j + 1];
+      if (p.snap_conv && t < T - 1)  // the window after token t
+        for (int j = 0; j < KC - 1; ++j)
+          p.snap_conv[t * p.snap_conv_t + (int64_t)b * p.conv_stride + (int64_t)j * p.C + ch] = win[j];
     }
     for (int j = 0; j < KC - 1; ++j) conv[(int64_t)j * p.C + ch] = win[j];
   }
@@ -105,6 +108,11 @@ __global__ void __launch_bounds__(kGdnThreads) gdn_step_kernel(GdnParams p) {
       float o = 0.0f;
       for (int g = 0; g < n_kg; ++g) o += red[g * Dv + v];
       os[t * Dv + v] = o * p.scale;
+    }
+    if (p.snap_state && t < T - 1) {  // the state after token t
+      float* Sn = p.snap_state + t * p.snap_state_t + (int64_t)b * p.state_stride + (int64_t)h * Dk * Dv;
+#pragma unroll
+      for (int i = 0; i < KPT; ++i) Sn[(int64_t)(kg * KPT + i) * Dv + v] = s[i];
     }
     __syncthreads();
   }

@@ -20,6 +20,10 @@ struct GdnParams {
   int64_t state_stride;
   float* conv;         // sequence 0 of this layer: [KC-1][C]
   int64_t conv_stride;
+  float* snap_state;   // per-token snapshots (null = off): + t * snap_state_t, same offsets as state
+  int64_t snap_state_t;
+  float* snap_conv;    // + t * snap_conv_t, same offsets as conv
+  int64_t snap_conv_t;
   float* out;          // [batch*T][ldo]
   int ldo;
   int batch, T, H, Dk, Dv, C, KC;

@@ -9,11 +9,16 @@
 namespace cb {
 
 constexpr int kMkThreads = 512;
+constexpr int kMkCluster = 8;          // CTAs per thread-block cluster
+constexpr int kMkMaxClusters = 18;     // 144 CTAs at most
+constexpr int kMkSlotBytes = 56 * 1024;   // two weight-staging slots (8 tiles of K = 768 each)
+constexpr int kMkWorkBytes = 108 * 1024;  // per-phase working memory, parameter region at its end
 constexpr int kMkHistBins = 2048;      // top 11 bits of the score key
-constexpr int kMkSwaSplit = 128;       // window keys per SWA work item
+constexpr int kMkSwaSplit = 80;        // window keys per SWA work item (and key chunk of cross attention)
 constexpr int kMkCrossSplit = 64;      // selected keys per cross-attention work item
 constexpr int kMkMaxRows = 8;          // batch * T handled by one persistent launch
-constexpr int kMkMaxQ = 24;            // (q heads per KV head) * T per SWA work item
+constexpr int kMkMaxQ = 24;            // (q heads per KV head) * T per attention work item
+constexpr int kMkMaxD = 1024;          // d_model and every GEMV K the kernel stages
 constexpr int kMkTrace = 512;          // phase timestamps
 constexpr unsigned long long kDefaultWaitNs = 200ull * 1000 * 1000;  // bounded-wait limit when none is set
 
@@ -30,11 +35,10 @@ struct MkArgs {
   CbModel m;
   CbCache c;
   // workspace
-  float* h;          // [M][d] residual stream of the self-decoder
-  float* proj;       // [M][ldp]
-  float* attn;       // [M][att_ld]
-  float* act;        // [M][ffn]   silu(gate) * up
-  float* xc;         // [RQ][d]   cross-decoder residual stream
+  long long* hq;     // [M][d] self-decoder residual stream, fixed point (value * 2^32)
+  long long* xq;     // [RQ][d] cross-decoder residual stream, fixed point
+  float* proj;       // [M][ldp] in-projection outputs (SWA, shared KV)
+  float* act;        // unused scratch kept for the workspace layout
   float* cproj;      // [RQ][cr_ld]
   float* part;       // SWA partials [M][Hq][swa_splits][hd + 2]
   float* part2;      // cross partials [RQ][Hq][cross_splits][hd + 2]
@@ -50,7 +54,6 @@ struct MkArgs {
   unsigned long long* amax;  // [RQ] packed argmax
   unsigned* sync;    // grid barrier counter (zeroed before every launch)
   unsigned long long* trace;  // [kMkTrace] phase timestamps of CTA 0
-  int32_t* abort_flag;
   int32_t* status;
   int ldp, att_ld, cr_ld, sel_ld, swa_splits, cross_splits;
   // this launch
@@ -63,7 +66,8 @@ struct MkArgs {
 };
 
 size_t mk_smem_bytes();
+int mk_swa_splits(const CbModel& m);
 bool mk_supported(const CbModel& m, const CbCache& c, int T, int nq);
-int launch_mk(const MkArgs& a, int grid, cudaStream_t st);
+int launch_mk(const MkArgs& a, cudaStream_t st);
 
 }  // namespace cb

@@ -416,6 +416,38 @@ extern "C" int cb_nvfp4_quantize(const float* w, int32_t n, int32_t k, float ten
   return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
 }
 
+namespace cb {
+// Column slices of `width` columns: slice s = [n][width/2 code bytes] then
+// [n][1 scale byte] (the E4M3 scale of the 16-column block holding the slice).
+__global__ void pack_slices_kernel(const uint8_t* __restrict__ codes, const uint8_t* __restrict__ scales, int n, int k,
+                                   int width, int64_t slice_bytes, uint8_t* __restrict__ out) {
+  const int cb = width / 2, ns = k / width;
+  const int64_t total = (int64_t)ns * n;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int s = (int)(i / n), r = (int)(i - (int64_t)s * n);
+    uint8_t* dst = out + s * slice_bytes;
+    for (int j = 0; j < cb; ++j) dst[(int64_t)r * cb + j] = codes[(int64_t)r * (k / 2) + s * cb + j];
+    dst[(int64_t)n * cb + r] = scales[(int64_t)r * (k / 16) + (s * width) / 16];
+    if (r == 0)  // zero the padding after the scales
+      for (int64_t j = (int64_t)n * (cb + 1); j < slice_bytes; ++j) dst[j] = 0;
+  }
+}
+}  // namespace cb
+
+extern "C" int64_t cb_nvfp4_slice_bytes(int32_t n, int32_t width) {
+  if (n <= 0 || (width != 2 && width != 4 && width != 8 && width != 16)) return 0;
+  return ((int64_t)n * (width / 2 + 1) + 15) / 16 * 16;
+}
+
+extern "C" int cb_nvfp4_pack_slices(const uint8_t* codes, const uint8_t* scales, int32_t n, int32_t k, int32_t width,
+                                    uint8_t* out, void* stream) {
+  const int64_t sb = cb_nvfp4_slice_bytes(n, width);
+  if (!codes || !scales || !out || sb == 0 || k <= 0 || k % 16 || k % width) return CB_ERR_ARG;
+  pack_slices_kernel<<<num_sms() * 4, 256, 0, (cudaStream_t)stream>>>(codes, scales, n, k, width, sb, out);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
+
 extern "C" int cb_nvfp4_pack_tiles(const uint8_t* codes, const uint8_t* scales, int32_t n, int32_t k, uint8_t* tiles,
                                    void* stream) {
   if (!codes || !scales || !tiles || n <= 0 || k <= 0 || k % 16) return CB_ERR_ARG;

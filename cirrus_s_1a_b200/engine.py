@@ -23,7 +23,8 @@ from dataclasses import dataclass, field
 import torch
 
 from cirrus_s_1a_b200 import _lib
-from cirrus_s_1a_b200._lib import CB_LAYER_GDN, CB_LAYER_SWA, CB_MAX_T, CB_SWA_EXTRA, CbCache, CbMatrix, CbModel
+from cirrus_s_1a_b200._lib import (CB_LAYER_GDN, CB_LAYER_SWA, CB_MAX_T, CB_SWA_EXTRA, CbCache, CbMatrix, CbModel,
+                                   CbMtp, CbSliced)
 
 
 def pad16(n: int) -> int:
@@ -79,6 +80,32 @@ class PackedMatrix:
         return CbMatrix(self.tiles.data_ptr(), self.tile_scale.data_ptr(), self.rows, self.k)
 
 
+class SlicedMatrix:
+    """A column-sliced NVFP4 copy of one matrix (``CbSliced``): the persistent
+    kernel's split-K phases read one slice of ``width`` columns per CTA."""
+
+    def __init__(self, weight, width: int, device, tensor_scale: float = 1.0):
+        n, k = weight.shape
+        L = _lib.lib()
+        self.width, self.rows, self.k = width, n, k
+        sb = L.cb_nvfp4_slice_bytes(n, width)
+        if sb <= 0 or k % width or k % 16:
+            raise ValueError(f"cannot slice a [{n}, {k}] matrix into {width}-column slices")
+        st = _stream_ptr(device)
+        wd = weight.detach().to(device=device, dtype=torch.float32).contiguous()
+        codes = torch.empty(n, k // 2, dtype=torch.uint8, device=device)
+        scales = torch.empty(n, k // 16, dtype=torch.uint8, device=device)
+        _lib.check(L.cb_nvfp4_quantize(wd.data_ptr(), n, k, float(tensor_scale), codes.data_ptr(), scales.data_ptr(),
+                                       st), "cb_nvfp4_quantize")
+        self.data = torch.empty(k // width * sb, dtype=torch.uint8, device=device)
+        _lib.check(L.cb_nvfp4_pack_slices(codes.data_ptr(), scales.data_ptr(), n, k, width, self.data.data_ptr(), st),
+                   "cb_nvfp4_pack_slices")
+        self.scale = torch.full((1,), float(tensor_scale), dtype=torch.float32, device=device)
+
+    def struct(self) -> CbSliced:
+        return CbSliced(self.data.data_ptr(), self.scale.data_ptr(), self.rows, self.k, self.width)
+
+
 class DeviceModel:
     """NVFP4 weights of one model on one CUDA device plus its ``CbModel`` descriptor."""
 
@@ -117,6 +144,11 @@ class DeviceModel:
             self._keep.append(pm)
             return pm
 
+        def sliced(name, width):
+            sm = SlicedMatrix(sd[name], width, dev, tensor_scale)
+            self._keep.append(sm)
+            return sm.struct()
+
         H, dk, dv = cfg.gdn_heads, cfg.gdn_head_dim_k, cfg.gdn_head_dim_v
         n_gdn = n_swa = 0
         gdn_offs = swa_offs = None
@@ -135,6 +167,8 @@ class DeviceModel:
                 gdn_offs = pm.offsets
                 L.in_proj = pm.struct()
                 L.o_proj = pack(p + "mixer.o_proj.weight").struct()
+                if dv % 16 == 0:
+                    L.o_proj_ks = sliced(p + "mixer.o_proj.weight", dv // 8)
                 L.conv_w = keep(sd[p + "mixer.conv.weight"])
                 L.A_log = keep(sd[p + "mixer.A_log"])
                 L.dt_bias = keep(sd[p + "mixer.dt_bias"])
@@ -150,6 +184,7 @@ class DeviceModel:
                 L.k_norm = keep(sd[p + "mixer.k_norm.weight"])
             L.gate_up = pack(p + "ffn.gate_up.weight").struct()
             L.down = pack(p + "ffn.down.weight").struct()
+            L.down_ks = sliced(p + "ffn.down.weight", 16)
         if gdn_offs is not None:
             m.gdn_off_gate, m.gdn_off_a, m.gdn_off_b = gdn_offs[1], gdn_offs[2], gdn_offs[3]
         if swa_offs is not None:
@@ -175,12 +210,33 @@ class DeviceModel:
             L.o_proj = pack(p + "mixer.o_proj.weight").struct()
             L.gate_up = pack(p + "ffn.gate_up.weight").struct()
             L.down = pack(p + "ffn.down.weight").struct()
+            L.down_ks = sliced(p + "ffn.down.weight", 16)
             L.q_norm = keep(sd[p + "mixer.q_norm.weight"])
         m.final_norm = keep(sd["final_norm.weight"])
         self.lm_head = pack("lm_head.weight")
         m.lm_head = self.lm_head.struct()
         self.desc = m
+        # the first MTP module and the FR-Spec draft head (the embedding rows of draft_ids)
+        self.mtp = None
+        if getattr(cfg, "n_mtp_heads", 0) > 0 and "mtp.0.proj.weight" in sd:
+            ids = sd.get("draft_ids", torch.arange(min(cfg.mtp_draft_vocab, cfg.vocab_size)))
+            ids = ids.detach().to(torch.int64).cpu()
+            t = CbMtp()
+            t.norm_h, t.norm_e = keep(sd["mtp.0.norm_h.weight"]), keep(sd["mtp.0.norm_e.weight"])
+            t.ffn_norm = keep(sd["mtp.0.ffn_norm.weight"])
+            t.proj = pack("mtp.0.proj.weight").struct()
+            t.gate_up = pack("mtp.0.ffn.gate_up.weight").struct()
+            t.down = pack("mtp.0.ffn.down.weight").struct()
+            head = PackedMatrix([sd["lm_head.weight"].detach().float()[ids]], dev, tensor_scale)
+            self._keep.append(head)
+            t.draft_head = head.struct()
+            self.draft_ids = ids.to(device=dev, dtype=torch.int32)
+            t.draft_ids, t.n_draft = self.draft_ids.data_ptr(), int(ids.numel())
+            self.mtp = t
         packed = [x for x in self._keep if isinstance(x, PackedMatrix)]
+        if self.mtp is not None:  # the decode step streams every weight but the MTP module and its draft head
+            mtp_ptrs = {self.mtp.proj.tiles, self.mtp.gate_up.tiles, self.mtp.down.tiles, self.mtp.draft_head.tiles}
+            packed = [x for x in packed if x.tiles.data_ptr() not in mtp_ptrs]
         self.weight_bytes = sum(x.tiles.numel() for x in packed)
         self.weight_real_bytes = sum(x.real_bytes for x in packed)
         torch.cuda.synchronize(dev)
@@ -222,6 +278,20 @@ class DeviceCache:
             self.swa_k, self.swa_v = _share.swa_k, _share.swa_v
             self.kv_k, self.kv_v, self.kv_ik = _share.kv_k, _share.kv_v, _share.kv_ik
             self.pos_host = list(_share.pos_host)
+        self.snap_state = self.snap_conv = None
+        self._struct = None
+
+    def enable_snapshots(self, tokens: int) -> None:
+        """Allocate per-token GDN snapshots for verify forwards of up to ``tokens``
+        tokens (``CbCache.snap_state`` / ``snap_conv``): a forward then also
+        records the recurrent state after each of its first ``tokens - 1`` tokens."""
+        if tokens > CB_MAX_T:
+            raise ValueError(f"a verify forward takes at most {CB_MAX_T} tokens")
+        n = max(tokens - 1, 1)
+        self.snap_state = torch.zeros((n,) + tuple(self.gdn_state.shape), dtype=torch.float32,
+                                      device=self.gdn_state.device)
+        self.snap_conv = torch.zeros((n,) + tuple(self.gdn_conv.shape), dtype=torch.float32,
+                                     device=self.gdn_conv.device)
         self._struct = None
 
     @property
@@ -241,6 +311,8 @@ class DeviceCache:
                                               self.gdn_conv.data_ptr())
             s.swa_k, s.swa_v = self.swa_k.data_ptr(), self.swa_v.data_ptr()
             s.kv_k, s.kv_v, s.kv_ik = self.kv_k.data_ptr(), self.kv_v.data_ptr(), self.kv_ik.data_ptr()
+            if self.snap_state is not None:
+                s.snap_state, s.snap_conv = self.snap_state.data_ptr(), self.snap_conv.data_ptr()
             self._struct = s
         return self._struct
 
@@ -386,6 +458,33 @@ class CirrusB200:
             out.append((i, (arrive - prev) / 1e3, (leave - arrive) / 1e3))
             prev = leave
         return out
+
+    # ----------------------------------------------------------- MTP draft
+    @torch.no_grad()
+    def mtp_draft(self, h_last: torch.Tensor, token, n: int | None = None) -> list:
+        """``CirrusModel.mtp_draft`` (``model.py:230-245``): ``n`` (default
+        ``cfg.mtp_passes``) draft tokens after ``token`` from the first MTP module
+        and the FR-Spec draft head, computed on the device (``cb_mtp_draft``).
+        ``h_last``: [1, d] hidden that predicted ``token`` (``Output.hidden[:, -1]``)."""
+        t = self.model.mtp
+        if t is None:
+            return []
+        n = self.cfg.mtp_passes if n is None else int(n)
+        L = _lib.lib()
+        dev = self.device
+        with torch.cuda.device(dev):
+            h = h_last.detach().to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+            if h.numel() != self.cfg.d_model:
+                raise ValueError("h_last must hold one d_model vector")
+            tok = torch.as_tensor(token).reshape(-1)[:1].to(device=dev, dtype=torch.int32)
+            out = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+            if getattr(self, "_mtp_ws", None) is None:
+                nbytes = L.cb_mtp_workspace_bytes(C.byref(self.model.desc), C.byref(t))
+                self._mtp_ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+            _lib.check(L.cb_mtp_draft(C.byref(self.model.desc), C.byref(t), h.data_ptr(), tok.data_ptr(), n,
+                                      out.data_ptr(), self._mtp_ws.data_ptr(), self._mtp_ws.numel(),
+                                      _stream_ptr(dev)), "cb_mtp_draft")
+            return out[:n].tolist()
 
     # ----------------------------------------------------------- forward
     @torch.no_grad()

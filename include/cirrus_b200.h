@@ -13,6 +13,7 @@
  *   cb_nvfp4_quantize     (no quantiser in the reference; the NVFP4 format is
  *                          cirrus/perf/bench_kernels.cu:141-145)
  *   cb_nvfp4_pack_tiles   pack_nvfp4_mma / pack_nvfp4_v3  scripts/bench_spark.py:369-391, 639-660
+ *   cb_nvfp4_pack_slices  (same packers: a column-sliced layout of the standard format)
  *   cb_gemv_nvfp4         nvfp4_gemv                     cirrus/perf/bench_kernels.cu:202-227
  *   cb_verify_gemm_nvfp4  nvfp4_gemv, M = 2..16 (verify)  cirrus/perf/bench_kernels.cu:202-227, 1079-1300
  *   cb_gdn_chunk_prefill  chunk_gated_delta_rule (fla)    cirrus/model/layers.py:165-170 (recurrence :108-129)
@@ -32,7 +33,7 @@
 extern "C" {
 #endif
 
-#define CB_ABI_VERSION 2
+#define CB_ABI_VERSION 3
 #define CB_MAX_SELF 32   /* self-decoder layers */
 #define CB_MAX_CROSS 16  /* cross-decoder layers */
 #define CB_MAX_T 8       /* tokens per sequence per launch chunk (1 + draft) */
@@ -68,6 +69,18 @@ typedef struct CbMatrix {
   int32_t k;            /* multiple of 16 */
 } CbMatrix;
 
+/* A second copy of an NVFP4 matrix cut into column slices of `width` columns
+ * (width 2, 4, 8 or 16), for the split-K phases of the persistent kernel: slice
+ * s holds, for every row r, the width/2 code bytes of columns [s*width,
+ * (s+1)*width) of row r, then for every row the E4M3 scale byte of the 16-column
+ * block that contains those columns; each slice is padded to a multiple of 16
+ * bytes (cb_nvfp4_slice_bytes).  tensor_scale points at the float32 tensor scale. */
+typedef struct CbSliced {
+  const uint8_t* data;
+  const float* tensor_scale;
+  int32_t rows, k, width;
+} CbSliced;
+
 typedef struct CbSelfLayer {
   int32_t kind;         /* CB_LAYER_GDN or CB_LAYER_SWA */
   int32_t slot;         /* index among the GDN layers, or among the SWA layers */
@@ -83,6 +96,8 @@ typedef struct CbSelfLayer {
   const float* o_norm;  /* GDN [dv] */
   const float* q_norm;  /* SWA [head_dim] */
   const float* k_norm;  /* SWA [head_dim] */
+  CbSliced o_proj_ks;   /* GDN: o_proj in slices of gdn_dv/8 columns (the persistent kernel's split-K o-projection) */
+  CbSliced down_ks;     /* down in slices of 16 columns (the persistent kernel's split-K FFN) */
 } CbSelfLayer;
 
 typedef struct CbCrossLayer {
@@ -93,6 +108,7 @@ typedef struct CbCrossLayer {
   CbMatrix gate_up;
   CbMatrix down;
   const float* q_norm;  /* [head_dim] */
+  CbSliced down_ks;     /* down in slices of 16 columns */
 } CbCrossLayer;
 
 typedef struct CbModel {
@@ -125,7 +141,12 @@ typedef struct CbModel {
  * model.py:41-51).  pos[b] = tokens already in the cache.  SWA keys live in a
  * ring of swa_slots = swa_window + CB_SWA_EXTRA rows, slot = position % swa_slots;
  * the shared KV rows are indexed by position.  Rows at positions >= pos[b]
- * are scratch: a forward that is later discarded may write them. */
+ * are scratch: a forward that is later discarded may write them.
+ * snap_state / snap_conv (may be null): when set, a forward of T > 1 tokens
+ * also writes the GDN state and conv window after each of its first T - 1
+ * tokens, [CB_MAX_T - 1][batch][n_gdn][...] in the layouts of gdn_state /
+ * gdn_conv, so that a verify can be rewound to any accepted prefix
+ * (cb_spec_accept) without running it again. */
 typedef struct CbCache {
   int32_t batch, max_ctx, swa_slots, n_gdn, n_swa;
   int32_t* pos;        /* device [batch] */
@@ -136,6 +157,8 @@ typedef struct CbCache {
   uint16_t* kv_k;      /* bf16 [batch][max_ctx][n_kv_heads][head_dim] */
   uint16_t* kv_v;
   uint8_t* kv_ik;      /* E4M3 [batch][max_ctx][indexer_dim] */
+  float* snap_state;   /* [CB_MAX_T-1][batch][n_gdn][H][dk][dv] or null */
+  float* snap_conv;    /* [CB_MAX_T-1][batch][n_gdn][conv_size-1][C] or null */
 } CbCache;
 
 int cb_abi_version(void);
@@ -148,6 +171,14 @@ const char* cb_status_string(int code);
  * (w/tensor_scale)/scale, saturating; zero scale -> zero codes. */
 int cb_nvfp4_quantize(const float* w, int32_t n, int32_t k, float tensor_scale, uint8_t* codes,
                       uint8_t* scales, void* stream);
+
+/* Bytes of one column slice of an [n, k] matrix (see CbSliced); the whole
+ * sliced copy is (k / width) slices. */
+int64_t cb_nvfp4_slice_bytes(int32_t n, int32_t width);
+
+/* standard NVFP4 [n, k] -> (k / width) column slices (see CbSliced). */
+int cb_nvfp4_pack_slices(const uint8_t* codes, const uint8_t* scales, int32_t n, int32_t k, int32_t width,
+                         uint8_t* out, void* stream);
 
 /* standard NVFP4 [n, k] -> ceil(n/16) tiles (see CbMatrix); pad rows are zero. */
 int cb_nvfp4_pack_tiles(const uint8_t* codes, const uint8_t* scales, int32_t n, int32_t k, uint8_t* tiles,
@@ -261,6 +292,59 @@ typedef struct CbWorkspaceLayout {
   int32_t ld_proj, sel_ld;
 } CbWorkspaceLayout;
 int cb_workspace_layout(const CbModel* m, int32_t batch, int32_t T, int32_t max_ctx, CbWorkspaceLayout* out);
+
+/* ------------------------------------------------------------ MTP draft */
+/* The first multi-token-prediction module and the FR-Spec restricted draft
+ * head (cirrus/model/layers.py:351-370, cirrus/model/model.py:230-245). */
+typedef struct CbMtp {
+  const float* norm_h;      /* [d] */
+  const float* norm_e;      /* [d] */
+  const float* ffn_norm;    /* [d] */
+  CbMatrix proj;            /* [d rows][2d]: cat(norm_h(h), norm_e(e)) -> d */
+  CbMatrix gate_up;         /* [2*ffn_hidden rows][d] */
+  CbMatrix down;            /* [d rows][ffn_hidden] */
+  CbMatrix draft_head;      /* the embedding rows of draft_ids, [n_draft rows][d] */
+  const int32_t* draft_ids; /* device [n_draft] */
+  int32_t n_draft;
+} CbMtp;
+
+/* Scratch bytes cb_mtp_draft needs. */
+size_t cb_mtp_workspace_bytes(const CbModel* m, const CbMtp* mtp);
+
+/* CirrusModel.mtp_draft(h_last, token, n) (model.py:230-245): n passes of
+ * h = mtp(h, embed(tok)); tok = draft_ids[argmax(final_norm(h) . draft_head^T)],
+ * starting from the hidden state h_last (device float [d], the pre-final-norm
+ * hidden that predicted `token`) and token (device int32 [1]); the n drafted
+ * tokens go to out (device int32 [n]). */
+int cb_mtp_draft(const CbModel* m, const CbMtp* mtp, const float* h_last, const int32_t* token, int32_t n,
+                 int32_t* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------- speculative decoding */
+/* Prompt-lookup drafts for `batch` sequences, on the device.  Sequence b's
+ * tokens so far are tokens[b*ld .. b*ld + lens[b]) (prompt, then generated
+ * tokens; the last one is the pending token not yet in the cache).  The draft
+ * is the reference rule (cirrus/decoding/prompt_lookup.py:19-58): for n from
+ * max_ngram down to min_ngram, the tokens that followed the most recent earlier
+ * occurrence of the last n tokens, at most min(max_draft, T - 1, budget[b] - 1)
+ * of them (budget = tokens still to generate; <= 0 marks a finished sequence).
+ * Writes the verify input ids[b][0..T) = pending token, draft, then the pending
+ * token again as padding, and draft_len[b]. */
+int cb_prompt_lookup_draft(const int32_t* tokens, int32_t ld, const int32_t* lens, const int32_t* budget,
+                           int32_t batch, int32_t min_ngram, int32_t max_ngram, int32_t max_draft, int64_t* ids,
+                           int32_t T, int32_t* draft_len, void* stream);
+
+/* Greedy acceptance after a verify forward of T = 1 + draft tokens per
+ * sequence (cirrus/decoding/prompt_lookup.py:61-74 and the bookkeeping of
+ * cirrus/model/generate.py:66-88): n = the leading draft tokens equal to the
+ * model's argmax[b][t]; the n accepted tokens and the model's next token are
+ * appended to tokens/lens, budget[b] drops by n + 1, *emitted (device int64)
+ * grows by n + 1; the cache is rewound to the accepted prefix: pos[b] drops by
+ * T - 1 - n and, when n < T - 1, the GDN state and conv window are restored
+ * from the snapshot after token n (the cache must have snap_state/snap_conv).
+ * A finished sequence (budget <= 0) only gets its position rewound by T. */
+int cb_spec_accept(const CbModel* m, const CbCache* c, const int32_t* argmax, const int64_t* ids,
+                   const int32_t* draft_len, int32_t T, int32_t* tokens, int32_t ld, int32_t* lens,
+                   int32_t* budget, int64_t* emitted, void* stream);
 
 /* Copy the workspace's device status word into *status (synchronises on the stream). */
 int cb_read_status(const void* workspace, int32_t* status, void* stream);

@@ -224,19 +224,72 @@ def baseline_fixture() -> dict:
     return rec
 
 
+def _token_stream(n: int, vocab: int, seed: int) -> list:
+    """Uniform ids in which a quarter of the 8-token spans copy an earlier span."""
+    g = torch.Generator().manual_seed(seed)
+    toks = torch.randint(0, vocab, (n,), generator=g)
+    for s in range(1, n // 8):
+        if float(torch.rand((), generator=g)) < 0.25:
+            j = int(torch.randint(0, s * 8 - 7, (), generator=g))
+            toks[s * 8:s * 8 + 8] = toks[j:j + 8].clone()
+    return toks.tolist()
+
+
+def decoding_fixture() -> dict:
+    """The reference's prompt-lookup drafter, greedy acceptance and draft choice
+    (cirrus/decoding/prompt_lookup.py) on seeded token streams."""
+    from cirrus.decoding.prompt_lookup import PromptLookupDrafter, accept_greedy, choose_draft
+
+    drafts, streams = [], []
+    for seed, (n, vocab) in enumerate(((400, 50), (600, 7), (300, 1000), (200, 3))):
+        stream = _token_stream(n, vocab, seed)
+        streams.append(stream)
+        for cfg in ((2, 4, 4), (2, 4, 8), (1, 3, 5), (3, 3, 2)):
+            mn, mx, k = cfg
+            d = PromptLookupDrafter(max_ngram=mx, min_ngram=mn, max_draft=k)
+            d.extend(stream[:1])
+            for L in range(2, n + 1):
+                d.extend(stream[L - 1:L])
+                if L % 7 == 0 or L < 12:
+                    drafts.append({"stream": seed, "len": L, "min_ngram": mn, "max_ngram": mx, "k": k,
+                                   "draft": d.draft(k)})
+    g = torch.Generator().manual_seed(11)
+    accepts = []
+    for _ in range(200):
+        nd = int(torch.randint(0, 9, (), generator=g))
+        draft = torch.randint(0, 4, (nd,), generator=g).tolist()
+        target = torch.randint(0, 4, (nd + 1,), generator=g).tolist()
+        accepts.append({"draft": draft, "target": target, "out": accept_greedy(draft, target)})
+    chooses = []
+    for _ in range(100):
+        lk = torch.randint(0, 9, (int(torch.randint(0, 5, (), generator=g)),), generator=g).tolist()
+        mt = torch.randint(0, 9, (int(torch.randint(0, 3, (), generator=g)),), generator=g).tolist()
+        chooses.append({"lookup": lk, "mtp": mt, "out": choose_draft(lk, mt)})
+    return {"streams": streams, "drafts": drafts, "accepts": accepts, "chooses": chooses}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
+    ap.add_argument("--parts", default="debug,units,nvfp4,baseline,decoding",
+                    help="comma-separated fixtures to write")
     args = ap.parse_args()
     ref = os.path.abspath(args.reference)
     sys.path.insert(0, ref)
     import cirrus.model.layers as L
 
     L._fla_chunk_gdr = None  # the exact recurrence, as scripts/bench_spark.py:968 does
-    torch.save(debug_fixture(ref), os.path.join(HERE, "debug_ref.pt"))
-    torch.save(units_fixture(), os.path.join(HERE, "units_ref.pt"))
-    torch.save(nvfp4_fixture(ref), os.path.join(HERE, "nvfp4_ref.pt"))
-    torch.save(baseline_fixture(), os.path.join(HERE, "baseline_ref.pt"))
+    parts = set(args.parts.split(","))
+    if "debug" in parts:
+        torch.save(debug_fixture(ref), os.path.join(HERE, "debug_ref.pt"))
+    if "units" in parts:
+        torch.save(units_fixture(), os.path.join(HERE, "units_ref.pt"))
+    if "nvfp4" in parts:
+        torch.save(nvfp4_fixture(ref), os.path.join(HERE, "nvfp4_ref.pt"))
+    if "baseline" in parts:
+        torch.save(baseline_fixture(), os.path.join(HERE, "baseline_ref.pt"))
+    if "decoding" in parts:
+        torch.save(decoding_fixture(), os.path.join(HERE, "decoding_ref.pt"))
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".pt"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

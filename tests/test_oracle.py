@@ -213,3 +213,25 @@ def test_baseline_shapes_oracle_matches_reference():
     assert ov.logits[0].argmax(-1).tolist() == rec["verify_argmax"]
     torch.testing.assert_close(torch.stack((ov.logits[0, 0], ov.logits[0, -1])), rec["verify_logits_first_last"],
                                rtol=1e-4, atol=1e-4)
+
+
+# ---------------------------------------------------------------- decoding
+def test_decoding_oracle_matches_reference_drafter():
+    """oracle/decoding.py against the reference's PromptLookupDrafter,
+    accept_greedy and choose_draft (fixtures from cirrus/decoding/prompt_lookup.py)."""
+    from oracle import decoding as od
+
+    rec = golden("decoding_ref.pt")
+    assert len(rec["drafts"]) > 300
+    nonempty = 0
+    for c in rec["drafts"]:
+        toks = rec["streams"][c["stream"]][:c["len"]]
+        got = od.lookup_draft(toks, c["k"], c["min_ngram"], c["max_ngram"])
+        assert got == c["draft"], c
+        nonempty += bool(got)
+    assert nonempty > 100
+    for c in rec["accepts"]:
+        n, emit = c["out"]
+        assert od.accept_greedy(c["draft"], c["target"]) == (n, list(emit))
+    for c in rec["chooses"]:
+        assert od.choose_draft(c["lookup"], c["mtp"]) == list(c["out"])
