@@ -289,12 +289,17 @@ def spec_decode(eng, dev, stream, flush, args, rank: int) -> dict:
     from cirrus_s_1a_b200 import synthetic
     from cirrus_s_1a_b200.speculative import SpecDecoder
 
+    from cirrus_s_1a_b200.shard import shard_bounds
+
     cfg = eng.cfg
-    B, T = SPEC_BATCH, 1 + SPEC_DRAFT
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    # this rank's contiguous shard of the global batch of SPEC_BATCH * world sequences
+    s0, s1 = shard_bounds(SPEC_BATCH * world, world, rank)
+    B, T = s1 - s0, 1 + SPEC_DRAFT
     max_new = (args.warmup + SPEC_STEPS + 2) * T + 8
     cache = eng.new_cache(B, max_ctx=CTX + max_new + 2 * T)
     synthetic.fill_cache(cache, CTX, seed=3 + rank)
-    prompts = [synthetic.random_prompt(CTX - 1, cfg.vocab_size, seed=1000 * rank + b) for b in range(B)]
+    prompts = [synthetic.random_prompt(CTX - 1, cfg.vocab_size, seed=1000 + s) for s in range(s0, s1)]
     first = [p[-1] for p in prompts]  # any token: the synthetic cache has no real prompt to predict from
     dec = SpecDecoder(eng, cache, max_draft=SPEC_DRAFT)
     dec.start(prompts, max_new, first_tokens=first)
