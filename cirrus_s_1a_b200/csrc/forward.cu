@@ -18,6 +18,7 @@
 #include "attn.cuh"
 #include "common.cuh"
 #include "gdn.cuh"
+#include "gemm.cuh"
 #include "mk.cuh"
 #include "nvfp4.cuh"
 
@@ -154,9 +155,50 @@ static int gemv(const CbMatrix& W, const float* x, int ldx, int m_rows, const fl
   return launch_gemv(p, pre, epi, st);
 }
 
+// Token rows from which a projection runs on the tensor cores (cb_gemm_nvfp4)
+// instead of the CUDA-core GEMV.
+constexpr int kGemmMinRows = 17;
+
+static bool use_gemm(const CbMatrix& W, int m_rows) { return m_rows >= kGemmMinRows && W.k % 64 == 0; }
+
+static int gemm(const CbMatrix& W, const float* x, int ldx, int m_rows, const float* norm_w, float eps, int pre,
+                int epi, float* y, int ldy, int rows_out, int32_t* status, cudaStream_t st) {
+  GemmParams p{};
+  p.tiles = W.tiles;
+  p.tile_scale = W.tile_scale;
+  p.rows = W.rows;
+  p.K = W.k;
+  p.x = x;
+  p.ldx = ldx;
+  p.m_rows = m_rows;
+  p.pre = pre;
+  p.norm_w = norm_w;
+  p.eps = eps;
+  p.y = y;
+  p.ldy = ldy;
+  p.rows_out = rows_out;
+  p.epi = epi;
+  p.status = status;
+  return launch_gemm(p, st);
+}
+
+// One projection of m_rows token rows: the tensor-core GEMM for many rows, the GEMV otherwise.
+static int proj(const CbMatrix& W, const float* x, int ldx, int m_rows, const float* norm_w, float eps, int pre,
+                int epi, float* y, int ldy, int rows_out, int32_t* status, cudaStream_t st) {
+  if (use_gemm(W, m_rows))
+    return gemm(W, x, ldx, m_rows, norm_w, eps, pre == PRE_RMSNORM ? GEMM_PRE_RMSNORM : GEMM_PRE_NONE,
+                epi == EPI_ADD ? GEMM_EPI_ADD : GEMM_EPI_STORE, y, ldy, rows_out, status, st);
+  return gemv(W, x, ldx, m_rows, norm_w, eps, pre, epi, y, ldy, rows_out, st);
+}
+
 static int ffn(const CbMatrix& gate_up, const CbMatrix& down, const float* norm2, const CbModel& m, float* x, int rows,
                const Workspace& w, cudaStream_t st) {
-  const int d = m.d_model, F2 = 2 * m.ffn_hidden;
+  const int d = m.d_model, F = m.ffn_hidden, F2 = 2 * F;
+  if (use_gemm(gate_up, rows) && use_gemm(down, rows) && F % 64 == 0 && gate_up.rows == F2) {
+    // gate_up with the SwiGLU epilogue -> [rows][F]; down adds into the residual stream
+    CB_TRY(gemm(gate_up, x, d, rows, norm2, m.norm_eps, GEMM_PRE_RMSNORM, GEMM_EPI_SWIGLU, w.gu, F, F, w.status, st));
+    return gemm(down, w.gu, F, rows, nullptr, 0.f, GEMM_PRE_NONE, GEMM_EPI_ADD, x, d, d, w.status, st);
+  }
   CB_TRY(gemv(gate_up, x, d, rows, norm2, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.gu, F2, F2, st));
   return gemv(down, w.gu, F2, rows, nullptr, 0.f, PRE_SWIGLU, EPI_ADD, x, d, d, st);
 }
@@ -333,7 +375,7 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
     for (int i = 0; i < m.n_self_layers; ++i) {
       const CbSelfLayer& L = m.self_layers[i];
       const int ldp = L.in_proj.rows;
-      CB_TRY(gemv(L.in_proj, w.h, d, R, L.norm1, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.proj, ldp, ldp, st));
+      CB_TRY(proj(L.in_proj, w.h, d, R, L.norm1, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.proj, ldp, ldp, w.status, st));
       if (L.kind == CB_LAYER_GDN) {
         GdnParams g{};
         g.proj = w.proj;
@@ -418,15 +460,15 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
         sp.ldo = w.att_ld;
         CB_TRY(launch_swa(sp, B, st));
       }
-      CB_TRY(gemv(L.o_proj, w.attn, w.att_ld, R, nullptr, 0.f, PRE_NONE, EPI_ADD, w.h, d, d, st));
+      CB_TRY(proj(L.o_proj, w.attn, w.att_ld, R, nullptr, 0.f, PRE_NONE, EPI_ADD, w.h, d, d, w.status, st));
       CB_TRY(ffn(L.gate_up, L.down, L.norm2, m, w.h, R, w, st));
     }
 
     // ------------------------------------------------ shared KV (YOCO)
     // row stride w.ldp, as in the persistent kernel (cb_workspace_layout reports it)
     const int lds = w.ldp;
-    CB_TRY(gemv(m.shared_proj, w.h, d, R, m.shared_norm, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.proj, lds,
-                m.shared_proj.rows, st));
+    CB_TRY(proj(m.shared_proj, w.h, d, R, m.shared_norm, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.proj, lds,
+                m.shared_proj.rows, w.status, st));
     {
       HeadPrepParams hp{};
       hp.proj = w.proj;
@@ -492,7 +534,7 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
     for (int j = 0; j < m.n_cross_layers; ++j) {
       const CbCrossLayer& L = m.cross_layers[j];
       const int ldc = L.q_gate.rows;
-      CB_TRY(gemv(L.q_gate, w.xc, d, RQ, L.norm1, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.cproj, ldc, ldc, st));
+      CB_TRY(proj(L.q_gate, w.xc, d, RQ, L.norm1, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.cproj, ldc, ldc, w.status, st));
       CrossParams cpp{};
       cpp.proj = w.cproj;
       cpp.ldp = ldc;
@@ -519,7 +561,7 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
       cpp.out = w.attn;
       cpp.ldo = w.att_ld;
       CB_TRY(launch_cross(cpp, RQ, st));
-      CB_TRY(gemv(L.o_proj, w.attn, w.att_ld, RQ, nullptr, 0.f, PRE_NONE, EPI_ADD, w.xc, d, d, st));
+      CB_TRY(proj(L.o_proj, w.attn, w.att_ld, RQ, nullptr, 0.f, PRE_NONE, EPI_ADD, w.xc, d, d, w.status, st));
       CB_TRY(ffn(L.gate_up, L.down, L.norm2, m, w.xc, RQ, w, st));
     }
 
@@ -528,7 +570,7 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
     const int out_off = c0 + t_off - (T - nq);  // first logits row of this chunk, per sequence
     const bool direct = (tc == T) && logits != nullptr;
     float* lg = direct ? logits : w.logits;
-    CB_TRY(gemv(m.lm_head, w.xc, d, RQ, m.final_norm, m.norm_eps, PRE_RMSNORM, EPI_STORE, lg, V, V, st));
+    CB_TRY(proj(m.lm_head, w.xc, d, RQ, m.final_norm, m.norm_eps, PRE_RMSNORM, EPI_STORE, lg, V, V, w.status, st));
     if (logits && !direct) {
       scatter_rows_kernel<float><<<RQ, 256, 0, st>>>(lg, V, nqc, nq, out_off, logits);
       count_launch();

@@ -200,6 +200,30 @@ int cb_gemv_nvfp4(const CbMatrix* w, const float* x, int32_t ldx, int32_t m_rows
 int cb_verify_gemm_nvfp4(const CbMatrix* w, const uint16_t* x, int32_t ldx, int32_t m_rows, float* y, int32_t ldy,
                          int32_t rows_out, int32_t* status, void* stream);
 
+/* Many-token GEMM on the tensor cores (tcgen05.mma kind::f16 into tensor memory)
+ * for steps that carry many token rows (batched decode, batched verify, prompt
+ * chunks): y[m, r] (=, +=) pre(x)[m, :k] . dequant(W)[r, :] for m < m_rows (any
+ * count), r < rows_out.  x float32 [m_rows][ldx] (16-byte aligned rows, ldx % 4
+ * == 0), y float32 [m_rows][ldy].  W.k a multiple of 64.  The dequantised
+ * weights are exact in f16; each input is carried as an f16 head + tail pair
+ * (about 22 bits), accumulation fp32.
+ *   pre CB_GEMM_PRE_RMSNORM: x * rsqrt(mean(x^2) + eps) * norm_w (norm_w 16-byte aligned)
+ *   epi CB_GEMM_EPI_STORE / _ADD (y += ...) / _SWIGLU: W = [gate; up] with 2F rows,
+ *       F % 64 == 0, y[m, r] = silu(gate_r) * up_r for r < rows_out <= F.
+ * status (device int32, may be null) receives CB_ERR_TIMEOUT if a bounded wait
+ * on the tensor-core pipeline gives up.
+ * Replaces the nn.Linear products of CirrusModel.forward for T > 1 token rows
+ * (cirrus/model/model.py:99-176, layers.py:49-54 for the fused SwiGLU) that the
+ * reference runs as dense matmuls, and nvfp4_gemv with M > 1
+ * (cirrus/perf/bench_kernels.cu:202-227). */
+#define CB_GEMM_PRE_NONE 0
+#define CB_GEMM_PRE_RMSNORM 1
+#define CB_GEMM_EPI_STORE 0
+#define CB_GEMM_EPI_ADD 1
+#define CB_GEMM_EPI_SWIGLU 2
+int cb_gemm_nvfp4(const CbMatrix* w, const float* x, int32_t ldx, int32_t m_rows, int32_t pre, const float* norm_w,
+                  float eps, float* y, int32_t ldy, int32_t rows_out, int32_t epi, int32_t* status, void* stream);
+
 /* h[r, :] = dequant(lm_head row ids[r]) for r < n_rows (float32 [n_rows, d]). */
 int cb_embed(const CbMatrix* table, const int64_t* ids, int32_t n_rows, float* h, int32_t* status, void* stream);
 
