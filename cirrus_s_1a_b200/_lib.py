@@ -18,6 +18,7 @@ CB_MAX_CROSS = 16
 CB_MAX_T = 8
 CB_TILE_ROWS = 16
 CB_SWA_EXTRA = 16
+CB_PREFILL_CHUNK = 128
 CB_LAYER_GDN, CB_LAYER_SWA = 0, 1
 
 STATUS = {0: "ok", 1: "invalid argument", 2: "shape not supported", 3: "CUDA launch failed",
@@ -94,7 +95,7 @@ class CbCache(C.Structure):
 
 class CbWorkspaceLayout(C.Structure):
     _fields_ = [("bytes", C.c_uint64), ("proj", C.c_uint64), ("sel_idx", C.c_uint64), ("sel_cnt", C.c_uint64),
-                ("ld_proj", I32), ("sel_ld", I32)]
+                ("ld_proj", I32), ("sel_ld", I32), ("rows", I32)]
 
 
 class CbError(RuntimeError):

@@ -217,6 +217,163 @@ int launch_swa(const SwaParams& p, int batch, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
 }
 
+// ------------------------------------------------------------- SWA prefill
+// Block-wise sliding-window attention for a prompt chunk (the reference's
+// _sliding_window_attend, layers.py:195-210, over the ring instead of a padded
+// key tensor).  One CTA takes kSpQ consecutive tokens of one sequence and the
+// G query heads of one KV head (rows r = t * G + j) and walks the keys of their
+// windows 64 at a time with a running (max, sum) per row:
+//   S = q K^T * scale (masked to 0 <= pos - key < window), m' = max(m, max S),
+//   p = exp(S - m'), l = l e^{m - m'} + sum p, o = o e^{m - m'} + p V,
+// then writes o / l times the head gate sigmoid(gate) (layers.py:243).  The
+// chunk's own keys are already in the ring, which must hold window + T - 1
+// positions so that no key a query of the chunk needs is overwritten.
+constexpr int kSpThreads = 256;
+constexpr int kSpQ = 16;     // tokens per CTA
+constexpr int kSpKeys = 64;  // keys per tile
+constexpr int kSpMaxRows = kSpQ * 4;  // G <= 4 query heads per KV head
+
+// PER = output rows per thread (kSpMaxRows * hd / kSpThreads)
+template <int PER>
+__global__ void __launch_bounds__(kSpThreads) swa_prefill_kernel(SwaParams p) {
+  const int qb = blockIdx.x, g = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  const int hd = p.hd, G = p.Hq / p.Hkv;
+  const int t0 = qb * kSpQ, nq = min(kSpQ, p.T - t0), rows = nq * G;
+  extern __shared__ __align__(16) float sm[];
+  float* Qs = sm;                           // [rows][hd]
+  float* Ks = Qs + kSpMaxRows * hd;         // [kSpKeys][hd + 1]
+  float* Vs = Ks + kSpKeys * (hd + 1);      // [kSpKeys][hd]
+  float* Ps = Vs + kSpKeys * hd;            // [rows][kSpKeys + 1]
+  __shared__ float m_run[kSpMaxRows], l_run[kSpMaxRows], corr[kSpMaxRows];
+  const int P0 = p.pos[b] + p.c0 + t0;      // position of the block's first token
+  const int klo = max(0, P0 - p.window + 1), khi = P0 + nq - 1;
+  for (int i = tid; i < rows * hd; i += kSpThreads) {
+    const int r = i / hd, d = i - r * hd, t = r / G, j = r - t * G;
+    Qs[i] = p.q[((int64_t)b * p.T + t0 + t) * p.ldq + (g * G + j) * hd + d];
+  }
+  for (int r = tid; r < rows; r += kSpThreads) {
+    m_run[r] = -INFINITY;
+    l_run[r] = 0.0f;
+  }
+  // output accumulators: column d, rows rg, rg + groups, ...
+  const int groups = kSpThreads / hd, d = tid % hd, rg = tid / hd;
+  constexpr int kMaxPer = PER;
+  float o[kMaxPer];
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) o[i] = 0.0f;
+  const uint16_t* kr = p.kring + (int64_t)b * p.seq_stride;
+  const uint16_t* vr = p.vring + (int64_t)b * p.seq_stride;
+  const int warp = tid >> 5, lane = tid & 31, vpk = hd / 8;
+  for (int kt0 = klo; kt0 <= khi; kt0 += kSpKeys) {
+    const int n = min(kSpKeys, khi + 1 - kt0);
+    __syncthreads();  // the previous tile's K, V and P are consumed
+    for (int i = tid; i < n * vpk; i += kSpThreads) {
+      const int key = i / vpk, e8 = (i - key * vpk) * 8;
+      const int64_t off = ((int64_t)((kt0 + key) % p.slots) * p.Hkv + g) * hd + e8;
+      const uint4 kq = *reinterpret_cast<const uint4*>(kr + off);
+      const uint4 vq = *reinterpret_cast<const uint4*>(vr + off);
+      const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w}, vw[4] = {vq.x, vq.y, vq.z, vq.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        Ks[key * (hd + 1) + e8 + 2 * e] = bf16_to_f32(kw[e]);
+        Ks[key * (hd + 1) + e8 + 2 * e + 1] = bf16_to_f32(kw[e] >> 16);
+        Vs[key * hd + e8 + 2 * e] = bf16_to_f32(vw[e]);
+        Vs[key * hd + e8 + 2 * e + 1] = bf16_to_f32(vw[e] >> 16);
+      }
+    }
+    __syncthreads();
+    // scores: thread (key j, rows r0, r0 + 4, ...)
+    {
+      const int j = tid & (kSpKeys - 1), kp = kt0 + j;
+      for (int r = tid >> 6; r < rows; r += kSpThreads / kSpKeys) {
+        const int qp = P0 + r / G;
+        float sc = -INFINITY;
+        if (j < n && kp <= qp && kp > qp - p.window) {
+          const float* qq = Qs + r * hd;
+          const float* kk = Ks + j * (hd + 1);
+          float acc = 0.0f;
+          for (int e = 0; e < hd; ++e) acc = fmaf(qq[e], kk[e], acc);
+          sc = acc * p.scale;
+        }
+        Ps[r * (kSpKeys + 1) + j] = sc;
+      }
+    }
+    __syncthreads();
+    // running max / sum per row (a warp per row)
+    for (int r = warp; r < rows; r += kSpThreads / 32) {
+      float* pr = Ps + r * (kSpKeys + 1);
+      const float s0 = pr[lane], s1 = pr[lane + 32];
+      const float mt = warp_max(fmaxf(s0, s1));
+      const float mo = m_run[r], mn = fmaxf(mo, mt);
+      const float e0 = s0 == -INFINITY ? 0.0f : expf(s0 - mn), e1 = s1 == -INFINITY ? 0.0f : expf(s1 - mn);
+      const float ls = warp_sum(e0 + e1);
+      pr[lane] = e0;
+      pr[lane + 32] = e1;
+      if (lane == 0) {
+        const float c = mo == -INFINITY ? 0.0f : expf(mo - mn);
+        corr[r] = c;
+        l_run[r] = l_run[r] * c + ls;
+        m_run[r] = mn;
+      }
+    }
+    __syncthreads();
+    // o = o * corr + P V
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      const int r = rg + i * groups;
+      if (r < rows) {
+        const float* pr = Ps + r * (kSpKeys + 1);
+        float acc = o[i] * corr[r];
+        for (int jj = 0; jj < n; ++jj) acc = fmaf(pr[jj], Vs[jj * hd + d], acc);
+        o[i] = acc;
+      }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int r = rg + i * groups;
+    if (r < rows) {
+      const int t = r / G, j = r - t * G, qh = g * G + j;
+      const int64_t row = (int64_t)b * p.T + t0 + t;
+      const float gate = sigmoid(p.gate[row * p.ldg + qh]);
+      p.out[row * p.ldo + qh * hd + d] = (o[i] / l_run[r]) * gate;
+    }
+  }
+}
+
+bool swa_prefill_supported(int Hq, int Hkv, int hd) {
+  const int G = Hkv > 0 ? Hq / Hkv : 0;
+  return hd >= 8 && hd <= 128 && kSpThreads % hd == 0 && hd % 8 == 0 && (kSpMaxRows * hd) % kSpThreads == 0 &&
+         G >= 1 && G <= 4 && G * Hkv == Hq;
+}
+
+int launch_swa_prefill(const SwaParams& p, int batch, cudaStream_t st) {
+  if (!swa_prefill_supported(p.Hq, p.Hkv, p.hd)) return CB_ERR_SHAPE;
+  if (p.slots < p.window + p.T - 1) return CB_ERR_SHAPE;  // the chunk would overwrite keys it still needs
+  const size_t smem =
+      sizeof(float) * ((size_t)kSpMaxRows * p.hd + (size_t)kSpKeys * (2 * p.hd + 1) + (size_t)kSpMaxRows * (kSpKeys + 1));
+  const dim3 grid(ceil_div(p.T, kSpQ), p.Hkv, batch);
+  const int per = kSpMaxRows * p.hd / kSpThreads;
+#define CB_SP_CASE(N)                                                                              \
+  case N:                                                                                          \
+    if (ensure_smem_attr((const void*)swa_prefill_kernel<N>, (int)smem) != CB_OK) return CB_ERR_CUDA; \
+    swa_prefill_kernel<N><<<grid, kSpThreads, smem, st>>>(p);                                      \
+    break;
+  switch (per) {
+    CB_SP_CASE(2)
+    CB_SP_CASE(4)
+    CB_SP_CASE(8)
+    CB_SP_CASE(16)
+    CB_SP_CASE(32)
+    default:
+      return CB_ERR_SHAPE;
+  }
+#undef CB_SP_CASE
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
+
 // ---------------------------------------------------------- cross attention
 constexpr int kCrossThreads = 256;
 constexpr int kCrossChunk = 256;

@@ -99,6 +99,9 @@ struct IndexerParams {
 
 int launch_head_prep(const HeadPrepParams& p, int rows, cudaStream_t st);
 int launch_swa(const SwaParams& p, int batch, cudaStream_t st);
+// Prompt chunks: block-wise SWA (rows b * T + t), gated output straight into out.
+int launch_swa_prefill(const SwaParams& p, int batch, cudaStream_t st);
+bool swa_prefill_supported(int Hq, int Hkv, int hd);
 int launch_cross(const CrossParams& p, int rows, cudaStream_t st);
 int launch_indexer_topk(const IndexerParams& p, cudaStream_t st);
 

@@ -65,9 +65,30 @@ static int cross_splits(const CbModel& m) {
   return m.sparse_topk > 0 ? ceil_div(m.sparse_topk + 1, kMkCrossSplit) : 32;
 }
 
+// Whether prompt chunks longer than CB_MAX_T tokens can run on the prefill
+// kernels: the chunked GDN (Dk = Dv = 64), block-wise SWA, and the tensor-core
+// GEMM for every projection (K multiples of 64, F a multiple of 64).
+static bool prefill_ok(const CbModel& m) {
+  bool gdn = false, swa = false;
+  for (int i = 0; i < m.n_self_layers; ++i) (m.self_layers[i].kind == CB_LAYER_GDN ? gdn : swa) = true;
+  if (gdn && (m.gdn_dk != 64 || m.gdn_dv != 64 || m.conv_size != 4)) return false;
+  if (swa && !swa_prefill_supported(m.n_q_heads, m.n_kv_heads, m.head_dim)) return false;
+  return m.d_model % 64 == 0 && m.ffn_hidden % 64 == 0 && (m.n_q_heads * m.head_dim) % 64 == 0 &&
+         (m.gdn_heads * m.gdn_dv) % 64 == 0;
+}
+
+// Tokens per sequence of one chunk of a T-token forward: the whole forward up
+// to CB_MAX_T (decode, verify), CB_PREFILL_CHUNK for prompts on the prefill
+// kernels, CB_MAX_T otherwise.
+static int chunk_tokens(const CbModel& m, int T) {
+  T = std::max(T, 1);
+  if (T <= CB_MAX_T) return T;
+  return prefill_ok(m) ? std::min(T, CB_PREFILL_CHUNK) : CB_MAX_T;
+}
+
 static Workspace carve(const CbModel& m, int batch, int T, int max_ctx, char* base) {
   Workspace w{};
-  const int R = batch * std::min(std::max(T, 1), CB_MAX_T);
+  const int R = batch * chunk_tokens(m, T);
   int ldp = m.shared_proj.rows;
   for (int i = 0; i < m.n_self_layers; ++i) ldp = std::max(ldp, m.self_layers[i].in_proj.rows);
   w.ldp = ldp;
@@ -300,6 +321,7 @@ extern "C" int cb_workspace_layout(const CbModel* m, int32_t batch, int32_t T, i
   out->sel_cnt = off(z.sel_cnt);
   out->ld_proj = z.ldp;
   out->sel_ld = z.sel_ld;
+  out->rows = batch * chunk_tokens(*m, T);
   return CB_OK;
 }
 
@@ -354,7 +376,10 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
   cudaStream_t st = (cudaStream_t)stream;
   const int d = m.d_model;
   const int nq = (n_logits <= 0 || n_logits > T) ? T : n_logits;
-  const int Tc = std::min(T, CB_MAX_T);
+  int Tc = chunk_tokens(m, T);
+  // a prompt chunk appends all its keys to the SWA ring before its attention:
+  // the ring must hold window + Tc - 1 positions
+  if (Tc > CB_MAX_T) Tc = std::max(CB_MAX_T, std::min(Tc, c.swa_slots - m.swa_window + 1));
   const int H = m.gdn_heads, C = 2 * H * m.gdn_dk + H * m.gdn_dv;
   const int64_t gdn_S_layer = (int64_t)H * m.gdn_dk * m.gdn_dv;
   const int64_t gdn_conv_layer = (int64_t)(m.conv_size - 1) * C;
@@ -376,7 +401,35 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
       const CbSelfLayer& L = m.self_layers[i];
       const int ldp = L.in_proj.rows;
       CB_TRY(proj(L.in_proj, w.h, d, R, L.norm1, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.proj, ldp, ldp, w.status, st));
-      if (L.kind == CB_LAYER_GDN) {
+      if (L.kind == CB_LAYER_GDN && tc > CB_MAX_T) {
+        // prompt chunk: the conv over the chunk into w.gu (free until the FFN), then
+        // the chunked recurrence with the gating and the gated RMSNorm fused
+        CB_TRY(launch_gdn_conv(w.proj, ldp, L.conv_w, c.gdn_conv + (int64_t)L.slot * gdn_conv_layer,
+                               (int64_t)c.n_gdn * gdn_conv_layer, B, tc, C, m.conv_size, w.gu, C, st));
+        GdnChunkParams g{};
+        g.q = w.gu;
+        g.k = w.gu + H * m.gdn_dk;
+        g.v = w.gu + 2 * H * m.gdn_dk;
+        g.ld_qkv = C;
+        g.a_raw = w.proj + m.gdn_off_a;
+        g.b_raw = w.proj + m.gdn_off_b;
+        g.ld_ab = ldp;
+        g.A_log = L.A_log;
+        g.dt_bias = L.dt_bias;
+        g.state = c.gdn_state + (int64_t)L.slot * gdn_S_layer;
+        g.state_seq = (int64_t)c.n_gdn * gdn_S_layer;
+        g.out = w.attn;
+        g.ld_out = w.att_ld;
+        g.gate = w.proj + m.gdn_off_gate;
+        g.ld_gate = ldp;
+        g.o_norm = L.o_norm;
+        g.eps = m.norm_eps;
+        g.B = B;
+        g.T = tc;
+        g.H = H;
+        g.scale = 1.0f / sqrtf((float)m.gdn_dk);
+        CB_TRY(launch_gdn_chunk(g, st));
+      } else if (L.kind == CB_LAYER_GDN) {
         GdnParams g{};
         g.proj = w.proj;
         g.ldp = ldp;
@@ -458,7 +511,8 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
         sp.ldg = ldp;
         sp.out = w.attn;
         sp.ldo = w.att_ld;
-        CB_TRY(launch_swa(sp, B, st));
+        if (tc > CB_MAX_T) CB_TRY(launch_swa_prefill(sp, B, st));
+        else CB_TRY(launch_swa(sp, B, st));
       }
       CB_TRY(proj(L.o_proj, w.attn, w.att_ld, R, nullptr, 0.f, PRE_NONE, EPI_ADD, w.h, d, d, w.status, st));
       CB_TRY(ffn(L.gate_up, L.down, L.norm2, m, w.h, R, w, st));

@@ -20,6 +20,7 @@
 // triangular solve goes in 16-row blocks: a parallel update from the finished
 // blocks, then one thread per right-hand-side column inside the block.
 #include "common.cuh"
+#include "gdn.cuh"
 
 namespace cb {
 namespace {
@@ -28,14 +29,6 @@ constexpr int kGc = 64;        // chunk length
 constexpr int kGd = 64;        // Dk = Dv
 constexpr int kGp = kGd + 1;   // padded row stride (floats)
 constexpr int kGThreads = 256;
-
-struct GdnChunkParams {
-  const float *q, *k, *v, *g, *beta;  // [B][T][H][D], g and beta [B][T][H]
-  float* state;                       // [B][H][Dk][Dv], in/out
-  float* out;                         // [B][T][H][Dv]
-  int B, T, H;
-  float scale;
-};
 
 // acc[r][c] += sum_{k < n} X[(r0 + r) * xr + k * xk] * Y[k * yk + (c0 + c) * yc]
 __device__ __forceinline__ void mm44(const float* X, int xr, int xk, const float* Y, int yk, int yc, int n, int r0,
@@ -67,7 +60,8 @@ __global__ void __launch_bounds__(kGThreads, 1) gdn_chunk_kernel(const __grid_co
   __shared__ float Gs[kGc], bs[kGc];
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15, r0 = 4 * ty, c0 = 4 * tx;
   const int b = blockIdx.x / p.H, h = blockIdx.x - b * p.H, H = p.H;
-  float* Sg = p.state + ((int64_t)b * H + h) * kGd * kGd;
+  const bool model = p.a_raw != nullptr;
+  float* Sg = p.state + (int64_t)b * p.state_seq + (int64_t)h * kGd * kGd;
   for (int i = tid; i < kGd * kGd; i += kGThreads) S[(i / kGd) * kGp + (i % kGd)] = Sg[i];
 
   for (int t0 = 0; t0 < p.T; t0 += kGc) {
@@ -77,21 +71,52 @@ __global__ void __launch_bounds__(kGThreads, 1) gdn_chunk_kernel(const __grid_co
       const int t = i / kGd, d = i - t * kGd;
       float kv = 0.0f, qv = 0.0f, vv = 0.0f;
       if (t < tc) {
-        const int64_t off = (((int64_t)b * p.T + t0 + t) * H + h) * kGd + d;
+        const int64_t off = ((int64_t)b * p.T + t0 + t) * p.ld_qkv + (int64_t)h * kGd + d;
         kv = p.k[off];
-        qv = p.q[off] * p.scale;
+        qv = p.q[off];
         vv = p.v[off];
       }
       Kc[t * kGp + d] = kv;
       Qc[t * kGp + d] = qv;
       Vc[t * kGp + d] = vv;
     }
+    if (model) {
+      // L2-normalise the chunk's q and k rows (x / max(||x||, 1e-12)); a warp per row
+      __syncthreads();
+      const int warp = tid >> 5, lane = tid & 31;
+      for (int j = warp; j < 2 * kGc; j += kGThreads / 32) {
+        float* x = (j < kGc ? Qc : Kc) + (j & (kGc - 1)) * kGp;
+        const float a0 = x[lane], a1 = x[lane + 32];
+        const float ss = warp_sum(a0 * a0 + a1 * a1);
+        const float inv = 1.0f / fmaxf(sqrtf(ss), 1e-12f);
+        x[lane] = a0 * inv;
+        x[lane + 32] = a1 * inv;
+      }
+      __syncthreads();
+    }
+    for (int i = tid; i < kGc * kGd; i += kGThreads) Qc[(i / kGd) * kGp + (i % kGd)] *= p.scale;
     if (tid < 32) {  // G = inclusive prefix sum of g (padded tokens: g = 0, beta = 0)
-      const int64_t o0 = ((int64_t)b * p.T + t0) * H + h;
-      float g0 = tid < tc ? p.g[o0 + (int64_t)tid * H] : 0.0f;
-      float g1 = tid + 32 < tc ? p.g[o0 + (int64_t)(tid + 32) * H] : 0.0f;
-      bs[tid] = tid < tc ? p.beta[o0 + (int64_t)tid * H] : 0.0f;
-      bs[tid + 32] = tid + 32 < tc ? p.beta[o0 + (int64_t)(tid + 32) * H] : 0.0f;
+      float g0 = 0.0f, g1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
+      if (model) {
+        const float A = -expf(p.A_log[h]), dtb = p.dt_bias[h];
+        const int64_t r0 = (int64_t)b * p.T + t0;
+        if (tid < tc) {
+          g0 = A * softplus(p.a_raw[(r0 + tid) * p.ld_ab + h] + dtb);
+          b0 = sigmoid(p.b_raw[(r0 + tid) * p.ld_ab + h]);
+        }
+        if (tid + 32 < tc) {
+          g1 = A * softplus(p.a_raw[(r0 + tid + 32) * p.ld_ab + h] + dtb);
+          b1 = sigmoid(p.b_raw[(r0 + tid + 32) * p.ld_ab + h]);
+        }
+      } else {
+        const int64_t o0 = ((int64_t)b * p.T + t0) * H + h;
+        g0 = tid < tc ? p.g[o0 + (int64_t)tid * H] : 0.0f;
+        g1 = tid + 32 < tc ? p.g[o0 + (int64_t)(tid + 32) * H] : 0.0f;
+        b0 = tid < tc ? p.beta[o0 + (int64_t)tid * H] : 0.0f;
+        b1 = tid + 32 < tc ? p.beta[o0 + (int64_t)(tid + 32) * H] : 0.0f;
+      }
+      bs[tid] = b0;
+      bs[tid + 32] = b1;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const float a0 = __shfl_up_sync(0xffffffffu, g0, o), a1 = __shfl_up_sync(0xffffffffu, g1, o);
@@ -162,13 +187,33 @@ __global__ void __launch_bounds__(kGThreads, 1) gdn_chunk_kernel(const __grid_co
     }
     __syncthreads();
     mm44(P, kGp, 1, U, kGp, 1, kGc, r0, c0, o);
+    if (p.gate == nullptr) {
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int t = r0 + r;
-      if (t < tc) {
-        float* op = p.out + (((int64_t)b * p.T + t0 + t) * H + h) * kGd + c0;
+      for (int r = 0; r < 4; ++r) {
+        const int t = r0 + r;
+        if (t < tc) {
+          float* op = p.out + ((int64_t)b * p.T + t0 + t) * p.ld_out + (int64_t)h * kGd + c0;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) op[c] = o[r][c];
+          for (int c = 0; c < 4; ++c) op[c] = o[r][c];
+        }
+      }
+    } else {
+      // gated RMSNorm of each output row: o rows through shared memory (A is free now)
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) A[(r0 + r) * kGp + c0 + c] = o[r][c];
+      __syncthreads();
+      const int warp = tid >> 5, lane = tid & 31;
+      for (int t = warp; t < tc; t += kGThreads / 32) {
+        const float* x = A + t * kGp;
+        const float a0 = x[lane], a1 = x[lane + 32];
+        const float rr = rsqrtf(warp_sum(a0 * a0 + a1 * a1) / (float)kGd + p.eps);
+        const int64_t row = (int64_t)b * p.T + t0 + t;
+        const float* gt = p.gate + row * p.ld_gate + (int64_t)h * kGd;
+        float* op = p.out + row * p.ld_out + (int64_t)h * kGd;
+        op[lane] = a0 * rr * p.o_norm[lane] * silu(gt[lane]);
+        op[lane + 32] = a1 * rr * p.o_norm[lane + 32] * silu(gt[lane + 32]);
       }
     }
     // S = e^{G_C} S0 + K^T diag(e^{G_C - G}) D
@@ -201,6 +246,14 @@ __global__ void __launch_bounds__(kGThreads, 1) gdn_chunk_kernel(const __grid_co
 
 size_t gdn_chunk_smem() { return sizeof(float) * (size_t)(kGd * kGp + 7 * kGc * kGp); }
 
+int launch_gdn_chunk(const GdnChunkParams& p, cudaStream_t st) {
+  if (p.B < 1 || p.T < 1 || p.H < 1) return CB_ERR_ARG;
+  if (ensure_smem_attr((const void*)gdn_chunk_kernel, (int)gdn_chunk_smem()) != CB_OK) return CB_ERR_CUDA;
+  gdn_chunk_kernel<<<p.B * p.H, kGThreads, gdn_chunk_smem(), st>>>(p);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
+
 }  // namespace cb
 
 using namespace cb;
@@ -210,9 +263,20 @@ extern "C" int cb_gdn_chunk_prefill(const float* q, const float* k, const float*
                                     float* state, float* out, void* stream) {
   if (!q || !k || !v || !g || !beta || !state || !out || B < 1 || T < 1 || H < 1) return CB_ERR_ARG;
   if (Dk != kGd || Dv != kGd) return CB_ERR_SHAPE;
-  if (ensure_smem_attr((const void*)gdn_chunk_kernel, (int)gdn_chunk_smem()) != CB_OK) return CB_ERR_CUDA;
-  GdnChunkParams p{q, k, v, g, beta, state, out, B, T, H, scale};
-  gdn_chunk_kernel<<<B * H, kGThreads, gdn_chunk_smem(), (cudaStream_t)stream>>>(p);
-  count_launch();
-  return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+  GdnChunkParams p{};
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.ld_qkv = (int64_t)H * kGd;
+  p.g = g;
+  p.beta = beta;
+  p.state = state;
+  p.state_seq = (int64_t)H * kGd * kGd;
+  p.out = out;
+  p.ld_out = (int64_t)H * kGd;
+  p.B = B;
+  p.T = T;
+  p.H = H;
+  p.scale = scale;
+  return launch_gdn_chunk(p, (cudaStream_t)stream);
 }

@@ -23,7 +23,8 @@ from dataclasses import dataclass, field
 import torch
 
 from cirrus_s_1a_b200 import _lib
-from cirrus_s_1a_b200._lib import (CB_LAYER_GDN, CB_LAYER_SWA, CB_MAX_T, CB_SWA_EXTRA, CbCache, CbMatrix, CbModel,
+from cirrus_s_1a_b200._lib import (CB_LAYER_GDN, CB_LAYER_SWA, CB_MAX_T, CB_PREFILL_CHUNK, CB_SWA_EXTRA, CbCache,
+                                   CbMatrix, CbModel,
                                    CbMtp, CbSliced)
 
 
@@ -256,7 +257,8 @@ class DeviceCache:
     def __init__(self, model: DeviceModel, batch: int, max_ctx: int, _share: "DeviceCache | None" = None):
         cfg, dev = model.cfg, model.device
         self.model, self.batch, self.max_ctx = model, batch, max_ctx
-        self.swa_slots = cfg.swa_window + CB_SWA_EXTRA
+        # window + CB_PREFILL_CHUNK slots: a prompt chunk appends all its keys before its attention
+        self.swa_slots = cfg.swa_window + max(CB_SWA_EXTRA, CB_PREFILL_CHUNK)
         H, dk, dv, KC = cfg.gdn_heads, cfg.gdn_head_dim_k, cfg.gdn_head_dim_v, cfg.gdn_conv_size
         C_ = 2 * H * dk + H * dv
         if _share is None:
@@ -382,7 +384,7 @@ class CirrusB200:
         return DeviceCache(self.model, batch, max_ctx or self.max_ctx)
 
     def workspace(self, batch: int, T: int, max_ctx: int) -> torch.Tensor:
-        Tc = min(T, CB_MAX_T)
+        Tc = min(T, CB_PREFILL_CHUNK)  # cb_forward runs longer inputs in chunks of at most this many tokens
         key = (batch, Tc, max_ctx)
         ws = self._ws.get(key)
         if ws is None:
@@ -412,8 +414,7 @@ class CirrusB200:
         lay = _lib.CbWorkspaceLayout()
         _lib.check(_lib.lib().cb_workspace_layout(C.byref(self.model.desc), cache.batch, T, cache.max_ctx,
                                                   C.byref(lay)), "cb_workspace_layout")
-        Tc = min(T, CB_MAX_T)
-        rows = cache.batch * Tc
+        rows = lay.rows
 
         def view(off, n, dtype):
             return ws[off:off + 4 * n].view(dtype)

@@ -38,7 +38,8 @@ extern "C" {
 #define CB_MAX_CROSS 16  /* cross-decoder layers */
 #define CB_MAX_T 8       /* tokens per sequence per launch chunk (1 + draft) */
 #define CB_TILE_ROWS 16  /* rows per NVFP4 weight tile */
-#define CB_SWA_EXTRA 16  /* SWA ring slots beyond the window */
+#define CB_SWA_EXTRA 16  /* SWA ring slots beyond the window (minimum) */
+#define CB_PREFILL_CHUNK 128  /* tokens per sequence of one prompt chunk on the prefill kernels */
 
 enum {
   CB_OK = 0,
@@ -139,7 +140,9 @@ typedef struct CbModel {
 
 /* Decode state of `batch` independent sequences (the reference Cache,
  * model.py:41-51).  pos[b] = tokens already in the cache.  SWA keys live in a
- * ring of swa_slots = swa_window + CB_SWA_EXTRA rows, slot = position % swa_slots;
+ * ring of swa_slots >= swa_window + CB_SWA_EXTRA rows, slot = position % swa_slots
+ * (prompt chunks of up to swa_slots - swa_window + 1 tokens run on the prefill
+ * kernels, so swa_window + CB_PREFILL_CHUNK slots give full-size chunks);
  * the shared KV rows are indexed by position.  Rows at positions >= pos[b]
  * are scratch: a forward that is later discarded may write them.
  * snap_state / snap_conv (may be null): when set, a forward of T > 1 tokens
@@ -288,7 +291,11 @@ int cb_indexer_topk_noalloc(const float* iq, const float* iw, int32_t ld_q, cons
 
 /* ------------------------------------------------------- whole forward */
 /* Workspace bytes cb_forward needs for `batch` sequences and up to T tokens
- * per sequence (T is clamped to CB_MAX_T: longer inputs run in chunks). */
+ * per sequence.  Longer inputs run in chunks: up to CB_MAX_T tokens on the
+ * decode kernels; prompts (T > CB_MAX_T) in chunks of up to CB_PREFILL_CHUNK
+ * tokens on the prefill kernels (tensor-core GEMMs, chunked Gated DeltaNet,
+ * block-wise SWA) when the model's shapes allow them (GDN Dk = Dv = 64, every
+ * projection K a multiple of 64), else in chunks of CB_MAX_T. */
 size_t cb_workspace_bytes(const CbModel* m, int32_t batch, int32_t T, int32_t max_ctx);
 
 /* CirrusModel.forward(input_ids[batch, T], cache, n_logits) for a batch of
@@ -304,7 +311,7 @@ int cb_forward(const CbModel* m, const CbCache* c, void* workspace, size_t works
 /* Where cb_forward keeps its intermediate results inside a workspace sized for
  * (batch, T, max_ctx), as byte offsets from the workspace start, for reading
  * them back after a forward (tests, debugging):
- *   proj     float32 [batch*Tc][ld_proj], Tc = min(T, CB_MAX_T): the shared
+ *   proj     float32 [rows][ld_proj], rows = batch * Tc (Tc the chunk length): the shared
  *            projection of the last chunk's rows (k | v | idx_k | idx_q | idx_w at
  *            the CbModel offsets; row b*Tc + t);
  *   sel_idx  int32 [batch*nq][sel_ld]: the keys each query row of the last chunk
@@ -314,6 +321,7 @@ int cb_forward(const CbModel* m, const CbCache* c, void* workspace, size_t works
 typedef struct CbWorkspaceLayout {
   uint64_t bytes, proj, sel_idx, sel_cnt;
   int32_t ld_proj, sel_ld;
+  int32_t rows;  /* batch * Tc: rows of proj */
 } CbWorkspaceLayout;
 int cb_workspace_layout(const CbModel* m, int32_t batch, int32_t T, int32_t max_ctx, CbWorkspaceLayout* out);
 
