@@ -54,11 +54,17 @@ struct Workspace {
   unsigned long long* amax64;
   unsigned* sync;     // [0] barrier counter, [32] abort flag
   unsigned long long* trace;
+  uint8_t* gemm_x;     // prepared GEMM inputs (cb_gemm scratch)
+  size_t gemm_x_bytes;
   size_t bytes;
   int ldp, att_ld, cr_ld, n_splits, sel_ld, cross_splits;
 };
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Token rows from which a projection runs on the tensor cores (cb_gemm_nvfp4)
+// instead of the CUDA-core GEMV.
+constexpr int kGemmMinRows = 17;
 
 static int swa_splits(const CbModel& m) { return ceil_div(m.swa_window + CB_MAX_T, kSwaSplit); }
 static int cross_splits(const CbModel& m) {
@@ -129,6 +135,10 @@ static Workspace carve(const CbModel& m, int batch, int T, int max_ctx, char* ba
   w.amax64 = (unsigned long long*)take(sizeof(unsigned long long) * R);
   w.sync = (unsigned*)take(256);
   w.trace = (unsigned long long*)take(sizeof(unsigned long long) * kMkTrace);
+  // the tensor-core GEMM's prepared inputs: the widest projection input of R rows
+  const int kmax = std::max(std::max(m.d_model, m.ffn_hidden), w.att_ld);
+  w.gemm_x_bytes = R >= kGemmMinRows ? gemm_scratch_bytes((kmax + 63) / 64 * 64, R) : 0;
+  w.gemm_x = (uint8_t*)take(w.gemm_x_bytes);
   w.bytes = off;
   return w;
 }
@@ -176,15 +186,15 @@ static int gemv(const CbMatrix& W, const float* x, int ldx, int m_rows, const fl
   return launch_gemv(p, pre, epi, st);
 }
 
-// Token rows from which a projection runs on the tensor cores (cb_gemm_nvfp4)
-// instead of the CUDA-core GEMV.
-constexpr int kGemmMinRows = 17;
 
 static bool use_gemm(const CbMatrix& W, int m_rows) { return m_rows >= kGemmMinRows && W.k % 64 == 0; }
 
-static int gemm(const CbMatrix& W, const float* x, int ldx, int m_rows, const float* norm_w, float eps, int pre,
-                int epi, float* y, int ldy, int rows_out, int32_t* status, cudaStream_t st) {
+static int gemm(const Workspace& w, const CbMatrix& W, const float* x, int ldx, int m_rows, const float* norm_w,
+                float eps, int pre, int epi, float* y, int ldy, int rows_out, cudaStream_t st) {
+  int32_t* status = w.status;
   GemmParams p{};
+  p.xb = w.gemm_x;
+  p.xb_bytes = w.gemm_x_bytes;
   p.tiles = W.tiles;
   p.tile_scale = W.tile_scale;
   p.rows = W.rows;
@@ -204,11 +214,11 @@ static int gemm(const CbMatrix& W, const float* x, int ldx, int m_rows, const fl
 }
 
 // One projection of m_rows token rows: the tensor-core GEMM for many rows, the GEMV otherwise.
-static int proj(const CbMatrix& W, const float* x, int ldx, int m_rows, const float* norm_w, float eps, int pre,
-                int epi, float* y, int ldy, int rows_out, int32_t* status, cudaStream_t st) {
+static int proj(const Workspace& w, const CbMatrix& W, const float* x, int ldx, int m_rows, const float* norm_w,
+                float eps, int pre, int epi, float* y, int ldy, int rows_out, cudaStream_t st) {
   if (use_gemm(W, m_rows))
-    return gemm(W, x, ldx, m_rows, norm_w, eps, pre == PRE_RMSNORM ? GEMM_PRE_RMSNORM : GEMM_PRE_NONE,
-                epi == EPI_ADD ? GEMM_EPI_ADD : GEMM_EPI_STORE, y, ldy, rows_out, status, st);
+    return gemm(w, W, x, ldx, m_rows, norm_w, eps, pre == PRE_RMSNORM ? GEMM_PRE_RMSNORM : GEMM_PRE_NONE,
+                epi == EPI_ADD ? GEMM_EPI_ADD : GEMM_EPI_STORE, y, ldy, rows_out, st);
   return gemv(W, x, ldx, m_rows, norm_w, eps, pre, epi, y, ldy, rows_out, st);
 }
 
@@ -217,8 +227,8 @@ static int ffn(const CbMatrix& gate_up, const CbMatrix& down, const float* norm2
   const int d = m.d_model, F = m.ffn_hidden, F2 = 2 * F;
   if (use_gemm(gate_up, rows) && use_gemm(down, rows) && F % 64 == 0 && gate_up.rows == F2) {
     // gate_up with the SwiGLU epilogue -> [rows][F]; down adds into the residual stream
-    CB_TRY(gemm(gate_up, x, d, rows, norm2, m.norm_eps, GEMM_PRE_RMSNORM, GEMM_EPI_SWIGLU, w.gu, F, F, w.status, st));
-    return gemm(down, w.gu, F, rows, nullptr, 0.f, GEMM_PRE_NONE, GEMM_EPI_ADD, x, d, d, w.status, st);
+    CB_TRY(gemm(w, gate_up, x, d, rows, norm2, m.norm_eps, GEMM_PRE_RMSNORM, GEMM_EPI_SWIGLU, w.gu, F, F, st));
+    return gemm(w, down, w.gu, F, rows, nullptr, 0.f, GEMM_PRE_NONE, GEMM_EPI_ADD, x, d, d, st);
   }
   CB_TRY(gemv(gate_up, x, d, rows, norm2, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.gu, F2, F2, st));
   return gemv(down, w.gu, F2, rows, nullptr, 0.f, PRE_SWIGLU, EPI_ADD, x, d, d, st);
@@ -400,7 +410,7 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
     for (int i = 0; i < m.n_self_layers; ++i) {
       const CbSelfLayer& L = m.self_layers[i];
       const int ldp = L.in_proj.rows;
-      CB_TRY(proj(L.in_proj, w.h, d, R, L.norm1, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.proj, ldp, ldp, w.status, st));
+      CB_TRY(proj(w, L.in_proj, w.h, d, R, L.norm1, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.proj, ldp, ldp, st));
       if (L.kind == CB_LAYER_GDN && tc > CB_MAX_T) {
         // prompt chunk: the conv over the chunk into w.gu (free until the FFN), then
         // the chunked recurrence with the gating and the gated RMSNorm fused
@@ -514,15 +524,15 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
         if (tc > CB_MAX_T) CB_TRY(launch_swa_prefill(sp, B, st));
         else CB_TRY(launch_swa(sp, B, st));
       }
-      CB_TRY(proj(L.o_proj, w.attn, w.att_ld, R, nullptr, 0.f, PRE_NONE, EPI_ADD, w.h, d, d, w.status, st));
+      CB_TRY(proj(w, L.o_proj, w.attn, w.att_ld, R, nullptr, 0.f, PRE_NONE, EPI_ADD, w.h, d, d, st));
       CB_TRY(ffn(L.gate_up, L.down, L.norm2, m, w.h, R, w, st));
     }
 
     // ------------------------------------------------ shared KV (YOCO)
     // row stride w.ldp, as in the persistent kernel (cb_workspace_layout reports it)
     const int lds = w.ldp;
-    CB_TRY(proj(m.shared_proj, w.h, d, R, m.shared_norm, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.proj, lds,
-                m.shared_proj.rows, w.status, st));
+    CB_TRY(proj(w, m.shared_proj, w.h, d, R, m.shared_norm, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.proj, lds,
+                m.shared_proj.rows, st));
     {
       HeadPrepParams hp{};
       hp.proj = w.proj;
@@ -588,7 +598,7 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
     for (int j = 0; j < m.n_cross_layers; ++j) {
       const CbCrossLayer& L = m.cross_layers[j];
       const int ldc = L.q_gate.rows;
-      CB_TRY(proj(L.q_gate, w.xc, d, RQ, L.norm1, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.cproj, ldc, ldc, w.status, st));
+      CB_TRY(proj(w, L.q_gate, w.xc, d, RQ, L.norm1, m.norm_eps, PRE_RMSNORM, EPI_STORE, w.cproj, ldc, ldc, st));
       CrossParams cpp{};
       cpp.proj = w.cproj;
       cpp.ldp = ldc;
@@ -615,7 +625,7 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
       cpp.out = w.attn;
       cpp.ldo = w.att_ld;
       CB_TRY(launch_cross(cpp, RQ, st));
-      CB_TRY(proj(L.o_proj, w.attn, w.att_ld, RQ, nullptr, 0.f, PRE_NONE, EPI_ADD, w.xc, d, d, w.status, st));
+      CB_TRY(proj(w, L.o_proj, w.attn, w.att_ld, RQ, nullptr, 0.f, PRE_NONE, EPI_ADD, w.xc, d, d, st));
       CB_TRY(ffn(L.gate_up, L.down, L.norm2, m, w.xc, RQ, w, st));
     }
 
@@ -624,7 +634,7 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
     const int out_off = c0 + t_off - (T - nq);  // first logits row of this chunk, per sequence
     const bool direct = (tc == T) && logits != nullptr;
     float* lg = direct ? logits : w.logits;
-    CB_TRY(proj(m.lm_head, w.xc, d, RQ, m.final_norm, m.norm_eps, PRE_RMSNORM, EPI_STORE, lg, V, V, w.status, st));
+    CB_TRY(proj(w, m.lm_head, w.xc, d, RQ, m.final_norm, m.norm_eps, PRE_RMSNORM, EPI_STORE, lg, V, V, st));
     if (logits && !direct) {
       scatter_rows_kernel<float><<<RQ, 256, 0, st>>>(lg, V, nqc, nq, out_off, logits);
       count_launch();

@@ -18,7 +18,7 @@ struct GemmParams {
   const uint8_t* tiles;
   const float* tile_scale;
   int rows;        // rows of W (multiple of 16)
-  int K;           // multiple of 64
+  int K;           // multiple of 64 (RMSNorm inputs: any such K)
   const float* x;  // [m_rows][ldx] float32, 16-byte aligned rows
   int ldx, m_rows;
   int pre;
@@ -26,10 +26,13 @@ struct GemmParams {
   float eps;
   float* y;
   int ldy, rows_out, epi;
+  uint8_t* xb;      // scratch for the prepared inputs (gemm_scratch_bytes)
+  size_t xb_bytes;
   int32_t* status;  // CB_ERR_TIMEOUT when a bounded wait gives up (may be null)
 };
 
+// Bytes of prepared-input scratch for m_rows token rows of K inputs.
+size_t gemm_scratch_bytes(int K, int m_rows);
 int launch_gemm(const GemmParams& p, cudaStream_t st);
-int gemm_tokens_per_cta();
 
 }  // namespace cb

@@ -213,8 +213,11 @@ int cb_verify_gemm_nvfp4(const CbMatrix* w, const uint16_t* x, int32_t ldx, int3
  *   pre CB_GEMM_PRE_RMSNORM: x * rsqrt(mean(x^2) + eps) * norm_w (norm_w 16-byte aligned)
  *   epi CB_GEMM_EPI_STORE / _ADD (y += ...) / _SWIGLU: W = [gate; up] with 2F rows,
  *       F % 64 == 0, y[m, r] = silu(gate_r) * up_r for r < rows_out <= F.
- * status (device int32, may be null) receives CB_ERR_TIMEOUT if a bounded wait
- * on the tensor-core pipeline gives up.
+ * scratch: device memory of at least cb_gemm_scratch_bytes(W.k, m_rows) bytes
+ * (16-byte aligned) for the inputs prepared as f16 operand blocks; two launches
+ * (input preparation, GEMM), both as programmatic dependents of the kernel
+ * before them.  status (device int32, may be null) receives CB_ERR_TIMEOUT if a
+ * bounded wait on the tensor-core pipeline gives up.
  * Replaces the nn.Linear products of CirrusModel.forward for T > 1 token rows
  * (cirrus/model/model.py:99-176, layers.py:49-54 for the fused SwiGLU) that the
  * reference runs as dense matmuls, and nvfp4_gemv with M > 1
@@ -224,8 +227,10 @@ int cb_verify_gemm_nvfp4(const CbMatrix* w, const uint16_t* x, int32_t ldx, int3
 #define CB_GEMM_EPI_STORE 0
 #define CB_GEMM_EPI_ADD 1
 #define CB_GEMM_EPI_SWIGLU 2
+size_t cb_gemm_scratch_bytes(int32_t k, int32_t m_rows);
 int cb_gemm_nvfp4(const CbMatrix* w, const float* x, int32_t ldx, int32_t m_rows, int32_t pre, const float* norm_w,
-                  float eps, float* y, int32_t ldy, int32_t rows_out, int32_t epi, int32_t* status, void* stream);
+                  float eps, float* y, int32_t ldy, int32_t rows_out, int32_t epi, void* scratch,
+                  size_t scratch_bytes, int32_t* status, void* stream);
 
 /* h[r, :] = dequant(lm_head row ids[r]) for r < n_rows (float32 [n_rows, d]). */
 int cb_embed(const CbMatrix* table, const int64_t* ids, int32_t n_rows, float* h, int32_t* status, void* stream);

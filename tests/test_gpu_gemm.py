@@ -1,5 +1,6 @@
 """Many-token tensor-core GEMM (cb_gemm_nvfp4: tcgen05.mma kind::f16 into
-tensor memory, f16 weights exact, f16 head + tail activations) against a
+tensor memory, f16 weights exact, f16 head + tail activations prepared by a
+first launch into caller scratch) against a
 float64 matmul of the float32 inputs and the oracle's dequantised NVFP4
 weights: the model's (N, K) shapes, token counts from 1 to 320 (several token
 tiles, ragged last tile), the RMSNorm prologue, the residual add and the fused
@@ -27,6 +28,12 @@ def L():
 
 def _st():
     return torch.cuda.current_stream().cuda_stream
+
+
+def _scratch(L, k, m):
+    n = L.cb_gemm_scratch_bytes(k, m)
+    buf = torch.empty(max(n, 16), dtype=torch.uint8, device=DEV)
+    return buf, buf.data_ptr(), n
 
 
 def _packed(n, k, seed):
@@ -57,8 +64,9 @@ def test_gemm_store_vs_f64(L, shape):
         x = torch.randn(M, k, generator=g)
         xd = x.to(DEV)
         y = torch.full((M, pm.rows), float("nan"), device=DEV)
+        buf, sp, sb = _scratch(L, k, M)
         rc = L.cb_gemm_nvfp4(C.byref(ms), xd.data_ptr(), k, M, _lib.CB_GEMM_PRE_NONE, None, 0.0,
-                             y.data_ptr(), pm.rows, n, _lib.CB_GEMM_EPI_STORE, status.data_ptr(), _st())
+                             y.data_ptr(), pm.rows, n, _lib.CB_GEMM_EPI_STORE, sp, sb, status.data_ptr(), _st())
         assert rc == 0, rc
         torch.cuda.synchronize()
         ref = x.double() @ deq.T
@@ -81,8 +89,9 @@ def test_gemm_rmsnorm_add(L, M):
     y = y0.clone().to(DEV)
     xd, nwd = x.to(DEV), nw.to(DEV)  # held in names: a temporary's memory could be reused before the launch
     ms = pm.struct()
+    buf, sp, sb = _scratch(L, k, M)
     rc = L.cb_gemm_nvfp4(C.byref(ms), xd.data_ptr(), k, M, _lib.CB_GEMM_PRE_RMSNORM, nwd.data_ptr(),
-                         eps, y.data_ptr(), n, n, _lib.CB_GEMM_EPI_ADD, None, _st())
+                         eps, y.data_ptr(), n, n, _lib.CB_GEMM_EPI_ADD, sp, sb, None, _st())
     assert rc == 0
     torch.cuda.synchronize()
     ref = y0.double() + _rms(x, nw, eps) @ deq.T
@@ -102,8 +111,9 @@ def test_gemm_swiglu(L, M):
     y = torch.full((M, F + 16), float("nan"), device=DEV)
     xd, nwd = x.to(DEV), nw.to(DEV)
     ms = pm.struct()
+    buf, sp, sb = _scratch(L, k, M)
     rc = L.cb_gemm_nvfp4(C.byref(ms), xd.data_ptr(), k, M, _lib.CB_GEMM_PRE_RMSNORM, nwd.data_ptr(),
-                         eps, y.data_ptr(), F + 16, F, _lib.CB_GEMM_EPI_SWIGLU, None, _st())
+                         eps, y.data_ptr(), F + 16, F, _lib.CB_GEMM_EPI_SWIGLU, sp, sb, None, _st())
     assert rc == 0
     torch.cuda.synchronize()
     h = _rms(x, nw, eps) @ deq.T
@@ -124,7 +134,9 @@ def test_gemm_matches_gemv(L):
     y1 = torch.empty(M, n, device=DEV)
     y2 = torch.empty(M, n, device=DEV)
     ms = pm.struct()
-    assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr(), k, M, 0, None, 0.0, y1.data_ptr(), n, n, 0, None, _st()) == 0
+    buf, sp, sb = _scratch(L, k, M)
+    assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr(), k, M, 0, None, 0.0, y1.data_ptr(), n, n, 0, sp, sb, None,
+                           _st()) == 0
     assert L.cb_gemv_nvfp4(C.byref(ms), x.data_ptr(), k, M, y2.data_ptr(), n, n, _st()) == 0
     torch.cuda.synchronize()
     assert ((y1 - y2).abs().max() / y2.abs().max()).item() < TOL
@@ -137,27 +149,33 @@ def test_gemm_rejects_bad_arguments(L):
     ms = pm.struct()
     x = torch.zeros(4, 64, device=DEV)
     y = torch.zeros(4, 64, device=DEV)
-    E_ARG, E_SHAPE = 1, 2
+    buf, sp, sb = _scratch(L, 64, 4)
+    E_ARG, E_SHAPE, E_WS = 1, 2, 4
     # unaligned x, ldx not a multiple of 4, rows_out above the rows, zero tokens, bad modes, RMSNorm without weights
-    assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr() + 4, 64, 2, 0, None, 0.0, y.data_ptr(), 64, 64, 0, None,
+    assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr() + 4, 64, 2, 0, None, 0.0, y.data_ptr(), 64, 64, 0, sp, sb, None,
                            _st()) == E_ARG
-    assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr(), 66, 2, 0, None, 0.0, y.data_ptr(), 64, 64, 0, None,
+    assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr(), 66, 2, 0, None, 0.0, y.data_ptr(), 64, 64, 0, sp, sb, None,
                            _st()) == E_ARG
-    assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr(), 64, 2, 0, None, 0.0, y.data_ptr(), 80, 80, 0, None,
+    assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr(), 64, 2, 0, None, 0.0, y.data_ptr(), 80, 80, 0, sp, sb, None,
                            _st()) == E_ARG
-    assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr(), 64, 0, 0, None, 0.0, y.data_ptr(), 64, 64, 0, None,
+    assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr(), 64, 0, 0, None, 0.0, y.data_ptr(), 64, 64, 0, sp, sb, None,
                            _st()) == E_ARG
-    assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr(), 64, 2, 5, None, 0.0, y.data_ptr(), 64, 64, 0, None,
+    assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr(), 64, 2, 5, None, 0.0, y.data_ptr(), 64, 64, 0, sp, sb, None,
                            _st()) == E_ARG
-    assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr(), 64, 2, 0, None, 0.0, y.data_ptr(), 64, 64, 7, None,
+    assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr(), 64, 2, 0, None, 0.0, y.data_ptr(), 64, 64, 7, sp, sb, None,
                            _st()) == E_ARG
     assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr(), 64, 2, _lib.CB_GEMM_PRE_RMSNORM, None, 0.0, y.data_ptr(), 64,
-                           64, 0, None, _st()) == E_ARG
+                           64, 0, sp, sb, None, _st()) == E_ARG
     # SwiGLU needs F = rows / 2 a multiple of 64
     assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr(), 64, 2, 0, None, 0.0, y.data_ptr(), 64, 32,
-                           _lib.CB_GEMM_EPI_SWIGLU, None, _st()) == E_SHAPE
+                           _lib.CB_GEMM_EPI_SWIGLU, sp, sb, None, _st()) == E_SHAPE
+    # scratch smaller than cb_gemm_scratch_bytes, or none
+    assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr(), 64, 2, 0, None, 0.0, y.data_ptr(), 64, 64, 0, sp, sb - 16, None,
+                           _st()) == E_WS
+    assert L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr(), 64, 2, 0, None, 0.0, y.data_ptr(), 64, 64, 0, None, sb, None,
+                           _st()) == E_ARG
     # K must be a multiple of 64
     pm2, _, _ = _packed(32, 48, 2)
     ms2 = pm2.struct()
-    assert L.cb_gemm_nvfp4(C.byref(ms2), x.data_ptr(), 64, 2, 0, None, 0.0, y.data_ptr(), 64, 32, 0, None,
+    assert L.cb_gemm_nvfp4(C.byref(ms2), x.data_ptr(), 64, 2, 0, None, 0.0, y.data_ptr(), 64, 32, 0, sp, sb, None,
                            _st()) == E_SHAPE
