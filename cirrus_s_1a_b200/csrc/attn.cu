@@ -229,7 +229,7 @@ int launch_swa(const SwaParams& p, int batch, cudaStream_t st) {
 // chunk's own keys are already in the ring, which must hold window + T - 1
 // positions so that no key a query of the chunk needs is overwritten.
 constexpr int kSpThreads = 256;
-constexpr int kSpQ = 16;     // tokens per CTA
+constexpr int kSpQ = 8;      // tokens per CTA
 constexpr int kSpKeys = 64;  // keys per tile
 constexpr int kSpMaxRows = kSpQ * 4;  // G <= 4 query heads per KV head
 
@@ -361,6 +361,7 @@ int launch_swa_prefill(const SwaParams& p, int batch, cudaStream_t st) {
     swa_prefill_kernel<N><<<grid, kSpThreads, smem, st>>>(p);                                      \
     break;
   switch (per) {
+    CB_SP_CASE(1)
     CB_SP_CASE(2)
     CB_SP_CASE(4)
     CB_SP_CASE(8)

@@ -162,3 +162,24 @@ def test_mtp_draft_matches_oracle(name):
         got = eng.mtp_draft(r.hidden[:, -1], torch.tensor([tok]))
         assert len(got) == cfg.mtp_passes
         assert got == want, (trial, got, want)
+
+
+@pytest.mark.parametrize("name", ["debug", "baseline"])
+def test_reference_verifier_loop_runs_over_the_engine(name):
+    """The reference's decoding loops (restated in oracle.decoding, pinned to the
+    reference's own token sequences on CPU) driven over CirrusB200 with their
+    default arguments -- speculative_greedy's max_draft 8 and MTP drafts from
+    CirrusB200.mtp_draft, cache.clone() snapshots and re-runs on partial
+    acceptance: the tokens are the greedy tokens, up to documented near-ties."""
+    eng, _ = _engine(name, seed=6)
+    vocab = eng.cfg.vocab_size
+    g = torch.Generator().manual_seed(11)
+    base = torch.randint(0, vocab, (9,), generator=g).tolist()
+    prompt = base + torch.randint(0, vocab, (7,), generator=g).tolist() + base[:4]
+    n = 24
+    want, margins = _eager_greedy(eng, [prompt], n)
+    assert od.greedy_loop(eng, prompt, n) == want[0]
+    got, steps = od.speculative_loop(eng, prompt, n)
+    assert len(got) == n
+    _agree(got, want[0], margins[0], "reference speculative loop")
+    assert steps <= n

@@ -235,3 +235,32 @@ def test_decoding_oracle_matches_reference_drafter():
         assert od.accept_greedy(c["draft"], c["target"]) == (n, list(emit))
     for c in rec["chooses"]:
         assert od.choose_draft(c["lookup"], c["mtp"]) == list(c["out"])
+
+
+class _OracleModel:
+    """The oracle forward behind the reference model's inference surface."""
+
+    def __init__(self, p, cfg):
+        self.p, self.cfg = p, cfg
+
+    def __call__(self, ids, cache=None, use_cache=False, n_logits=None):
+        return om.forward(self.p, self.cfg, ids, cache=cache, use_cache=use_cache, n_logits=n_logits)
+
+    def mtp_draft(self, h_last, token):
+        ids = self.p["draft_ids"].long()  # the fixture stores every tensor as float
+        return om.mtp_draft(self.p, self.cfg, h_last, int(token.reshape(-1)[0]), draft_ids=ids)
+
+
+@pytest.mark.parametrize("variant", ["sparse", "dense"])
+def test_verifier_loops_reproduce_reference_token_sequences(variant):
+    """oracle.decoding.greedy_loop / speculative_loop over the float64 oracle model
+    emit the tokens the reference's greedy / speculative_greedy emitted (default
+    max_draft 8 with MTP drafts, and without MTP) on the same model and prompt."""
+    from oracle import decoding as od
+
+    rec = golden("debug_ref.pt")[variant]
+    model = _OracleModel(_sd(rec), _debug_cfg(variant))
+    prompt = rec["gen_prompt"]
+    assert od.greedy_loop(model, prompt, 30) == rec["greedy"]
+    assert od.speculative_loop(model, prompt, 30)[0] == rec["spec_mtp"]
+    assert od.speculative_loop(model, prompt, 30, use_mtp=False)[0] == rec["spec_nomtp"]
