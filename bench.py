@@ -23,9 +23,14 @@ One JSON line on rank 0:
                read + write of one launch from an ncu capture of this workload
   weight_stream  the NVFP4 weight stream alone (every projection of a step,
                M = 1, as separate GEMV launches in one CUDA graph)
-  verify_gemm  the weight stream at M = 2, 4, 8 token rows through the tcgen05
-               verify GEMM and the CUDA-core GEMV
-  batched      step time of B sequences x T tokens (B = 8, 64; T = 1, 5)
+  weight_stream_by_M  the weight stream at M = 2 .. 64 token rows through the
+               tensor-core GEMM and the CUDA-core GEMV
+  batched      step time of B sequences x T tokens (B = 8, 64; T = 1, 5); more
+               than 16 token rows run on the tensor-core GEMM
+  spec_decode  configs[4] on this GPU: 64 sequences at 32K, prompt-lookup drafts
+               of 4, greedy acceptance with on-device rewind (SpecDecoder)
+  prefill      prompt tokens / s of the prefill path (512 and 32K tokens at
+               batch 1, 8 x 4096)
   cpu_baseline the oracle restatement of the reference forward on the host
                cores (rank 0, N = 1, a bounded number of 32K-context steps)
 
@@ -54,8 +59,8 @@ METRIC = "decode tok/s (batch 1, τ=1, 32K ctx) per B200 + HBM GB/s vs 8 TB/s; b
 # from an ncu capture (dram__bytes_read.sum + dram__bytes_write.sum), and the
 # SHA-256 prefix of the kernel source it was captured from: a changed source
 # reports traffic null until it is captured again.
-STEP_TRAFFIC = {"bytes": 95_557_120 + 3_375_104, "source": "cirrus_s_1a_b200/csrc/decode_mk.cu",
-                "sha256_16": "545d23fbf5629036"}
+STEP_TRAFFIC = {"bytes": 95_830_528 + 4_441_856, "source": "cirrus_s_1a_b200/csrc/decode_mk.cu",
+                "sha256_16": "4cb6df1e3d305bf6"}
 CPU_ARM_WHY = ("the reference is a Python package that cannot travel to the GPU box, so the CPU arm runs the "
                "oracle: the reference forward restated operation by operation (oracle/model.py), checked against "
                "fixtures generated from the reference itself (tests/golden), with the B200 storage casts")
@@ -154,9 +159,9 @@ def step_bytes(cfg, weight_bytes: float, ctx: int) -> dict:
 
 
 def weight_stream_graph(eng, M: int = 1, tensor_cores: bool = False):
-    """CUDA graph of one GEMV per projection matrix of the model (the
+    """CUDA graph of one product per projection matrix of the model (the
     reference's "decode-step weight stream", configs[1]) for M token rows:
-    the CUDA-core GEMV (fp32 x), or the tcgen05 verify GEMM (bf16 x)."""
+    the CUDA-core GEMV, or the tensor-core GEMM (input preparation + tcgen05)."""
     import ctypes as C
 
     import torch
@@ -168,8 +173,10 @@ def weight_stream_graph(eng, M: int = 1, tensor_cores: bool = False):
     dev = eng.device
     kmax = max(m.k for m in mats)
     x = torch.randn(M, kmax, device=dev)
-    xb = x.to(torch.bfloat16).view(torch.int16).contiguous()
     y = torch.empty(M, max(m.rows for m in mats), device=dev)
+    L0 = _lib.lib()
+    nb = L0.cb_gemm_scratch_bytes((kmax + 63) // 64 * 64, M)
+    scratch = torch.empty(max(nb, 16), dtype=torch.uint8, device=dev)
     ldy = y.shape[1]
     structs = [m.struct() for m in mats]
     L = _lib.lib()
@@ -178,8 +185,9 @@ def weight_stream_graph(eng, M: int = 1, tensor_cores: bool = False):
     def run(st):
         for s in structs:
             if tensor_cores:
-                _lib.check(L.cb_verify_gemm_nvfp4(C.byref(s), xb.data_ptr(), kmax, M, y.data_ptr(), ldy, s.rows,
-                                                  None, st), "verify_gemm")
+                _lib.check(L.cb_gemm_nvfp4(C.byref(s), x.data_ptr(), kmax, M, _lib.CB_GEMM_PRE_NONE, None, 0.0,
+                                           y.data_ptr(), ldy, s.rows, _lib.CB_GEMM_EPI_STORE, scratch.data_ptr(), nb,
+                                           None, st), "gemm")
             else:
                 _lib.check(L.cb_gemv_nvfp4(C.byref(s), x.data_ptr(), kmax, M, y.data_ptr(), ldy, s.rows, st), "gemv")
 
@@ -192,6 +200,7 @@ def weight_stream_graph(eng, M: int = 1, tensor_cores: bool = False):
     torch.cuda.current_stream(dev).wait_stream(side)
     torch.cuda.synchronize(dev)
     real = sum(m.real_bytes for m in mats)
+    g.keep = (x, y, scratch)  # buffers the captured launches use
     return g, len(structs), real
 
 
@@ -329,6 +338,34 @@ def spec_decode(eng, dev, stream, flush, args, rank: int) -> dict:
     del dec, cache
     torch.cuda.empty_cache()
     return out
+
+
+def prefill_bench(eng, dev, stream) -> dict:
+    """Prompt prefill through the public forward (cb_forward in 128-token chunks on
+    the prefill kernels): configs[0]'s 512-token prompt and a 32K prompt at batch 1,
+    and 8 x 4096; one warm-up, then one device-timed prefill each."""
+    import torch
+
+    from cirrus_s_1a_b200 import synthetic
+
+    out = []
+    for B, P in ((1, 512), (1, CTX), (8, 4096)):
+        ids = torch.tensor([synthetic.random_prompt(P, eng.cfg.vocab_size, seed=50 + b) for b in range(B)],
+                           device=dev)
+        ms = 0.0
+        for it in range(2):
+            cache = eng.new_cache(B, max_ctx=P + 64)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            eng(ids, cache=cache, n_logits=1)
+            b.record(stream)
+            b.synchronize()
+            ms = a.elapsed_time(b)
+            del cache
+        out.append({"batch": B, "prompt": P, "ms": ms, "tokens_per_s": B * P / (ms * 1e-3)})
+        torch.cuda.empty_cache()
+    return {"note": "prompt tokens / s through CirrusB200.forward (n_logits=1), device-timed, random weights",
+            "runs": out}
 
 
 def profile_step(B: int, T: int) -> None:
@@ -479,9 +516,9 @@ def main() -> None:
         if i >= args.warmup:
             w_ms.append(a.elapsed_time(b))
 
-    # ------------------------------------------------ verify GEMM (M = 2, 4, 8)
+    # ------------------------------------------------ weight stream at M token rows: tensor-core GEMM vs GEMV
     verify = {}
-    for M in (2, 4, 8):
+    for M in (2, 8, 16, 32, 64):
         row = {}
         for kind, tc in (("tcgen05", True), ("cuda_core", False)):
             vg, _, vbytes = weight_stream_graph(eng, M=M, tensor_cores=tc)
@@ -527,6 +564,7 @@ def main() -> None:
 
     # ------------------------------------------------ batched speculative decoding
     spec = spec_decode(eng, dev, stream, flush, args, rank)
+    prefill = prefill_bench(eng, dev, stream) if world == 1 else None
 
     tot = torch.tensor([t_total_ms, e2e_total, spec["ms"], spec["emitted"]], dtype=torch.float64, device=dev)
     if world > 1:  # the slowest rank's times; the tokens of every rank
@@ -561,12 +599,14 @@ def main() -> None:
                           "achieved": wbytes / w_avg_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                           "frac": wbytes / w_avg_s / 1e9 / peaks["hbm_gbs"], "bytes": wbytes,
                           "us": w_avg_s * 1e6},
-        "verify_gemm": {"bytes": wbytes, "unit": "GB/s", "note": f"{n_mats} projections per pass, L2 flushed, "
-                        "M token rows; tcgen05 = cb_verify_gemm_nvfp4 (bf16 x), cuda_core = cb_gemv_nvfp4",
-                        "by_M": verify},
+        "weight_stream_by_M": {"bytes": wbytes, "unit": "GB/s", "note": f"{n_mats} projections per pass, L2 "
+                               "flushed, M token rows; tcgen05 = cb_gemm_nvfp4 (input preparation + tcgen05 GEMM, 2 "
+                               "launches per projection), cuda_core = cb_gemv_nvfp4; cb_forward uses the GEMM from "
+                               "17 token rows", "by_M": verify},
         "batched": {"note": "per GPU, ctx 32768, L2 flushed, T tokens per sequence per step (T=5: a verify "
                                "of 1 + 4 draft tokens), device-timed CUDA-graph replay", "steps": batched},
         "spec_decode": spec,
+        "prefill": prefill,
         "e2e": {"value": world * args.steps / (e2e_total * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 8,
                 "d2h_bytes_per_step": 4, "ms_per_step": e2e_total / args.steps},
         "gpu_launches": launches_per_step * args.steps,

@@ -33,7 +33,7 @@ CB_GEMM_EPI_STORE, CB_GEMM_EPI_ADD, CB_GEMM_EPI_SWIGLU = 0, 1, 2
 EXPORTS = ("cb_abi_version", "cb_status_string", "cb_nvfp4_quantize", "cb_nvfp4_pack_tiles", "cb_gemv_nvfp4",
            "cb_embed", "cb_argmax", "cb_gdn_step", "cb_indexer_topk", "cb_workspace_bytes", "cb_forward",
            "cb_read_status", "cb_clear_status", "cb_launch_count", "cb_indexer_topk_noalloc", "cb_read_trace",
-           "cb_verify_gemm_nvfp4", "cb_gdn_chunk_prefill", "cb_set_wait_limit",
+           "cb_gdn_chunk_prefill", "cb_set_wait_limit",
            "cb_workspace_layout", "cb_nvfp4_slice_bytes", "cb_nvfp4_pack_slices", "cb_prompt_lookup_draft",
            "cb_spec_accept", "cb_mtp_workspace_bytes", "cb_mtp_draft", "cb_gemm_nvfp4", "cb_gemm_scratch_bytes")
 
@@ -122,7 +122,6 @@ def lib() -> C.CDLL:
         L.cb_nvfp4_slice_bytes.argtypes = [I32, I32]
         L.cb_nvfp4_pack_slices.argtypes = [P, P, I32, I32, I32, P, P]
         L.cb_gemv_nvfp4.argtypes = [C.POINTER(CbMatrix), P, I32, I32, P, I32, I32, P]
-        L.cb_verify_gemm_nvfp4.argtypes = [C.POINTER(CbMatrix), P, I32, I32, P, I32, I32, P, P]
         L.cb_gemm_nvfp4.argtypes = [C.POINTER(CbMatrix), P, I32, I32, I32, P, C.c_float, P, I32, I32, I32, P,
                                     C.c_size_t, P, P]
         L.cb_gemm_scratch_bytes.restype = C.c_size_t

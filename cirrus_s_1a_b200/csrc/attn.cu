@@ -264,24 +264,44 @@ __global__ void __launch_bounds__(kSpThreads) swa_prefill_kernel(SwaParams p) {
   const uint16_t* kr = p.kring + (int64_t)b * p.seq_stride;
   const uint16_t* vr = p.vring + (int64_t)b * p.seq_stride;
   const int warp = tid >> 5, lane = tid & 31, vpk = hd / 8;
+  // K/V tiles: the next tile's 16-byte vectors are loaded into registers while
+  // the current tile is processed, then converted into shared memory
+  constexpr int kSpLd = kSpKeys * 16 / kSpThreads;  // vectors per thread (head_dim <= 128)
+  uint4 pk[kSpLd], pv[kSpLd];
+  auto fetch = [&](int kt) {
+    const int nn = min(kSpKeys, khi + 1 - kt);
+#pragma unroll
+    for (int e = 0; e < kSpLd; ++e) {
+      const int i = tid + e * kSpThreads;
+      if (kt <= khi && i < nn * vpk) {
+        const int key = i / vpk, e8 = (i - key * vpk) * 8;
+        const int64_t off = ((int64_t)((kt + key) % p.slots) * p.Hkv + g) * hd + e8;
+        pk[e] = *reinterpret_cast<const uint4*>(kr + off);
+        pv[e] = *reinterpret_cast<const uint4*>(vr + off);
+      }
+    }
+  };
+  fetch(klo);
   for (int kt0 = klo; kt0 <= khi; kt0 += kSpKeys) {
     const int n = min(kSpKeys, khi + 1 - kt0);
     __syncthreads();  // the previous tile's K, V and P are consumed
-    for (int i = tid; i < n * vpk; i += kSpThreads) {
-      const int key = i / vpk, e8 = (i - key * vpk) * 8;
-      const int64_t off = ((int64_t)((kt0 + key) % p.slots) * p.Hkv + g) * hd + e8;
-      const uint4 kq = *reinterpret_cast<const uint4*>(kr + off);
-      const uint4 vq = *reinterpret_cast<const uint4*>(vr + off);
-      const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w}, vw[4] = {vq.x, vq.y, vq.z, vq.w};
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        Ks[key * (hd + 1) + e8 + 2 * e] = bf16_to_f32(kw[e]);
-        Ks[key * (hd + 1) + e8 + 2 * e + 1] = bf16_to_f32(kw[e] >> 16);
-        Vs[key * hd + e8 + 2 * e] = bf16_to_f32(vw[e]);
-        Vs[key * hd + e8 + 2 * e + 1] = bf16_to_f32(vw[e] >> 16);
+    for (int e = 0; e < kSpLd; ++e) {
+      const int i = tid + e * kSpThreads;
+      if (i < n * vpk) {
+        const int key = i / vpk, e8 = (i - key * vpk) * 8;
+        const uint32_t kw[4] = {pk[e].x, pk[e].y, pk[e].z, pk[e].w}, vw[4] = {pv[e].x, pv[e].y, pv[e].z, pv[e].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          Ks[key * (hd + 1) + e8 + 2 * q] = bf16_to_f32(kw[q]);
+          Ks[key * (hd + 1) + e8 + 2 * q + 1] = bf16_to_f32(kw[q] >> 16);
+          Vs[key * hd + e8 + 2 * q] = bf16_to_f32(vw[q]);
+          Vs[key * hd + e8 + 2 * q + 1] = bf16_to_f32(vw[q] >> 16);
+        }
       }
     }
     __syncthreads();
+    fetch(kt0 + kSpKeys);
     // scores: thread (key j, rows r0, r0 + 4, ...)
     {
       const int j = tid & (kSpKeys - 1), kp = kt0 + j;

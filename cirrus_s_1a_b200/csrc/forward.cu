@@ -65,6 +65,8 @@ static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 // Token rows from which a projection runs on the tensor cores (cb_gemm_nvfp4)
 // instead of the CUDA-core GEMV.
 constexpr int kGemmMinRows = 17;
+// Token rows (batch * tokens) from which SWA decode runs block-wise.
+constexpr int kSwaBlockRows = 32;
 
 static int swa_splits(const CbModel& m) { return ceil_div(m.swa_window + CB_MAX_T, kSwaSplit); }
 static int cross_splits(const CbModel& m) {
@@ -521,7 +523,12 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
         sp.ldg = ldp;
         sp.out = w.attn;
         sp.ldo = w.att_ld;
-        if (tc > CB_MAX_T) CB_TRY(launch_swa_prefill(sp, B, st));
+        // prompt chunks, and decode / verify steps of many sequences: the block-wise
+        // kernel (one CTA per sequence, KV head and 8 tokens) instead of the
+        // split-window kernel, whose launch grows with the window
+        const bool blockwise = swa_prefill_supported(m.n_q_heads, m.n_kv_heads, m.head_dim) &&
+                               c.swa_slots >= m.swa_window + tc - 1 && (tc > CB_MAX_T || R >= kSwaBlockRows);
+        if (blockwise) CB_TRY(launch_swa_prefill(sp, B, st));
         else CB_TRY(launch_swa(sp, B, st));
       }
       CB_TRY(proj(w, L.o_proj, w.attn, w.att_ld, R, nullptr, 0.f, PRE_NONE, EPI_ADD, w.h, d, d, st));

@@ -1,6 +1,7 @@
-"""Microbenchmark of one NVFP4 projection: the tcgen05 verify GEMM
-(cb_verify_gemm_nvfp4) or the CUDA-core GEMV (cb_gemv_nvfp4) on random
-weights of one (N, K) shape, M token rows, L2 flushed before every launch.
+"""Microbenchmark of one NVFP4 projection: the tensor-core GEMM
+(cb_gemm_nvfp4: input preparation + tcgen05 GEMM) or the CUDA-core GEMV
+(cb_gemv_nvfp4) on random weights of one (N, K) shape, M token rows, L2
+flushed before every launch.
 
     python -m cirrus_s_1a_b200.microbench --n 32000 --k 768 --m 8 --iters 20 [--gemv]
 
@@ -47,20 +48,22 @@ def main() -> None:
     g = torch.Generator().manual_seed(0)
     pm = PackedMatrix([torch.randn(args.n, args.k, generator=g) * 0.02], dev)
     x = torch.randn(args.m, args.k, generator=g).to(dev)
-    xb = x.to(torch.bfloat16).view(torch.int16).contiguous()
     y = torch.empty(args.m, pm.rows, device=dev)
     flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
     L = _lib.lib()
     ms = pm.struct()
     st = torch.cuda.current_stream(dev).cuda_stream
+    nb = L.cb_gemm_scratch_bytes(args.k, args.m)
+    scratch = torch.empty(max(nb, 16), dtype=torch.uint8, device=dev)
 
     def launch():
         if args.gemv:
             _lib.check(L.cb_gemv_nvfp4(C.byref(ms), x.data_ptr(), args.k, args.m, y.data_ptr(), pm.rows, args.n, st),
                        "cb_gemv_nvfp4")
         else:
-            _lib.check(L.cb_verify_gemm_nvfp4(C.byref(ms), xb.data_ptr(), args.k, args.m, y.data_ptr(), pm.rows,
-                                              args.n, None, st), "cb_verify_gemm_nvfp4")
+            _lib.check(L.cb_gemm_nvfp4(C.byref(ms), x.data_ptr(), args.k, args.m, _lib.CB_GEMM_PRE_NONE, None, 0.0,
+                                       y.data_ptr(), pm.rows, args.n, _lib.CB_GEMM_EPI_STORE, scratch.data_ptr(), nb,
+                                       None, st), "cb_gemm_nvfp4")
 
     times = []
     for i in range(args.warmup + args.iters):
@@ -73,7 +76,7 @@ def main() -> None:
         if i >= args.warmup:
             times.append(a.elapsed_time(b) * 1e3)
     us = statistics.mean(times)
-    print(json.dumps({"kernel": "gemv_nvfp4" if args.gemv else "verify_gemm (tcgen05)", "n": args.n, "k": args.k,
+    print(json.dumps({"kernel": "gemv_nvfp4" if args.gemv else "gemm_nvfp4 (tcgen05)", "n": args.n, "k": args.k,
                       "m": args.m, "us": us, "bytes": pm.real_bytes, "gbs": pm.real_bytes / (us * 1e-6) / 1e9,
                       "flops": 2 * args.m * args.n * args.k}))
 

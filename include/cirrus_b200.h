@@ -15,7 +15,8 @@
  *   cb_nvfp4_pack_tiles   pack_nvfp4_mma / pack_nvfp4_v3  scripts/bench_spark.py:369-391, 639-660
  *   cb_nvfp4_pack_slices  (same packers: a column-sliced layout of the standard format)
  *   cb_gemv_nvfp4         nvfp4_gemv                     cirrus/perf/bench_kernels.cu:202-227
- *   cb_verify_gemm_nvfp4  nvfp4_gemv, M = 2..16 (verify)  cirrus/perf/bench_kernels.cu:202-227, 1079-1300
+ *   cb_gemm_nvfp4         nvfp4_gemv, M > 1 (verify, batched, prefill)  cirrus/perf/bench_kernels.cu:202-227,
+ *                         1079-1300; the dense nn.Linear products of CirrusModel.forward
  *   cb_gdn_chunk_prefill  chunk_gated_delta_rule (fla)    cirrus/model/layers.py:165-170 (recurrence :108-129)
  *                         (and every nn.Linear of the model, layers.py)
  *   cb_gdn_step           GatedDeltaNet.forward          cirrus/model/layers.py:151-174
@@ -191,17 +192,6 @@ int cb_nvfp4_pack_tiles(const uint8_t* codes, const uint8_t* scales, int32_t n, 
  * x row stride ldx, y row stride ldy (elements).  Any m_rows >= 1. */
 int cb_gemv_nvfp4(const CbMatrix* w, const float* x, int32_t ldx, int32_t m_rows, float* y, int32_t ldy,
                   int32_t rows_out, void* stream);
-
-/* Multi-token verify GEMM on the tensor cores (tcgen05.mma kind::f16 into tensor
- * memory): y[m, :rows_out] = x[m, :k] @ dequant(W)^T for m < m_rows <= 16, with x
- * bf16 [m_rows][ldx] (ldx % 8 == 0, 16-byte aligned) and y fp32 [m_rows][ldy].
- * W.k must be a multiple of 64 and <= 2048.  The dequantised weights are exact in
- * bf16; accumulation is fp32.  status (device int32, may be null) receives
- * CB_ERR_TIMEOUT if a bounded wait on the tensor-core pipeline gives up.
- * Replaces nvfp4_gemv with M > 1 (the verify of 1 + draft tokens),
- * cirrus/perf/bench_kernels.cu:202-227 and its v4/v5 mma kernels :1079-1300. */
-int cb_verify_gemm_nvfp4(const CbMatrix* w, const uint16_t* x, int32_t ldx, int32_t m_rows, float* y, int32_t ldy,
-                         int32_t rows_out, int32_t* status, void* stream);
 
 /* Many-token GEMM on the tensor cores (tcgen05.mma kind::f16 into tensor memory)
  * for steps that carry many token rows (batched decode, batched verify, prompt

@@ -55,7 +55,8 @@ def test_host_argument_checks_fail_without_launching(built_lib):
     assert built_lib.cb_argmax(None, 1, 1, 1, None, None) == 1
     assert built_lib.cb_forward(None, None, None, 0, None, 1, 1, None, None, None, None) == 1
     assert built_lib.cb_workspace_bytes(None, 1, 1, 1) == 0
-    assert built_lib.cb_verify_gemm_nvfp4(None, None, 0, 1, None, 0, 0, None, None) == 1
+    assert built_lib.cb_gemm_nvfp4(None, None, 0, 1, 0, None, 0.0, None, 0, 0, 0, None, 0, None, None) == 1
+    assert built_lib.cb_gemm_scratch_bytes(768, 64) == 12 * 16384 and built_lib.cb_gemm_scratch_bytes(100, 1) == 0
     assert built_lib.cb_gdn_chunk_prefill(None, None, None, None, None, 1, 1, 1, 64, 64, 1.0, None, None, None) == 1
 
 
