@@ -59,7 +59,7 @@ METRIC = "decode tok/s (batch 1, τ=1, 32K ctx) per B200 + HBM GB/s vs 8 TB/s; b
 # from an ncu capture (dram__bytes_read.sum + dram__bytes_write.sum), and the
 # SHA-256 prefix of the kernel source it was captured from: a changed source
 # reports traffic null until it is captured again.
-STEP_TRAFFIC = {"bytes": 95_830_528 + 4_441_856, "source": "cirrus_s_1a_b200/csrc/decode_mk.cu",
+STEP_TRAFFIC = {"bytes": 95_833_088 + 4_164_096, "source": "cirrus_s_1a_b200/csrc/decode_mk.cu",
                 "sha256_16": "4cb6df1e3d305bf6"}
 CPU_ARM_WHY = ("the reference is a Python package that cannot travel to the GPU box, so the CPU arm runs the "
                "oracle: the reference forward restated operation by operation (oracle/model.py), checked against "
@@ -393,6 +393,87 @@ def profile_step(B: int, T: int) -> None:
     print(json.dumps({"profile_step": {"batch": B, "T": T, "ctx": CTX}}), flush=True)
 
 
+def profile_prefill(B: int, P: int) -> None:
+    """One warm-up prefill and one prefill inside an NVTX range 'prefill' (B
+    prompts of P tokens), for a profiler's launch list."""
+    import torch
+
+    from cirrus_s_1a_b200 import synthetic
+    from cirrus_s_1a_b200.config import baseline_config
+    from cirrus_s_1a_b200.engine import CirrusB200
+
+    cfg = baseline_config()
+    eng = CirrusB200(cfg, synthetic.random_state_dict(cfg, seed=0), device="cuda:0", max_ctx=P + 64)
+    ids = torch.tensor([synthetic.random_prompt(P, cfg.vocab_size, seed=s) for s in range(B)], device="cuda:0")
+    for it in range(2):
+        cache = eng.new_cache(B, max_ctx=P + 64)
+        torch.cuda.synchronize()
+        if it:
+            torch.cuda.nvtx.range_push("prefill")
+        eng(ids, cache=cache, n_logits=1)
+        if it:
+            torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+    print(json.dumps({"profile_prefill": {"batch": B, "prompt": P}}), flush=True)
+
+
+def trace_step(B: int, T: int) -> None:
+    """Per-phase timing of the persistent kernel (CTA 0's %globaltimer stamps at
+    every grid barrier and its sub-phase marks) for B sequences x T tokens at
+    32K, L2 flushed before each of 6 steps; prints one JSON line grouped by phase type."""
+    import ctypes as C
+
+    import torch
+
+    from cirrus_s_1a_b200 import _lib, synthetic
+    from cirrus_s_1a_b200.config import baseline_config
+    from cirrus_s_1a_b200.engine import CirrusB200, DecodeGraph
+
+    cfg = baseline_config()
+    eng = CirrusB200(cfg, synthetic.random_state_dict(cfg, seed=0), device="cuda:0", max_ctx=CTX + 64)
+    names = []
+    for kind in cfg.self_layer_kinds:
+        names += ["gdn"] if kind == "gdn" else ["swa_in", "swa_attention", "swa_o"]
+        names.append("ffn_self")
+    names += ["shared_proj", "append_scores", "compaction"] + ["cross_q", "cross_attention", "cross_o",
+                                                               "ffn_cross"] * cfg.n_cross_layers + ["lm_head"]
+    cache = eng.new_cache(B)
+    synthetic.fill_cache(cache, CTX - 8, seed=1)
+    g = DecodeGraph(eng, cache, T=T, n_logits=T, want_logits=False)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda:0")
+    us = []
+    for _ in range(6):
+        cache.pos_dev.fill_(CTX - 8)
+        flush.random_(0, 255)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        b.synchronize()
+        us.append(a.elapsed_time(b) * 1e3)
+    ws = eng.workspace(B, T, cache.max_ctx)
+    buf = (C.c_uint64 * 512)()
+    n = _lib.lib().cb_read_trace(C.byref(eng.model.desc), B, T, cache.max_ctx, ws.data_ptr(), buf, 512,
+                                 torch.cuda.current_stream().cuda_stream)
+    v = list(buf[:n])
+    agg = {}
+    for p, name in enumerate(names):  # barrier 1 ends the set-up; phase p ends at barrier p + 2
+        start, arrive, leave = v[2 * (p + 1)], v[2 * (p + 2) - 1], v[2 * (p + 2)]
+        marks = [(v[256 + 4 * p + i] - start) / 1e3 for i in range(4) if start <= v[256 + 4 * p + i] <= arrive]
+        e = agg.setdefault(name, {"count": 0, "work_us": 0.0, "wait_us": 0.0, "marks_us": [0.0] * 4})
+        e["count"] += 1
+        e["work_us"] += (arrive - start) / 1e3
+        e["wait_us"] += (leave - arrive) / 1e3
+        for i, m in enumerate(marks):
+            e["marks_us"][i] += m
+    for e in agg.values():
+        c = e["count"]
+        e["work_us"], e["wait_us"] = e["work_us"] / c, e["wait_us"] / c
+        e["marks_us"] = [m / c for m in e["marks_us"]]
+    print(json.dumps({"trace_step": {"batch": B, "T": T, "ctx": CTX, "step_us_median": sorted(us)[len(us) // 2],
+                                     "per_phase": agg}}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -404,11 +485,22 @@ def main() -> None:
     ap.add_argument("--profile-step", metavar="BxT", default=None,
                     help="run two eager batched steps (B sequences x T tokens) inside NVTX ranges named 'step' "
                          "for a profiler's launch list, then exit")
+    ap.add_argument("--trace-step", metavar="BxT", default=None,
+                    help="print the persistent kernel's per-phase timing for B sequences x T tokens, then exit")
+    ap.add_argument("--profile-prefill", metavar="BxP", default=None,
+                    help="run a warm-up prefill and one prefill (B prompts of P tokens) inside an NVTX range "
+                         "named 'prefill', then exit")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.profile_step:
         profile_step(*(int(v) for v in args.profile_step.lower().split("x")))
+        return
+    if args.trace_step:
+        trace_step(*(int(v) for v in args.trace_step.lower().split("x")))
+        return
+    if args.profile_prefill:
+        profile_prefill(*(int(v) for v in args.profile_prefill.lower().split("x")))
         return
 
     rank = int(os.environ.get("RANK", "0"))
