@@ -217,6 +217,136 @@ int launch_swa(const SwaParams& p, int batch, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
 }
 
+// ------------------------------------------------------------- SWA decode, many sequences
+// One token per sequence: one CTA per (KV head, sequence), 8 warps over the
+// window's keys.  In a warp, groups of hd/8 lanes take one key each (a lane
+// owns 8 dimensions: one 16-byte K load and one V load per key), so a warp
+// reads 32 * 16 bytes of K and of V per step; each group keeps a running
+// (max, sum, o) per query head of the KV head, the groups and then the warps
+// are merged in a fixed order.  Scores are partial dot products summed over
+// the group's lanes by shuffles.
+constexpr int kSdThreads = 256;
+constexpr int kSdMaxG = 4;
+
+__global__ void __launch_bounds__(kSdThreads) swa_decode_kernel(SwaParams p) {
+  const int g = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int hd = p.hd, G = p.Hq / p.Hkv, LK = hd / 8, KG = 32 / LK;
+  const int kg = lane / LK, sub = lane - kg * LK;
+  const int P0 = p.pos[b] + p.c0;
+  const int lo = max(0, P0 - p.window + 1), n = P0 - lo + 1;
+  // this warp's keys [k0, k1)
+  const int k0 = lo + warp * n / (kSdThreads / 32), k1 = lo + (warp + 1) * n / (kSdThreads / 32);
+  float q[kSdMaxG][8], o[kSdMaxG][8], m[kSdMaxG], l[kSdMaxG];
+  const float* qrow = p.q + (int64_t)b * p.ldq;
+#pragma unroll
+  for (int j = 0; j < kSdMaxG; ++j) {
+    m[j] = -INFINITY;
+    l[j] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      q[j][e] = j < G ? qrow[(g * G + j) * hd + sub * 8 + e] * p.scale : 0.0f;
+      o[j][e] = 0.0f;
+    }
+  }
+  const uint16_t* kr = p.kring + (int64_t)b * p.seq_stride;
+  const uint16_t* vr = p.vring + (int64_t)b * p.seq_stride;
+  for (int kb = k0; kb < k1; kb += KG) {
+    const int key = kb + kg;
+    const bool valid = key < k1;
+    uint4 kq = make_uint4(0u, 0u, 0u, 0u), vq = kq;
+    if (valid) {
+      const int64_t off = ((int64_t)(key % p.slots) * p.Hkv + g) * hd + sub * 8;
+      kq = *reinterpret_cast<const uint4*>(kr + off);
+      vq = *reinterpret_cast<const uint4*>(vr + off);
+    }
+    const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w}, vw[4] = {vq.x, vq.y, vq.z, vq.w};
+    float kf[8], vf[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      kf[2 * e] = bf16_to_f32(kw[e]);
+      kf[2 * e + 1] = bf16_to_f32(kw[e] >> 16);
+      vf[2 * e] = bf16_to_f32(vw[e]);
+      vf[2 * e + 1] = bf16_to_f32(vw[e] >> 16);
+    }
+#pragma unroll
+    for (int j = 0; j < kSdMaxG; ++j) {
+      if (j < G) {
+        float sc = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sc = fmaf(q[j][e], kf[e], sc);
+        for (int off = LK / 2; off > 0; off >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, off);
+        if (valid) {
+          const float mn = fmaxf(m[j], sc);
+          const float c = m[j] == -INFINITY ? 0.0f : expf(m[j] - mn);
+          const float pe = expf(sc - mn);
+          l[j] = l[j] * c + pe;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[j][e] = fmaf(pe, vf[e], o[j][e] * c);
+          m[j] = mn;
+        }
+      }
+    }
+  }
+  // merge the key groups of the warp (lanes sub, sub + LK, ...), then the warps
+  for (int off = LK; off < 32; off <<= 1) {
+#pragma unroll
+    for (int j = 0; j < kSdMaxG; ++j) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m[j], off), l2 = __shfl_xor_sync(0xffffffffu, l[j], off);
+      const float mn = fmaxf(m[j], m2);
+      const float c1 = m[j] == -INFINITY ? 0.0f : expf(m[j] - mn), c2 = m2 == -INFINITY ? 0.0f : expf(m2 - mn);
+      l[j] = l[j] * c1 + l2 * c2;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float o2 = __shfl_xor_sync(0xffffffffu, o[j][e], off);
+        o[j][e] = o[j][e] * c1 + o2 * c2;
+      }
+      m[j] = mn;
+    }
+  }
+  __shared__ float wm[kSdThreads / 32][kSdMaxG], wl[kSdThreads / 32][kSdMaxG];
+  __shared__ float wo[kSdThreads / 32][kSdMaxG][256];
+  if (kg == 0) {
+#pragma unroll
+    for (int j = 0; j < kSdMaxG; ++j) {
+      if (sub == 0) {
+        wm[warp][j] = m[j];
+        wl[warp][j] = l[j];
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) wo[warp][j][sub * 8 + e] = o[j][e];
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < G * hd; i += kSdThreads) {
+    const int j = i / hd, d = i - j * hd;
+    float M = -INFINITY;
+    for (int w = 0; w < kSdThreads / 32; ++w) M = fmaxf(M, wm[w][j]);
+    float L = 0.0f, O = 0.0f;
+    for (int w = 0; w < kSdThreads / 32; ++w) {
+      if (wm[w][j] == -INFINITY) continue;
+      const float c = expf(wm[w][j] - M);
+      L += wl[w][j] * c;
+      O += wo[w][j][d] * c;
+    }
+    const int qh = g * G + j;
+    const float gate = sigmoid(p.gate[(int64_t)b * p.ldg + qh]);
+    p.out[(int64_t)b * p.ldo + qh * hd + d] = (O / L) * gate;
+  }
+}
+
+bool swa_decode_supported(int Hq, int Hkv, int hd) {
+  const int G = Hkv > 0 ? Hq / Hkv : 0;
+  return hd >= 8 && hd <= 256 && hd % 8 == 0 && 32 % (hd / 8) == 0 && G >= 1 && G <= kSdMaxG && G * Hkv == Hq;
+}
+
+int launch_swa_decode(const SwaParams& p, int batch, cudaStream_t st) {
+  if (!swa_decode_supported(p.Hq, p.Hkv, p.hd) || p.T != 1) return CB_ERR_SHAPE;
+  swa_decode_kernel<<<dim3(p.Hkv, batch), kSdThreads, 0, st>>>(p);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
+
 // ------------------------------------------------------------- SWA prefill
 // Block-wise sliding-window attention for a prompt chunk (the reference's
 // _sliding_window_attend, layers.py:195-210, over the ring instead of a padded

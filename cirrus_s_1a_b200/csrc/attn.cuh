@@ -102,6 +102,9 @@ int launch_swa(const SwaParams& p, int batch, cudaStream_t st);
 // Prompt chunks: block-wise SWA (rows b * T + t), gated output straight into out.
 int launch_swa_prefill(const SwaParams& p, int batch, cudaStream_t st);
 bool swa_prefill_supported(int Hq, int Hkv, int hd);
+// Decode steps (T = 1) of many sequences: one CTA per (KV head, sequence), lanes over keys.
+int launch_swa_decode(const SwaParams& p, int batch, cudaStream_t st);
+bool swa_decode_supported(int Hq, int Hkv, int hd);
 int launch_cross(const CrossParams& p, int rows, cudaStream_t st);
 int launch_indexer_topk(const IndexerParams& p, cudaStream_t st);
 

@@ -528,8 +528,12 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
         // split-window kernel, whose launch grows with the window
         const bool blockwise = swa_prefill_supported(m.n_q_heads, m.n_kv_heads, m.head_dim) &&
                                c.swa_slots >= m.swa_window + tc - 1 && (tc > CB_MAX_T || R >= kSwaBlockRows);
-        if (blockwise) CB_TRY(launch_swa_prefill(sp, B, st));
-        else CB_TRY(launch_swa(sp, B, st));
+        if (tc == 1 && R >= kSwaBlockRows && swa_decode_supported(m.n_q_heads, m.n_kv_heads, m.head_dim))
+          CB_TRY(launch_swa_decode(sp, B, st));
+        else if (blockwise)
+          CB_TRY(launch_swa_prefill(sp, B, st));
+        else
+          CB_TRY(launch_swa(sp, B, st));
       }
       CB_TRY(proj(w, L.o_proj, w.attn, w.att_ld, R, nullptr, 0.f, PRE_NONE, EPI_ADD, w.h, d, d, st));
       CB_TRY(ffn(L.gate_up, L.down, L.norm2, m, w.h, R, w, st));

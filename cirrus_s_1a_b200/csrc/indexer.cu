@@ -52,9 +52,50 @@ __global__ void __launch_bounds__(kScoreThreads) indexer_score_kernel(IndexerPar
   __syncthreads();
   const uint8_t* ikb = p.ik + (int64_t)b * p.ik_seq_stride;
   float* out = p.scores + (int64_t)r * p.max_ctx;
+  // Each key's 8-byte groups are read and converted once and feed every head
+  // (up to kHiFast heads in registers; more heads take the per-head loop).
+  constexpr int kHiFast = 4;
   for (int j = blockIdx.x * kScoreThreads + threadIdx.x; j < n; j += gridDim.x * kScoreThreads) {
     const uint8_t* kr = ikb + (int64_t)j * Di;
     float score = 0.0f;
+    if (Hi <= kHiFast) {
+      float pr[kHiFast][8];
+      for (int i = 0; i < Di / 8; ++i) {
+        const uint2 raw = *reinterpret_cast<const uint2*>(kr + 8 * i);
+        float kv[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {  // pairs of E4M3 codes -> exact halves -> floats
+          const uint32_t w2 = ((e < 2 ? raw.x : raw.y) >> (16 * (e & 1))) & 0xFFFF;
+          const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)w2, __NV_E4M3);
+          const float2 f = __half22float2(__half2(hr));
+          kv[2 * e] = f.x;
+          kv[2 * e + 1] = f.y;
+        }
+#pragma unroll
+        for (int h = 0; h < kHiFast; ++h) {
+          if (h < Hi) {
+            const float* qh = q + h * Di + 8 * i;
+#pragma unroll
+            for (int rr = 0; rr < 8; ++rr) {
+              const float prod = __fmul_rn(kv[rr], qh[rr]);
+              pr[h][rr] = i == 0 ? prod : __fadd_rn(pr[h][rr], prod);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < kHiFast; ++h) {
+        if (h < Hi) {
+          const float d = __fadd_rn(__fadd_rn(__fadd_rn(pr[h][0], pr[h][1]), __fadd_rn(pr[h][2], pr[h][3])),
+                                    __fadd_rn(__fadd_rn(pr[h][4], pr[h][5]), __fadd_rn(pr[h][6], pr[h][7])));
+          const float rl = d > 0.0f ? d : 0.0f;
+          const float term = __fmul_rn(rl, w[h]);
+          score = h == 0 ? term : __fadd_rn(score, term);
+        }
+      }
+      out[j] = score;
+      continue;
+    }
     for (int h = 0; h < Hi; ++h) {
       const float* qh = q + h * Di;
       float pr[8];
