@@ -217,46 +217,41 @@ int launch_swa(const SwaParams& p, int batch, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
 }
 
-// ------------------------------------------------------------- SWA decode, many sequences
-// One token per sequence: one CTA per (KV head, sequence), 8 warps over the
-// window's keys.  In a warp, groups of hd/8 lanes take one key each (a lane
-// owns 8 dimensions: one 16-byte K load and one V load per key), so a warp
-// reads 32 * 16 bytes of K and of V per step; each group keeps a running
-// (max, sum, o) per query head of the KV head, the groups and then the warps
-// are merged in a fixed order.  Scores are partial dot products summed over
-// the group's lanes by shuffles.
+// ------------------------------------------------------- decode attention, many rows
+// One query token: one CTA per (KV head, query row), 8 warps over the keys.
+// In a warp, groups of hd/8 lanes take one key each (a lane owns 8 dimensions:
+// one 16-byte K load and one V load per key), so a warp reads 32 x 16 bytes of
+// K and of V per step; each group keeps a running (max, sum, o) per query head
+// of the KV head, and the groups, then the warps, are merged in a fixed order.
+// Scores are partial dot products summed over the group's lanes by shuffles.
 constexpr int kSdThreads = 256;
 constexpr int kSdMaxG = 4;
 
-__global__ void __launch_bounds__(kSdThreads) swa_decode_kernel(SwaParams p) {
-  const int g = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
-  const int warp = tid >> 5, lane = tid & 31;
-  const int hd = p.hd, G = p.Hq / p.Hkv, LK = hd / 8, KG = 32 / LK;
-  const int kg = lane / LK, sub = lane - kg * LK;
-  const int P0 = p.pos[b] + p.c0;
-  const int lo = max(0, P0 - p.window + 1), n = P0 - lo + 1;
-  // this warp's keys [k0, k1)
-  const int k0 = lo + warp * n / (kSdThreads / 32), k1 = lo + (warp + 1) * n / (kSdThreads / 32);
+// Keys key_of(i) for i < n of this CTA's (KV head g, row) against qs [G][hd]
+// (already scaled), into out[row][(g * G + j) * hd + d] = o / l * sigmoid(gate[j]).
+template <typename KeyOf>
+__device__ __forceinline__ void decode_attend(const float* qs, int G, int hd, int g, int Hkv, int n, KeyOf key_of,
+                                              const uint16_t* kr, const uint16_t* vr, const float* gate, float* out) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int LK = hd / 8, KG = 32 / LK, kg = lane / LK, sub = lane - kg * LK;
+  const int k0 = warp * n / (kSdThreads / 32), k1 = (warp + 1) * n / (kSdThreads / 32);
   float q[kSdMaxG][8], o[kSdMaxG][8], m[kSdMaxG], l[kSdMaxG];
-  const float* qrow = p.q + (int64_t)b * p.ldq;
 #pragma unroll
   for (int j = 0; j < kSdMaxG; ++j) {
     m[j] = -INFINITY;
     l[j] = 0.0f;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      q[j][e] = j < G ? qrow[(g * G + j) * hd + sub * 8 + e] * p.scale : 0.0f;
+      q[j][e] = j < G ? qs[j * hd + sub * 8 + e] : 0.0f;
       o[j][e] = 0.0f;
     }
   }
-  const uint16_t* kr = p.kring + (int64_t)b * p.seq_stride;
-  const uint16_t* vr = p.vring + (int64_t)b * p.seq_stride;
   for (int kb = k0; kb < k1; kb += KG) {
-    const int key = kb + kg;
-    const bool valid = key < k1;
+    const int i = kb + kg;
+    const bool valid = i < k1;
     uint4 kq = make_uint4(0u, 0u, 0u, 0u), vq = kq;
     if (valid) {
-      const int64_t off = ((int64_t)(key % p.slots) * p.Hkv + g) * hd + sub * 8;
+      const int64_t off = ((int64_t)key_of(i) * Hkv + g) * hd + sub * 8;
       kq = *reinterpret_cast<const uint4*>(kr + off);
       vq = *reinterpret_cast<const uint4*>(vr + off);
     }
@@ -329,20 +324,71 @@ __global__ void __launch_bounds__(kSdThreads) swa_decode_kernel(SwaParams p) {
       L += wl[w][j] * c;
       O += wo[w][j][d] * c;
     }
-    const int qh = g * G + j;
-    const float gate = sigmoid(p.gate[(int64_t)b * p.ldg + qh]);
-    p.out[(int64_t)b * p.ldo + qh * hd + d] = (O / L) * gate;
+    out[(g * G + j) * hd + d] = (O / L) * sigmoid(gate[g * G + j]);
   }
 }
 
-bool swa_decode_supported(int Hq, int Hkv, int hd) {
+bool decode_attn_supported(int Hq, int Hkv, int hd) {
   const int G = Hkv > 0 ? Hq / Hkv : 0;
   return hd >= 8 && hd <= 256 && hd % 8 == 0 && 32 % (hd / 8) == 0 && G >= 1 && G <= kSdMaxG && G * Hkv == Hq;
 }
 
+// SWA, one token per sequence: the window's keys (positions, ring slots).
+__global__ void __launch_bounds__(kSdThreads) swa_decode_kernel(SwaParams p) {
+  const int g = blockIdx.x, b = blockIdx.y;
+  const int hd = p.hd, G = p.Hq / p.Hkv;
+  __shared__ float qs[kSdMaxG * 256];
+  const float* qrow = p.q + (int64_t)b * p.ldq;
+  for (int i = threadIdx.x; i < G * hd; i += kSdThreads) qs[i] = qrow[g * G * hd + i] * p.scale;
+  __syncthreads();
+  const int P0 = p.pos[b] + p.c0;
+  const int lo = max(0, P0 - p.window + 1), slots = p.slots;
+  decode_attend(qs, G, hd, g, p.Hkv, P0 - lo + 1, [&](int i) { return (lo + i) % slots; },
+                p.kring + (int64_t)b * p.seq_stride, p.vring + (int64_t)b * p.seq_stride,
+                p.gate + (int64_t)b * p.ldg, p.out + (int64_t)b * p.ldo);
+}
+
 int launch_swa_decode(const SwaParams& p, int batch, cudaStream_t st) {
-  if (!swa_decode_supported(p.Hq, p.Hkv, p.hd) || p.T != 1) return CB_ERR_SHAPE;
+  if (!decode_attn_supported(p.Hq, p.Hkv, p.hd) || p.T != 1) return CB_ERR_SHAPE;
   swa_decode_kernel<<<dim3(p.Hkv, batch), kSdThreads, 0, st>>>(p);
+  count_launch();
+  return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+}
+
+// Cross attention of one query row over its selected keys (or all keys at or
+// before its position when dense), q RMSNorm + RoPE and the head gate fused.
+__global__ void __launch_bounds__(kSdThreads) cross_decode_kernel(CrossParams p) {
+  const int g = blockIdx.x, r = blockIdx.y, tid = threadIdx.x;
+  const int hd = p.hd, G = p.Hq / p.Hkv, warp = tid >> 5, lane = tid & 31;
+  const int b = r / p.nq, j0 = r % p.nq;
+  const int position = p.pos[b] + p.c0 + p.t_off + j0;
+  __shared__ float qs[kSdMaxG * 256];
+  const float* row = p.proj + (int64_t)r * p.ldp;
+  for (int j = warp; j < G; j += kSdThreads / 32) {
+    const float* x = row + (g * G + j) * hd;
+    float ss = 0.0f;
+    for (int d = lane; d < hd; d += 32) ss += x[d] * x[d];
+    ss = warp_sum(ss);
+    const float rn = rsqrtf(ss / (float)hd + p.eps);
+    for (int jj = lane; jj < hd / 2; jj += 32) {
+      float x1 = x[2 * jj] * rn * p.q_norm[2 * jj];
+      float x2 = x[2 * jj + 1] * rn * p.q_norm[2 * jj + 1];
+      if (jj < p.rot2) rope_pair(x1, x2, position, p.inv_freq[jj]);
+      qs[j * hd + 2 * jj] = x1 * p.scale;
+      qs[j * hd + 2 * jj + 1] = x2 * p.scale;
+    }
+  }
+  __syncthreads();
+  const bool dense = p.sel_idx == nullptr;
+  const int n = dense ? max(0, min(position + 1, p.max_ctx)) : min(p.sel_cnt[r], p.sel_ld);
+  const int32_t* sel = dense ? nullptr : p.sel_idx + (int64_t)r * p.sel_ld;
+  decode_attend(qs, G, hd, g, p.Hkv, n, [&](int i) { return dense ? i : sel[i]; }, p.kk + (int64_t)b * p.seq_stride,
+                p.vv + (int64_t)b * p.seq_stride, row + p.off_gate, p.out + (int64_t)r * p.ldo);
+}
+
+int launch_cross_decode(const CrossParams& p, int rows, cudaStream_t st) {
+  if (!decode_attn_supported(p.Hq, p.Hkv, p.hd)) return CB_ERR_SHAPE;
+  cross_decode_kernel<<<dim3(p.Hkv, rows), kSdThreads, 0, st>>>(p);
   count_launch();
   return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
 }

@@ -102,9 +102,11 @@ int launch_swa(const SwaParams& p, int batch, cudaStream_t st);
 // Prompt chunks: block-wise SWA (rows b * T + t), gated output straight into out.
 int launch_swa_prefill(const SwaParams& p, int batch, cudaStream_t st);
 bool swa_prefill_supported(int Hq, int Hkv, int hd);
-// Decode steps (T = 1) of many sequences: one CTA per (KV head, sequence), lanes over keys.
+// Steps of many query rows: one CTA per (KV head, row), lane groups over keys
+// (SWA for one token per sequence, cross attention for any rows).
 int launch_swa_decode(const SwaParams& p, int batch, cudaStream_t st);
-bool swa_decode_supported(int Hq, int Hkv, int hd);
+int launch_cross_decode(const CrossParams& p, int rows, cudaStream_t st);
+bool decode_attn_supported(int Hq, int Hkv, int hd);
 int launch_cross(const CrossParams& p, int rows, cudaStream_t st);
 int launch_indexer_topk(const IndexerParams& p, cudaStream_t st);
 

@@ -65,7 +65,8 @@ static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 // Token rows from which a projection runs on the tensor cores (cb_gemm_nvfp4)
 // instead of the CUDA-core GEMV.
 constexpr int kGemmMinRows = 17;
-// Token rows (batch * tokens) from which SWA decode runs block-wise.
+// Query rows (batch * tokens) from which SWA and cross attention run on the
+// many-row kernels (lane groups over keys, block-wise SWA for several tokens).
 constexpr int kSwaBlockRows = 32;
 
 static int swa_splits(const CbModel& m) { return ceil_div(m.swa_window + CB_MAX_T, kSwaSplit); }
@@ -528,7 +529,7 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
         // split-window kernel, whose launch grows with the window
         const bool blockwise = swa_prefill_supported(m.n_q_heads, m.n_kv_heads, m.head_dim) &&
                                c.swa_slots >= m.swa_window + tc - 1 && (tc > CB_MAX_T || R >= kSwaBlockRows);
-        if (tc == 1 && R >= kSwaBlockRows && swa_decode_supported(m.n_q_heads, m.n_kv_heads, m.head_dim))
+        if (tc == 1 && R >= kSwaBlockRows && decode_attn_supported(m.n_q_heads, m.n_kv_heads, m.head_dim))
           CB_TRY(launch_swa_decode(sp, B, st));
         else if (blockwise)
           CB_TRY(launch_swa_prefill(sp, B, st));
@@ -635,7 +636,10 @@ extern "C" int cb_forward(const CbModel* mp, const CbCache* cp, void* workspace,
       cpp.max_ctx = c.max_ctx;
       cpp.out = w.attn;
       cpp.ldo = w.att_ld;
-      CB_TRY(launch_cross(cpp, RQ, st));
+      if (RQ >= kSwaBlockRows && decode_attn_supported(m.n_q_heads, m.n_kv_heads, m.head_dim))
+        CB_TRY(launch_cross_decode(cpp, RQ, st));
+      else
+        CB_TRY(launch_cross(cpp, RQ, st));
       CB_TRY(proj(w, L.o_proj, w.attn, w.att_ld, RQ, nullptr, 0.f, PRE_NONE, EPI_ADD, w.xc, d, d, st));
       CB_TRY(ffn(L.gate_up, L.down, L.norm2, m, w.xc, RQ, w, st));
     }
