@@ -2016,6 +2016,7 @@ int launch_mk(const MkArgs& a, cudaStream_t st) {
   if (M <= 1) fn = decode_mk_kernel<1>;
   else if (M <= 2) fn = decode_mk_kernel<2>;
   else if (M <= 4) fn = decode_mk_kernel<4>;
+  else if (M <= 5) fn = decode_mk_kernel<5>;  // a verify of 1 + 4 drafts: fewer live registers than <8>
   else fn = decode_mk_kernel<8>;
   if (ensure_smem_attr((const void*)fn, kSmem) != CB_OK) return CB_ERR_CUDA;
   const int ncl = std::min(resident_clusters((const void*)fn, kMkThreads, kSmem, kCl), kMkMaxClusters);
