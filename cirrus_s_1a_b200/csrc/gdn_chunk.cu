@@ -15,19 +15,25 @@
 //   S_C = e^{G_C} S0 + K^T diag(e^{G_C - G}) D,           Q~ = q * scale.
 // All exponents are <= 0 (g <= 0), so nothing overflows.
 //
-// One CTA per (sequence, head) walks the chunks in order with S in shared
-// memory; every 64 x 64 x 64 product is fp32, 4 x 4 outputs per thread.  The
-// triangular solve goes in 16-row blocks: a parallel update from the finished
-// blocks, then one thread per right-hand-side column inside the block.
+// The value columns of S, V, U, D and O never mix: a cluster of NS CTAs per
+// (sequence, head) splits them (4 when the grid is small, 1 with many
+// sequences), each CTA owning 64 / NS columns of the state in shared memory
+// and walking the chunks in order.  Every CTA also forms the
+// column-free parts (the normalised K and Q, the decays, A, P and W) itself.
+// The products are fp32 (4 x 4 or 4 x 1 outputs per thread); the triangular
+// solve goes in 16-row blocks: a parallel update from the finished blocks, then
+// one thread per right-hand-side column inside the block.  The gated RMSNorm of
+// an output row needs all 64 columns: the CTAs exchange their rows' sums of
+// squares through distributed shared memory.
 #include "common.cuh"
 #include "gdn.cuh"
 
 namespace cb {
 namespace {
 
-constexpr int kGc = 64;        // chunk length
-constexpr int kGd = 64;        // Dk = Dv
-constexpr int kGp = kGd + 1;   // padded row stride (floats)
+constexpr int kGc = 64;         // chunk length
+constexpr int kGd = 64;         // Dk = Dv
+constexpr int kGp = kGd + 1;    // padded row stride of 64-wide arrays (floats)
 constexpr int kGThreads = 256;
 
 // acc[r][c] += sum_{k < n} X[(r0 + r) * xr + k * xk] * Y[k * yk + (c0 + c) * yc]
@@ -47,38 +53,67 @@ __device__ __forceinline__ void mm44(const float* X, int xr, int xk, const float
   }
 }
 
+// acc[r][j] += sum_{k < n} X[(r0 + r) * xr + k * xk] * Y[k * yk + c0 + j]
+template <int CW>
+__device__ __forceinline__ void mm4c(const float* X, int xr, int xk, const float* Y, int yk, int n, int r0, int c0,
+                                     float (&acc)[4][CW]) {
+#pragma unroll 4
+  for (int k = 0; k < n; ++k) {
+    float a[4], bb[CW];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) a[r] = X[(r0 + r) * xr + k * xk];
+#pragma unroll
+    for (int j = 0; j < CW; ++j) bb[j] = Y[k * yk + c0 + j];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int j = 0; j < CW; ++j) acc[r][j] = fmaf(a[r], bb[j], acc[r][j]);
+  }
+}
+
+// NS CTAs per (sequence, head), each owning 64 / NS value columns.
+template <int NS>
 __global__ void __launch_bounds__(kGThreads, 1) gdn_chunk_kernel(const __grid_constant__ GdnChunkParams p) {
+  constexpr int kGns = NS;
+  constexpr int kGcw = kGd / NS;   // value columns of this CTA
+  constexpr int kGq = kGcw + 1;    // padded row stride of the column arrays
+  constexpr int CW = kGcw / 16;    // columns per thread in the 64 x kGcw products
   extern __shared__ __align__(16) float gsm[];
-  float* S = gsm;                   // [Dk][kGp]   state
-  float* Kc = S + kGd * kGp;        // [C][kGp]
+  float* Kc = gsm;                  // [C][kGp]
   float* Qc = Kc + kGc * kGp;       // [C][kGp]    q * scale
-  float* Vc = Qc + kGc * kGp;       // [C][kGp]
-  float* A = Vc + kGc * kGp;        // [C][kGp]    strictly lower e^{G_t-G_i} k_t.k_i
+  float* A = Qc + kGc * kGp;        // [C][kGp]    strictly lower e^{G_t-G_i} k_t.k_i
   float* P = A + kGc * kGp;         // [C][kGp]    lower-inclusive e^{G_t-G_i} q~_t.k_i
-  float* U = P + kGc * kGp;         // [C][kGp]    then D
-  float* W = U + kGc * kGp;         // [C][kGp]
+  float* W = P + kGc * kGp;         // [C][kGp]    solve of diag(beta e^G) K
+  float* S = W + kGc * kGp;         // [Dk][kGq]   this CTA's state columns
+  float* Vc = S + kGd * kGq;        // [C][kGq]
+  float* U = Vc + kGc * kGq;        // [C][kGq]    then D
+  float* X = U + kGc * kGq;         // [C][kGq]    D scaled for the state update; output rows
   __shared__ float Gs[kGc], bs[kGc];
+  __shared__ float ssq[2][NS][kGc];  // rows' partial sums of squares, from every rank (by chunk parity)
   const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15, r0 = 4 * ty, c0 = 4 * tx;
-  const int b = blockIdx.x / p.H, h = blockIdx.x - b * p.H, H = p.H;
+  const int cs = (int)(blockIdx.x % kGns), bh = (int)(blockIdx.x / kGns);
+  const int b = bh / p.H, h = bh - b * p.H, H = p.H, v0 = cs * kGcw;
   const bool model = p.a_raw != nullptr;
   float* Sg = p.state + (int64_t)b * p.state_seq + (int64_t)h * kGd * kGd;
-  for (int i = tid; i < kGd * kGd; i += kGThreads) S[(i / kGd) * kGp + (i % kGd)] = Sg[i];
+  for (int i = tid; i < kGd * kGcw; i += kGThreads) S[(i / kGcw) * kGq + (i % kGcw)] = Sg[(i / kGcw) * kGd + v0 + i % kGcw];
 
-  for (int t0 = 0; t0 < p.T; t0 += kGc) {
+  for (int t0 = 0, chunk = 0; t0 < p.T; t0 += kGc, ++chunk) {
     const int tc = min(kGc, p.T - t0);
     __syncthreads();  // S written by the previous chunk; chunk buffers free
     for (int i = tid; i < kGc * kGd; i += kGThreads) {
       const int t = i / kGd, d = i - t * kGd;
-      float kv = 0.0f, qv = 0.0f, vv = 0.0f;
+      float kv = 0.0f, qv = 0.0f;
       if (t < tc) {
         const int64_t off = ((int64_t)b * p.T + t0 + t) * p.ld_qkv + (int64_t)h * kGd + d;
         kv = p.k[off];
         qv = p.q[off];
-        vv = p.v[off];
       }
       Kc[t * kGp + d] = kv;
       Qc[t * kGp + d] = qv;
-      Vc[t * kGp + d] = vv;
+    }
+    for (int i = tid; i < kGc * kGcw; i += kGThreads) {
+      const int t = i / kGcw, d = i - t * kGcw;
+      Vc[t * kGq + d] = t < tc ? p.v[((int64_t)b * p.T + t0 + t) * p.ld_qkv + (int64_t)h * kGd + v0 + d] : 0.0f;
     }
     if (model) {
       // L2-normalise the chunk's q and k rows (x / max(||x||, 1e-12)); a warp per row
@@ -98,15 +133,15 @@ __global__ void __launch_bounds__(kGThreads, 1) gdn_chunk_kernel(const __grid_co
     if (tid < 32) {  // G = inclusive prefix sum of g (padded tokens: g = 0, beta = 0)
       float g0 = 0.0f, g1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
       if (model) {
-        const float A = -expf(p.A_log[h]), dtb = p.dt_bias[h];
-        const int64_t r0 = (int64_t)b * p.T + t0;
+        const float Ah = -expf(p.A_log[h]), dtb = p.dt_bias[h];
+        const int64_t rr = (int64_t)b * p.T + t0;
         if (tid < tc) {
-          g0 = A * softplus(p.a_raw[(r0 + tid) * p.ld_ab + h] + dtb);
-          b0 = sigmoid(p.b_raw[(r0 + tid) * p.ld_ab + h]);
+          g0 = Ah * softplus(p.a_raw[(rr + tid) * p.ld_ab + h] + dtb);
+          b0 = sigmoid(p.b_raw[(rr + tid) * p.ld_ab + h]);
         }
         if (tid + 32 < tc) {
-          g1 = A * softplus(p.a_raw[(r0 + tid + 32) * p.ld_ab + h] + dtb);
-          b1 = sigmoid(p.b_raw[(r0 + tid + 32) * p.ld_ab + h]);
+          g1 = Ah * softplus(p.a_raw[(rr + tid + 32) * p.ld_ab + h] + dtb);
+          b1 = sigmoid(p.b_raw[(rr + tid + 32) * p.ld_ab + h]);
         }
       } else {
         const int64_t o0 = ((int64_t)b * p.T + t0) * H + h;
@@ -146,112 +181,153 @@ __global__ void __launch_bounds__(kGThreads, 1) gdn_chunk_kernel(const __grid_co
         }
     }
     __syncthreads();
-    // forward substitution X_t = beta_t (R_t - sum_{i<t} A[t][i] X_i) for U (R = V) and
-    // W (R = e^G K), in 4 row blocks of 16: all threads subtract the finished
-    // blocks, then one thread per column finishes the block's rows in order
+    // forward substitution X_t = beta_t (R_t - sum_{i<t} A[t][i] X_i) for U (R = this
+    // CTA's V columns) and W (R = e^G K, all 64 columns), in 4 row blocks of 16:
+    // all threads subtract the finished blocks, then one thread per column finishes
+    // the block's rows in order
+    constexpr int kNcol = kGcw + kGd;
     for (int blk = 0; blk < kGc / 16; ++blk) {
       const int tb0 = 16 * blk;
-      for (int e = tid; e < 16 * 2 * kGd; e += kGThreads) {
-        const int t = tb0 + (e >> 7), col = e & 127, c = col & (kGd - 1);
-        const bool isu = col < kGd;
-        float* X = isu ? U : W;
-        float y = isu ? Vc[t * kGp + c] : expf(Gs[t]) * Kc[t * kGp + c];
-        for (int i = 0; i < tb0; ++i) y = fmaf(-A[t * kGp + i], X[i * kGp + c], y);
-        X[t * kGp + c] = y;
+      for (int e = tid; e < 16 * kNcol; e += kGThreads) {
+        const int t = tb0 + e / kNcol, col = e % kNcol;
+        const bool isu = col < kGcw;
+        const int c = isu ? col : col - kGcw;
+        float* Xs = isu ? U : W;
+        const int ld = isu ? kGq : kGp;
+        float y = isu ? Vc[t * kGq + c] : expf(Gs[t]) * Kc[t * kGp + c];
+        for (int i = 0; i < tb0; ++i) y = fmaf(-A[t * kGp + i], Xs[i * ld + c], y);
+        Xs[t * ld + c] = y;
       }
       __syncthreads();
-      if (tid < 2 * kGd) {
-        const int c = tid & (kGd - 1);
-        float* X = tid < kGd ? U : W;
+      if (tid < kNcol) {
+        const bool isu = tid < kGcw;
+        const int c = isu ? tid : tid - kGcw;
+        float* Xs = isu ? U : W;
+        const int ld = isu ? kGq : kGp;
         for (int t = tb0; t < tb0 + 16; ++t) {
-          float y = X[t * kGp + c];
-          for (int i = tb0; i < t; ++i) y = fmaf(-A[t * kGp + i], X[i * kGp + c], y);
-          X[t * kGp + c] = bs[t] * y;
+          float y = Xs[t * ld + c];
+          for (int i = tb0; i < t; ++i) y = fmaf(-A[t * kGp + i], Xs[i * ld + c], y);
+          Xs[t * ld + c] = bs[t] * y;
         }
       }
       __syncthreads();
     }
+    // thread (rows rr0 .. rr0 + 3, columns cc .. cc + CW - 1) of every 64 x kGcw product
+    const int rr0 = 4 * (tid >> 4), cc = CW * (tid & 15);
     // D = U - W S0 (into U), and O = diag(e^G) Q~ S0 + P D
-    float o[4][4] = {};
+    float o[4][CW] = {};
     {
-      float ws[4][4] = {};
-      mm44(W, kGp, 1, S, kGp, 1, kGd, r0, c0, ws);
-      mm44(Qc, kGp, 1, S, kGp, 1, kGd, r0, c0, o);
+      float ws[4][CW] = {};
+      mm4c<CW>(W, kGp, 1, S, kGq, kGd, rr0, cc, ws);
+      mm4c<CW>(Qc, kGp, 1, S, kGq, kGd, rr0, cc, o);
 #pragma unroll
       for (int r = 0; r < 4; ++r)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          U[(r0 + r) * kGp + c0 + c] -= ws[r][c];
-          o[r][c] *= expf(Gs[r0 + r]);
+        for (int j = 0; j < CW; ++j) {
+          U[(rr0 + r) * kGq + cc + j] -= ws[r][j];
+          o[r][j] *= expf(Gs[rr0 + r]);
         }
     }
     __syncthreads();
-    mm44(P, kGp, 1, U, kGp, 1, kGc, r0, c0, o);
+    mm4c<CW>(P, kGp, 1, U, kGq, kGc, rr0, cc, o);
     if (p.gate == nullptr) {
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        const int t = r0 + r;
-        if (t < tc) {
-          float* op = p.out + ((int64_t)b * p.T + t0 + t) * p.ld_out + (int64_t)h * kGd + c0;
+        const int t = rr0 + r;
+        if (t < tc)
 #pragma unroll
-          for (int c = 0; c < 4; ++c) op[c] = o[r][c];
-        }
+          for (int j = 0; j < CW; ++j)
+            p.out[((int64_t)b * p.T + t0 + t) * p.ld_out + (int64_t)h * kGd + v0 + cc + j] = o[r][j];
       }
     } else {
-      // gated RMSNorm of each output row: o rows through shared memory (A is free now)
+      // gated RMSNorm of each output row over all 64 columns: this CTA's rows through
+      // X, their sums of squares to every rank of the cluster
 #pragma unroll
       for (int r = 0; r < 4; ++r)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) A[(r0 + r) * kGp + c0 + c] = o[r][c];
+        for (int j = 0; j < CW; ++j) X[(rr0 + r) * kGq + cc + j] = o[r][j];
       __syncthreads();
-      const int warp = tid >> 5, lane = tid & 31;
-      for (int t = warp; t < tc; t += kGThreads / 32) {
-        const float* x = A + t * kGp;
-        const float a0 = x[lane], a1 = x[lane + 32];
-        const float rr = rsqrtf(warp_sum(a0 * a0 + a1 * a1) / (float)kGd + p.eps);
-        const int64_t row = (int64_t)b * p.T + t0 + t;
-        const float* gt = p.gate + row * p.ld_gate + (int64_t)h * kGd;
-        float* op = p.out + row * p.ld_out + (int64_t)h * kGd;
-        op[lane] = a0 * rr * p.o_norm[lane] * silu(gt[lane]);
-        op[lane + 32] = a1 * rr * p.o_norm[lane + 32] * silu(gt[lane + 32]);
+      const int par = chunk & 1;
+      if (tid < kGc) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int c = 0; c < kGcw; ++c) ss = fmaf(X[tid * kGq + c], X[tid * kGq + c], ss);
+        for (int q = 0; q < kGns; ++q) {
+          uint32_t ra;
+          asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                       : "=r"(ra)
+                       : "r"((uint32_t)__cvta_generic_to_shared(&ssq[par][cs][tid])), "r"(q));
+          asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(ss) : "memory");
+        }
       }
+      asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+      for (int i = tid; i < tc * kGcw; i += kGThreads) {
+        const int t = i / kGcw, c = i - t * kGcw;
+        float tot = 0.0f;
+        for (int q = 0; q < kGns; ++q) tot += ssq[par][q][t];
+        const float rr = rsqrtf(tot / (float)kGd + p.eps);
+        const int64_t row = (int64_t)b * p.T + t0 + t;
+        const float gt = p.gate[row * p.ld_gate + (int64_t)h * kGd + v0 + c];
+        p.out[row * p.ld_out + (int64_t)h * kGd + v0 + c] = X[t * kGq + c] * rr * p.o_norm[v0 + c] * silu(gt);
+      }
+      __syncthreads();  // X is rewritten below
     }
     // S = e^{G_C} S0 + K^T diag(e^{G_C - G}) D
     {
       const float gC = Gs[kGc - 1];
-      float sn[4][4] = {};
-      // scale D's rows in W (free now) so the product is a plain K^T X
-      for (int i = tid; i < kGc * kGd; i += kGThreads) {
-        const int t = i / kGd, d = i - t * kGd;
-        W[t * kGp + d] = expf(gC - Gs[t]) * U[t * kGp + d];
+      for (int i = tid; i < kGc * kGcw; i += kGThreads) {
+        const int t = i / kGcw, d = i - t * kGcw;
+        X[t * kGq + d] = expf(gC - Gs[t]) * U[t * kGq + d];
       }
       __syncthreads();
-      mm44(Kc, 1, kGp, W, kGp, 1, kGc, r0, c0, sn);
+      float sn[4][CW] = {};
+      mm4c<CW>(Kc, 1, kGp, X, kGq, kGc, rr0, cc, sn);
       __syncthreads();  // all reads of S0 finished
       const float eC = expf(gC);
 #pragma unroll
       for (int r = 0; r < 4; ++r)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float* sp = S + (r0 + r) * kGp + c0 + c;
-          *sp = fmaf(eC, *sp, sn[r][c]);
+        for (int j = 0; j < CW; ++j) {
+          float* sp = S + (rr0 + r) * kGq + cc + j;
+          *sp = fmaf(eC, *sp, sn[r][j]);
         }
     }
   }
   __syncthreads();
-  for (int i = tid; i < kGd * kGd; i += kGThreads) Sg[i] = S[(i / kGd) * kGp + (i % kGd)];
+  for (int i = tid; i < kGd * kGcw; i += kGThreads) Sg[(i / kGcw) * kGd + v0 + i % kGcw] = S[(i / kGcw) * kGq + (i % kGcw)];
 }
 
 }  // namespace
 
-size_t gdn_chunk_smem() { return sizeof(float) * (size_t)(kGd * kGp + 7 * kGc * kGp); }
+size_t gdn_chunk_smem(int ns) {
+  const size_t q = kGd / ns + 1;
+  return sizeof(float) * (size_t)(5 * kGc * kGp + kGd * q + 3 * kGc * q);
+}
 
 int launch_gdn_chunk(const GdnChunkParams& p, cudaStream_t st) {
   if (p.B < 1 || p.T < 1 || p.H < 1) return CB_ERR_ARG;
-  if (ensure_smem_attr((const void*)gdn_chunk_kernel, (int)gdn_chunk_smem()) != CB_OK) return CB_ERR_CUDA;
-  gdn_chunk_kernel<<<p.B * p.H, kGThreads, gdn_chunk_smem(), st>>>(p);
+  // split the value columns over 4 CTAs per head while that keeps the grid within
+  // about two waves; with many sequences one CTA per head does less redundant work
+  const int kGns = p.B * p.H * 4 <= 2 * num_sms() ? 4 : 1;
+  const void* fn = kGns == 4 ? (const void*)gdn_chunk_kernel<4> : (const void*)gdn_chunk_kernel<1>;
+  const size_t smem = gdn_chunk_smem(kGns);
+  if (ensure_smem_attr(fn, (int)smem) != CB_OK) return CB_ERR_CUDA;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(p.B * p.H * kGns);
+  cfg.blockDim = dim3(kGThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = kGns;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  void* args[] = {const_cast<GdnChunkParams*>(&p)};
+  const cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
   count_launch();
-  return cudaGetLastError() == cudaSuccess ? CB_OK : CB_ERR_CUDA;
+  return e == cudaSuccess ? CB_OK : CB_ERR_CUDA;
 }
 
 }  // namespace cb
