@@ -21,10 +21,12 @@ One JSON line on rank 0:
                is one whole step): the step's algorithmic bytes / its CUDA-event
                time vs the measured HBM copy bandwidth; ``traffic`` is the DRAM
                read + write of one launch from an ncu capture of this workload
-  weight_stream  the NVFP4 weight stream alone (every projection of a step,
-               M = 1, as separate GEMV launches in one CUDA graph)
+  weight_stream_kernel  the NVFP4 weight stream alone (every projection of a
+               step, M = 1) as one persistent launch (the reference's headline
+               microbenchmark, configs[1])
+  weight_stream  the same as separate GEMV launches in one CUDA graph
   weight_stream_by_M  the weight stream at M = 2 .. 64 token rows through the
-               tensor-core GEMM and the CUDA-core GEMV
+               tensor-core GEMM, the CUDA-core GEMV and (M <= 8) the stream kernel
   batched      step time of B sequences x T tokens (B = 8, 64; T = 1, 5); more
                than 16 token rows run on the tensor-core GEMM
   spec_decode  configs[4] on this GPU: 64 sequences at 32K, prompt-lookup drafts
@@ -202,6 +204,62 @@ def weight_stream_graph(eng, M: int = 1, tensor_cores: bool = False):
     real = sum(m.real_bytes for m in mats)
     g.keep = (x, y, scratch)  # buffers the captured launches use
     return g, len(structs), real
+
+
+def weight_stream_kernel_graph(eng, M: int = 1):
+    """CUDA graph of the one-launch weight stream (cb_weight_stream_nvfp4) over the
+    same projection matrices as ``weight_stream_graph``."""
+    import ctypes as C
+
+    import torch
+
+    from cirrus_s_1a_b200 import _lib
+    from cirrus_s_1a_b200.engine import PackedMatrix
+
+    L = _lib.lib()
+    mats = [m for m in eng.model._keep if isinstance(m, PackedMatrix)]
+    dev = eng.device
+    arr = (_lib.CbMatrix * len(mats))(*[m.struct() for m in mats])
+    plan = torch.empty(L.cb_stream_plan_bytes(len(mats)), dtype=torch.uint8, device=dev)
+    rows = C.c_int64(0)
+    _lib.check(L.cb_stream_plan(arr, len(mats), plan.data_ptr(), plan.numel(), C.byref(rows),
+                                torch.cuda.current_stream(dev).cuda_stream), "cb_stream_plan")
+    kmax = max(m.k for m in mats)
+    x = torch.randn(M, kmax, device=dev)
+    y = torch.empty(M, rows.value, device=dev)
+    side = torch.cuda.Stream(dev)
+
+    def run(st):
+        _lib.check(L.cb_weight_stream_nvfp4(plan.data_ptr(), len(mats), rows.value // 16, x.data_ptr(), kmax, kmax,
+                                            M, y.data_ptr(), rows.value, None, st), "cb_weight_stream_nvfp4")
+
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        run(side.cuda_stream)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            run(side.cuda_stream)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    g.keep = (plan, x, y)
+    return g, len(mats), sum(m.real_bytes for m in mats)
+
+
+def time_graph(g, flush, stream, warmup: int, iters: int) -> float:
+    """Mean CUDA-event time (ms) of a graph replay with L2 flushed before each."""
+    import torch
+
+    out = []
+    for i in range(warmup + iters):
+        flush.random_(0, 255)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        g.replay()
+        b.record(stream)
+        b.synchronize()
+        if i >= warmup:
+            out.append(a.elapsed_time(b))
+    return statistics.mean(out)
 
 
 def cpu_baseline(cfg, sd, cache, ctx: int, budget_s: float, max_steps: int) -> dict:
@@ -596,6 +654,9 @@ def main() -> None:
     e2e_total = sum(e2e_ms)
 
     # ------------------------------------------------ weight stream roofline
+    sgraph, _, _ = weight_stream_kernel_graph(eng, 1)
+    s_ms = time_graph(sgraph, flush, stream, args.warmup, args.steps)
+    del sgraph
     wgraph, n_mats, wbytes = weight_stream_graph(eng)
     w_ms = []
     for i in range(args.warmup + args.steps):
@@ -628,6 +689,12 @@ def main() -> None:
             row[kind] = {"us": us, "achieved_gbs": vbytes / (us * 1e-6) / 1e9,
                          "frac": vbytes / (us * 1e-6) / 1e9 / _peaks()["hbm_gbs"]}
             del vg
+        if M <= 8:
+            sg, _, sbytes = weight_stream_kernel_graph(eng, M)
+            us = time_graph(sg, flush, stream, args.warmup, max(args.steps // 5, 3)) * 1e3
+            row["stream_kernel"] = {"us": us, "achieved_gbs": sbytes / (us * 1e-6) / 1e9,
+                                    "frac": sbytes / (us * 1e-6) / 1e9 / _peaks()["hbm_gbs"]}
+            del sg
         verify[str(M)] = row
 
     # ------------------------------------------------ batched steps (B sequences x T tokens)
@@ -687,6 +754,10 @@ def main() -> None:
                      "traffic": traffic, "traffic_source": traffic_note, "bytes": step_total, "parts": sb,
                      "us": ms_step * 1e3,
                      "peak_source": peaks["source"]},
+        "weight_stream_kernel": {"bound": "hbm", "kernel": f"weight_stream_kernel<1> (one persistent launch over the "
+                                 f"{n_mats} projection matrices, M=1)", "us": s_ms * 1e3,
+                                 "achieved": wbytes / (s_ms * 1e-3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                 "frac": wbytes / (s_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], "bytes": wbytes},
         "weight_stream": {"bound": "hbm", "kernel": f"gemv_nvfp4 ({n_mats} launches, M=1, one CUDA graph)",
                           "achieved": wbytes / w_avg_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                           "frac": wbytes / w_avg_s / 1e9 / peaks["hbm_gbs"], "bytes": wbytes,

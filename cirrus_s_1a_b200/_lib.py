@@ -35,7 +35,8 @@ EXPORTS = ("cb_abi_version", "cb_status_string", "cb_nvfp4_quantize", "cb_nvfp4_
            "cb_read_status", "cb_clear_status", "cb_launch_count", "cb_indexer_topk_noalloc", "cb_read_trace",
            "cb_gdn_chunk_prefill", "cb_set_wait_limit",
            "cb_workspace_layout", "cb_nvfp4_slice_bytes", "cb_nvfp4_pack_slices", "cb_prompt_lookup_draft",
-           "cb_spec_accept", "cb_mtp_workspace_bytes", "cb_mtp_draft", "cb_gemm_nvfp4", "cb_gemm_scratch_bytes")
+           "cb_spec_accept", "cb_mtp_workspace_bytes", "cb_mtp_draft", "cb_gemm_nvfp4", "cb_gemm_scratch_bytes",
+           "cb_stream_plan_bytes", "cb_stream_plan", "cb_weight_stream_nvfp4")
 
 P = C.c_void_p
 I32 = C.c_int32
@@ -126,6 +127,10 @@ def lib() -> C.CDLL:
                                     C.c_size_t, P, P]
         L.cb_gemm_scratch_bytes.restype = C.c_size_t
         L.cb_gemm_scratch_bytes.argtypes = [I32, I32]
+        L.cb_stream_plan_bytes.restype = C.c_size_t
+        L.cb_stream_plan_bytes.argtypes = [I32]
+        L.cb_stream_plan.argtypes = [C.POINTER(CbMatrix), I32, P, C.c_size_t, C.POINTER(C.c_int64), P]
+        L.cb_weight_stream_nvfp4.argtypes = [P, I32, I32, P, I32, I32, I32, P, C.c_int64, P, P]
         L.cb_gdn_chunk_prefill.argtypes = [P, P, P, P, P, I32, I32, I32, I32, I32, C.c_float, P, P, P]
         L.cb_embed.argtypes = [C.POINTER(CbMatrix), P, I32, P, P, P]
         L.cb_argmax.argtypes = [P, I32, I32, I32, P, P]
@@ -149,7 +154,7 @@ def lib() -> C.CDLL:
         L.cb_launch_count.argtypes = []
         for name in EXPORTS:
             if name not in ("cb_status_string", "cb_workspace_bytes", "cb_launch_count", "cb_nvfp4_slice_bytes",
-                            "cb_mtp_workspace_bytes", "cb_gemm_scratch_bytes"):
+                            "cb_mtp_workspace_bytes", "cb_gemm_scratch_bytes", "cb_stream_plan_bytes"):
                 getattr(L, name).restype = C.c_int
         if L.cb_abi_version() != 3:
             raise CbError("libcirrus_b200.so ABI version mismatch")

@@ -222,6 +222,24 @@ int cb_gemm_nvfp4(const CbMatrix* w, const float* x, int32_t ldx, int32_t m_rows
                   float eps, float* y, int32_t ldy, int32_t rows_out, int32_t epi, void* scratch,
                   size_t scratch_bytes, int32_t* status, void* stream);
 
+/* The NVFP4 weight stream of a step as one persistent launch: for every matrix
+ * of a list (independent projections sharing one input, as in the reference's
+ * decode-step weight stream) y[m, row_off(i) + r] = x[m, :k_i] . dequant(W_i)[r, :]
+ * for m < m_rows <= 8.  cb_stream_plan writes the list (k a multiple of 256, at
+ * most 2048; at most 128 matrices) into a caller-allocated device buffer of
+ * cb_stream_plan_bytes(n_mats) bytes and returns the total rows (matrix i's rows
+ * start where matrix i-1's end); it synchronises the stream.  x float32
+ * [m_rows][ldx] with kmax <= ldx (every matrix reads x[:, :k_i]), y float32
+ * [m_rows][ldy], ldy >= total rows.  status (device int32, may be null) receives
+ * CB_ERR_TIMEOUT if a bounded wait gives up.
+ * Replaces the reference's persistent weight-stream kernels decode_stream_v4/v5
+ * (cirrus/perf/bench_kernels.cu:1079-1300, scripts/bench_spark.py:885-930). */
+size_t cb_stream_plan_bytes(int32_t n_mats);
+int cb_stream_plan(const CbMatrix* mats, int32_t n_mats, void* plan, size_t plan_bytes, int64_t* rows_total,
+                   void* stream);
+int cb_weight_stream_nvfp4(const void* plan, int32_t n_mats, int32_t total_tiles, const float* x, int32_t ldx,
+                           int32_t kmax, int32_t m_rows, float* y, int64_t ldy, int32_t* status, void* stream);
+
 /* h[r, :] = dequant(lm_head row ids[r]) for r < n_rows (float32 [n_rows, d]). */
 int cb_embed(const CbMatrix* table, const int64_t* ids, int32_t n_rows, float* h, int32_t* status, void* stream);
 
