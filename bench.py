@@ -491,10 +491,9 @@ def trace_step(B: int, T: int) -> None:
     eng = CirrusB200(cfg, synthetic.random_state_dict(cfg, seed=0), device="cuda:0", max_ctx=CTX + 64)
     names = []
     for kind in cfg.self_layer_kinds:
-        names += ["gdn"] if kind == "gdn" else ["swa_in", "swa_attention", "swa_o"]
-        names.append("ffn_self")
-    names += ["shared_proj", "append_scores", "compaction"] + ["cross_q", "cross_attention", "cross_o",
-                                                               "ffn_cross"] * cfg.n_cross_layers + ["lm_head"]
+        names += ["gdn" if kind == "gdn" else "swa_head", "ffn_self"]
+    names += ["shared_proj", "append_scores", "compaction", "resolve"]
+    names += ["cross_head", "ffn_cross"] * cfg.n_cross_layers + ["lm_head"]
     cache = eng.new_cache(B)
     synthetic.fill_cache(cache, CTX - 8, seed=1)
     g = DecodeGraph(eng, cache, T=T, n_logits=T, want_logits=False)
@@ -517,8 +516,9 @@ def trace_step(B: int, T: int) -> None:
     agg = {}
     for p, name in enumerate(names):  # barrier 1 ends the set-up; phase p ends at barrier p + 2
         start, arrive, leave = v[2 * (p + 1)], v[2 * (p + 2) - 1], v[2 * (p + 2)]
-        marks = [(v[256 + 4 * p + i] - start) / 1e3 for i in range(4) if start <= v[256 + 4 * p + i] <= arrive]
-        e = agg.setdefault(name, {"count": 0, "work_us": 0.0, "wait_us": 0.0, "marks_us": [0.0] * 4})
+        marks = [(v[256 + 6 * p + i] - start) / 1e3 if start <= v[256 + 6 * p + i] <= arrive else 0.0
+                 for i in range(6)]
+        e = agg.setdefault(name, {"count": 0, "work_us": 0.0, "wait_us": 0.0, "marks_us": [0.0] * 6})
         e["count"] += 1
         e["work_us"] += (arrive - start) / 1e3
         e["wait_us"] += (leave - arrive) / 1e3

@@ -15,12 +15,19 @@
 //                        (its gate and up tiles, SwiGLU, the matching 16 columns
 //                        of the down projection) -> partials summed in the cluster
 //                        -> added to the residual stream
-//   SWA layer:  in-projection GEMV -> split attention over the window ring ->
-//               o-projection (merging the split partials) -> FFN
+//   SWA layer:  [mixer]  one cluster per query head: the head's q, k, v and gate
+//                        rows -> distributed shared memory -> q / k RMSNorm +
+//                        RoPE (ring append) -> each CTA attends over an eighth of
+//                        the window -> partials merged in the cluster -> the
+//                        head's column block of the o-projection on the CTA's
+//                        d/8 output rows -> added to the residual stream
+//               [FFN]
 //   shared KV:  projection GEMV -> K/V/indexer-key append + indexer scores with a
-//               2048-bin histogram -> threshold bin + compaction -> exact
-//               selection (one CTA per query row, beside the first q GEMV)
-//   cross layer: q|gate GEMV -> selected-key attention -> o-projection -> FFN
+//               2048-bin histogram (and the cross residual stream initialised)
+//               -> threshold bin + compaction -> exact selection (one CTA per
+//               query row)
+//   cross layer: [mixer] as the SWA mixer, q and gate rows only, over the
+//               selected keys of the shared cache -> [FFN]
 //   head:       LM-head GEMV (final norm fused) with a per-row argmax
 //
 // The residual streams are kept in 64-bit fixed point (value * 2^32) and every
@@ -59,7 +66,7 @@ constexpr int kParSmall = kMkMaxD;               // [64] scales and constants
 constexpr int kParConv = kMkMaxD + 80;           // conv taps [NC][4], then windows [B][3][NC]
 constexpr int kParTs = 48;                       // tile scales held for the first 48 units of a GEMV
 enum { PS_A_LOG = 48, PS_DT_BIAS = 49, PS_TSCALE = 50, PS_O_NORM = 52 };  // indices in the small block (80)
-constexpr int kMarkBase = 256;                   // trace entries kMarkBase + 4 p + i: sub-phase marks of CTA 0
+constexpr int kMarkBase = 256;                   // trace entries kMarkBase + 6 p + i: sub-phase marks of CTA 0
 constexpr int kSmem = 2 * kSlot + kWork;
 constexpr int kMaxSort = 4096;
 constexpr int kMkBitmapWords = 4096;  // selection bitmap: up to 131072 keys
@@ -68,11 +75,11 @@ constexpr unsigned kAbortBit = 1u << 30;
 constexpr float kFix = 4294967296.0f;              // 2^32
 constexpr float kFixInv = 2.3283064365386963e-10f;  // 2^-32
 
-enum { PRE_NONE_ = 0, PRE_RMS_ = 1, PRE_EMBED_ = 2, PRE_COMBINE_ = 3 };
+enum { PRE_NONE_ = 0, PRE_RMS_ = 1, PRE_EMBED_ = 2 };
 enum { EPI_STORE_ = 0, EPI_RED_ = 1 };
 enum : int {
-  PH_GDN = 0, PH_FFN_SELF, PH_SWA_IN, PH_SWA_ATT, PH_SWA_O, PH_SH_PROJ, PH_SH_SCORE, PH_SH_COMPACT, PH_CR_Q,
-  PH_CR_ATT, PH_CR_O, PH_FFN_CROSS, PH_LM_HEAD
+  PH_GDN = 0, PH_FFN_SELF, PH_SWA_HEAD, PH_SH_PROJ, PH_SH_SCORE, PH_SH_COMPACT, PH_CR_RESOLVE, PH_CR_HEAD,
+  PH_FFN_CROSS, PH_LM_HEAD
 };
 
 // ------------------------------------------------------------------ timers, sync
@@ -94,7 +101,7 @@ __shared__ unsigned s_stall_barrier;
 
 __shared__ int s_mark_base;  // trace entry of this phase's first sub-phase mark
 
-// %globaltimer at a point inside the current phase (CTA 0 only; i < 4).
+// %globaltimer at a point inside the current phase (CTA 0 only; i < 6).
 __device__ __forceinline__ void mark(const MkArgs& a, int i) {
   if (blockIdx.x == 0 && threadIdx.x == 0 && s_mark_base + i < kMkTrace) a.trace[s_mark_base + i] = gtimer();
 }
@@ -385,21 +392,12 @@ struct GemvJob {
   const long long* xq;  // fixed-point input rows (or null)
   const float* x;       // float input rows (when xq is null)
   int ldx;
-  int xmap_nq, xmap_T, xmap_off;  // input row of m = (m / nq) * T + off + m % nq when xmap_nq > 0
   int pre;
   const float* norm_w;
   float* y;             // EPI_STORE_
   long long* yq;        // EPI_RED_: y is added to this fixed-point stream
   int ldy, rows_out, epi;
-  long long* copy_q;    // the first CTA of the phase copies the (mapped) fixed-point input rows here
   bool argmax;
-  // PRE_COMBINE_: the input is the gated merge of split-softmax attention
-  // partials, part[((m * H + h) * S + s) * (hd + 2)] = (max, sum, o[hd]), with
-  // the output gate sigmoid(gate_x[m * gate_ld + gate_off + h])
-  const float* part;
-  int S, hd;
-  const float* gate_x;
-  int gate_ld, gate_off;
   int ucta, uncta;      // this CTA's index among the phase's CTAs and their count (units ucta + i * uncta)
 };
 
@@ -411,12 +409,18 @@ __device__ __forceinline__ int gemv_mine(const GemvJob& g) {
 __device__ __forceinline__ int gemv_staged(const GemvJob& g) {
   return min(gemv_mine(g), (int)(kSlot / tile_bytes(g.W.k)));
 }
+// Tiles after the staged ones that the last phase copies into the other slot
+// (free once the phase before it is done).
+__device__ __forceinline__ int gemv_extra(const GemvJob& g) {
+  return max(0, min(gemv_mine(g) - gemv_staged(g), (int)(kSlot / tile_bytes(g.W.k))));
+}
 
 __device__ __forceinline__ float* par_norm(float* work) { return work + kPreOff / 4 + kParNorm; }
 __device__ __forceinline__ float* par_small(float* work) { return work + kPreOff / 4 + kParSmall; }
 
 template <int M>
-__device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, const uint8_t* slot, float* work) {
+__device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, const uint8_t* slot, const uint8_t* slot2,
+                           int nst2, float* work) {
   const int n_mine = gemv_mine(g);
   if (n_mine == 0) return;
   const float* ps = par_small(work);
@@ -427,54 +431,13 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, const 
   __shared__ unsigned long long s_best[kMkMaxRows];
   __shared__ int s_rowmap[kMkMaxRows];
   if (g.argmax && tid < kMkMaxRows) s_best[tid] = 0ull;
-  if (tid < kMkMaxRows)
-    s_rowmap[tid] = g.xmap_nq > 0 ? (tid / g.xmap_nq) * g.xmap_T + g.xmap_off + tid % g.xmap_nq : tid;
+  if (tid < kMkMaxRows) s_rowmap[tid] = tid;
   __syncthreads();
   float rn[M];
-  if (g.pre == PRE_COMBINE_) {
-    // Merge the S <= 32 split partials of every (row, head): a warp per pair,
-    // a lane per split: w_s = exp(m_s - max m), coef_s = w_s * gate / sum_s w_s l_s;
-    // then x = sum_s coef_s o_s with the loads of 8 splits in flight at a time.
-    const int hd = g.hd, H = K / hd, S = g.S, per = hd + 2;
-    float* coef = work + M * K;  // [M][H][32]
-    for (int i = warp; i < m_rows * H; i += kW) {
-      const int mr = i / H, h = i - mr * H;
-      const float* pb = g.part + (int64_t)i * S * per + lane * per;
-      const float ms = lane < S ? __ldcg(pb) : -INFINITY;
-      const float ls = lane < S ? __ldcg(pb + 1) : 0.0f;
-      const float gt = __ldcg(g.gate_x + (int64_t)mr * g.gate_ld + g.gate_off + h);
-      const float mx = warp_max(ms);
-      const float w = ms == -INFINITY ? 0.0f : expf(ms - mx);
-      const float L = warp_sum(w * ls);
-      coef[i * 32 + lane] = w * (sigmoid(gt) / L);
-    }
-    __syncthreads();
-    for (int i = tid; i < M * K; i += kT) {
-      const int mr = i / K, k = i - mr * K;
-      float v = 0.0f;
-      if (mr < m_rows) {
-        const int h = k / hd, dd = k - h * hd;
-        const float* pb = g.part + (int64_t)(mr * H + h) * S * per + 2 + dd;
-        const float* cf = coef + (mr * H + h) * 32;
-        for (int s0 = 0; s0 < S; s0 += 8) {
-          float o[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) o[e] = s0 + e < S ? __ldcg(pb + (s0 + e) * per) : 0.0f;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) v = fmaf(cf[s0 + e], o[e], v);
-        }
-      }
-      xs[i] = v;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int m = 0; m < M; ++m) rn[m] = 1.0f;
-  } else {
-    const bool first = g.ucta == 0;
-    stage_rows<M>(g.xq, g.x, g.ldx, s_rowmap, m_rows, K, g.pre == PRE_NONE_ ? nullptr : par_norm(work), a.m.norm_eps,
-                  xs, rn, first ? g.copy_q : nullptr, (g.pre == PRE_EMBED_ && first) ? a.hq : nullptr,
-                  g.pre == PRE_EMBED_ ? &a : nullptr);
-  }
+  const bool first = g.ucta == 0;
+  stage_rows<M>(g.xq, g.x, g.ldx, s_rowmap, m_rows, K, g.pre == PRE_NONE_ ? nullptr : par_norm(work), a.m.norm_eps,
+                xs, rn, nullptr, (g.pre == PRE_EMBED_ && first) ? a.hq : nullptr,
+                g.pre == PRE_EMBED_ ? &a : nullptr);
   mark(a, 0);
 
   unsigned long long best[M];
@@ -484,9 +447,10 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, const 
     const int ua = g.ucta + i * g.uncta, ub = ua + g.uncta;
     const bool hb = i + 1 < n_mine;
     const int ra = ua * kTileRows + warp, rb = ub * kTileRows + warp;
-    const bool ga = i >= nst, gb = i + 1 >= nst;
-    const uint8_t* ta = ga ? g.W.tiles + ua * tb : slot + i * tb;
-    const uint8_t* tbb = gb ? g.W.tiles + ub * tb : slot + (i + 1) * tb;
+    // tile i: the phase's slot, then the second slot, then global memory
+    const bool ga = i >= nst + nst2, gb = i + 1 >= nst + nst2;
+    const uint8_t* ta = ga ? g.W.tiles + ua * tb : (i < nst ? slot + i * tb : slot2 + (i - nst) * tb);
+    const uint8_t* tbb = gb ? g.W.tiles + ub * tb : (i + 1 < nst ? slot + (i + 1) * tb : slot2 + (i + 1 - nst) * tb);
     float aa[M], ab[M];
     row_dot<M>(ta, K, warp, true, ga, xs, aa);
     if (hb) row_dot<M>(tbb, K, warp, true, gb, xs, ab);
@@ -579,7 +543,7 @@ __device__ __forceinline__ int gdn_channel(const GdnGeo& g, int h, int c) {
 struct GdnSmem {
   float *hp, *ssq, *red, *xs, *qk, *vv, *og, *rs, *pv, *gb, *pconv_w, *pconv_s;
 };
-__device__ __forceinline__ int pad4(int n) { return (n + 3) & ~3; }  // floats to a 16-byte multiple
+__host__ __device__ inline int pad4(int n) { return (n + 3) & ~3; }  // floats to a 16-byte multiple
 
 template <int M>
 __device__ __forceinline__ GdnSmem gdn_smem(float* work, const GdnGeo& g) {
@@ -1054,249 +1018,6 @@ __device__ void norm_rope_warp(const float* x, const float* w, int hd, int rot2,
   }
 }
 
-// ------------------------------------------- attention helpers (split softmax)
-// Scores of nq queries (Qs [nq][hd]) against n keys (Ks [n][hd+1]) into Sc [nq][ldsc],
-// masked entries -inf; then per query max / exp / sum (qm, ql) and o += e V into oacc.
-__device__ void attend_chunk(const float* Qs, const float* Ks, const float* Vs, float* Sc, int ldsc, int nq, int n,
-                             int hd, float scale, float* qm, float* ql, float* corr, float* oacc,
-                             const int* key_pos, const int* q_pos, int window) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int i = tid; i < nq * n; i += kT) {
-    const int q = i / n, key = i - q * n;
-    bool ok = true;
-    if (window > 0) {
-      const int kp = key_pos[key], pt = q_pos[q];
-      ok = kp <= pt && kp > pt - window;
-    }
-    float sc = -INFINITY;
-    if (ok) {  // four independent chains over d (hd % 8 == 0), summed in a fixed order
-      const float* qq = Qs + q * hd;
-      const float* kk = Ks + key * (hd + 1);
-      float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-#pragma unroll 2
-      for (int dd = 0; dd < hd; dd += 4) {
-        a0 = fmaf(qq[dd], kk[dd], a0);
-        a1 = fmaf(qq[dd + 1], kk[dd + 1], a1);
-        a2 = fmaf(qq[dd + 2], kk[dd + 2], a2);
-        a3 = fmaf(qq[dd + 3], kk[dd + 3], a3);
-      }
-      sc = ((a0 + a1) + (a2 + a3)) * scale;
-    }
-    Sc[q * ldsc + key] = sc;
-  }
-  __syncthreads();
-  for (int q = warp; q < nq; q += kW) {
-    float mx = -INFINITY;
-    for (int key = lane; key < n; key += 32) mx = fmaxf(mx, Sc[q * ldsc + key]);
-    mx = warp_max(mx);
-    const float mnew = fmaxf(qm[q], mx);
-    float l = 0.0f;
-    for (int key = lane; key < n; key += 32) {
-      const float sc = Sc[q * ldsc + key];
-      const float e = sc == -INFINITY ? 0.0f : expf(sc - mnew);
-      Sc[q * ldsc + key] = e;
-      l += e;
-    }
-    l = warp_sum(l);
-    if (lane == 0) {
-      const float cr = qm[q] == -INFINITY ? 0.0f : expf(qm[q] - mnew);
-      corr[q] = cr;
-      ql[q] = ql[q] * cr + l;
-      qm[q] = mnew;
-    }
-  }
-  __syncthreads();
-  for (int i = tid; i < nq * hd; i += kT) {
-    const int q = i / hd, dd = i - q * hd;
-    const float* e = Sc + q * ldsc;
-    float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;  // keys mod 4, summed in a fixed order
-    int key = 0;
-#pragma unroll 2
-    for (; key + 4 <= n; key += 4) {
-      o0 = fmaf(e[key], Vs[key * hd + dd], o0);
-      o1 = fmaf(e[key + 1], Vs[(key + 1) * hd + dd], o1);
-      o2 = fmaf(e[key + 2], Vs[(key + 2) * hd + dd], o2);
-      o3 = fmaf(e[key + 3], Vs[(key + 3) * hd + dd], o3);
-    }
-    for (; key < n; ++key) o0 = fmaf(e[key], Vs[key * hd + dd], o0);
-    oacc[i] = fmaf(oacc[i], corr[q], (o0 + o1) + (o2 + o3));
-  }
-  __syncthreads();
-}
-
-// ------------------------------------------------------------------- SWA
-__device__ void swa_item(const MkArgs& a, const CbSelfLayer& L, int b, int g, int s, float* smem) {
-  const CbModel& m = a.m;
-  const CbCache& c = a.c;
-  const int hd = m.head_dim, Hq = m.n_q_heads, Hkv = m.n_kv_heads, G = Hq / Hkv, T = a.T;
-  const int W = m.swa_window, Ls = kMkSwaSplit, S = a.swa_splits, nqry = G * T;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int p0 = c.pos[b] + a.c0;
-  const int lo = max(0, p0 - W + 1), last = p0 + T - 1;
-  const int ks = lo + s * Ls, ke = min(ks + Ls, last + 1), n = max(0, ke - ks);
-  float* Ks = smem;                    // [Ls][hd + 1]
-  float* Vs = Ks + Ls * (hd + 1);      // [Ls][hd]
-  float* Qs = Vs + Ls * hd;            // [kMkMaxQ][hd]
-  float* Sc = Qs + kMkMaxQ * hd;       // [kMkMaxQ][Ls]
-  float* oacc = Sc + kMkMaxQ * Ls;     // [kMkMaxQ][hd]
-  __shared__ float qm[kMkMaxQ], ql[kMkMaxQ], corr[kMkMaxQ];
-  __shared__ int kpos[kMkSwaSplit], qpos[kMkMaxQ];
-  const int64_t ring = (int64_t)(b * c.n_swa + L.slot) * c.swa_slots * Hkv * hd;
-  uint16_t* kr = c.swa_k + ring;
-  uint16_t* vr = c.swa_v + ring;
-
-  uint16_t* raw = reinterpret_cast<uint16_t*>(oacc + kMkMaxQ * hd);  // [2][Ls][hd] bf16 ring rows
-  const int vpk = hd / 8;  // 16-byte vectors per key row
-  // the window's ring rows do not depend on this step: start their copies first
-  for (int i = tid; i < n * vpk; i += kT) {
-    const int key = i / vpk, e8 = (i - key * vpk) * 8, kp = ks + key;
-    if (kp < p0) {
-      const int64_t off = ((int64_t)(kp % c.swa_slots) * Hkv + g) * hd + e8;
-      cp_async16(raw + key * hd + e8, kr + off);
-      cp_async16(raw + (Ls + key) * hd + e8, vr + off);
-    }
-  }
-  for (int q = warp; q < nqry; q += kW) {
-    const int t = q / G, j = q - t * G;
-    norm_rope_warp(a.proj + ((int64_t)b * T + t) * a.ldp + (g * G + j) * hd, L.q_norm, hd, m.rot_dim / 2, p0 + t,
-                   m.inv_freq, m.norm_eps, Qs + q * hd, false, nullptr);
-  }
-  // keys of this chunk's own tokens come from the projection (and are appended
-  // to the ring here), on the warps after the query ones
-  const int new0 = max(ks, p0), wk = (warp + kW - nqry % kW) % kW;
-  for (int kp = new0 + wk; kp < ke; kp += kW) {
-    const int idx = kp - ks, t2 = kp - p0;
-    const float* row = a.proj + ((int64_t)b * T + t2) * a.ldp;
-    const int64_t off = ((int64_t)(kp % c.swa_slots) * Hkv + g) * hd;
-    norm_rope_warp(row + m.swa_off_kv + g * hd, L.k_norm, hd, m.rot_dim / 2, kp, m.inv_freq, m.norm_eps,
-                   Ks + idx * (hd + 1), true, kr + off);
-    const int lane = tid & 31;
-    for (int dd = lane; dd < hd; dd += 32) {
-      const uint16_t bits = f32_to_bf16(__ldcg(row + m.swa_off_kv + Hkv * hd + g * hd + dd));
-      vr[off + dd] = bits;
-      Vs[idx * hd + dd] = bf16_to_f32(bits);
-    }
-  }
-  cp_async_wait_all();
-  __syncthreads();
-#pragma unroll 2
-  for (int i = tid; i < n * vpk; i += kT) {
-    const int key = i / vpk, e8 = (i - key * vpk) * 8, kp = ks + key;
-    if (kp < p0) {
-      const uint4 kq = *reinterpret_cast<const uint4*>(raw + key * hd + e8);
-      const uint4 vq = *reinterpret_cast<const uint4*>(raw + (Ls + key) * hd + e8);
-      const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w}, vw[4] = {vq.x, vq.y, vq.z, vq.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        Ks[key * (hd + 1) + e8 + 2 * e] = bf16_to_f32(kw[e]);
-        Ks[key * (hd + 1) + e8 + 2 * e + 1] = bf16_to_f32(kw[e] >> 16);
-        Vs[key * hd + e8 + 2 * e] = bf16_to_f32(vw[e]);
-        Vs[key * hd + e8 + 2 * e + 1] = bf16_to_f32(vw[e] >> 16);
-      }
-    }
-  }
-  for (int i = tid; i < n; i += kT) kpos[i] = ks + i;
-  for (int i = tid; i < nqry; i += kT) {
-    qpos[i] = p0 + i / G;
-    qm[i] = -INFINITY;
-    ql[i] = 0.0f;
-  }
-  for (int i = tid; i < nqry * hd; i += kT) oacc[i] = 0.0f;
-  __syncthreads();
-  if (n > 0) attend_chunk(Qs, Ks, Vs, Sc, Ls, nqry, n, hd, rsqrtf((float)hd), qm, ql, corr, oacc, kpos, qpos, W);
-  for (int i = tid; i < nqry * (hd + 2); i += kT) {
-    const int q = i / (hd + 2), e = i - q * (hd + 2);
-    const int t = q / G, j = q - t * G;
-    float* pp = a.part + ((((int64_t)b * T + t) * Hq + g * G + j) * S + s) * (hd + 2);
-    pp[e] = e == 0 ? qm[q] : (e == 1 ? ql[q] : oacc[q * hd + e - 2]);
-  }
-  __syncthreads();
-  // the o projection merges the partials (PRE_COMBINE)
-}
-
-__device__ void swa_phase(const MkArgs& a, const CbSelfLayer& L, float* smem) {
-  const int Hkv = a.m.n_kv_heads, S = a.swa_splits;
-  for (int it = blockIdx.x; it < a.B * Hkv * S; it += gridDim.x) {
-    const int s = it % S, g = (it / S) % Hkv, b = it / (S * Hkv);
-    swa_item(a, L, b, g, s, smem);
-  }
-}
-
-// -------------------------------------------------------- cross attention
-__device__ void cross_item(const MkArgs& a, const CbCrossLayer& L, int r, int g, int s, float* smem) {
-  const CbModel& m = a.m;
-  const CbCache& c = a.c;
-  const int hd = m.head_dim, Hq = m.n_q_heads, Hkv = m.n_kv_heads, G = Hq / Hkv, S = a.cross_splits;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int b = r / a.nq, jr = r - b * a.nq;
-  const int position = c.pos[b] + a.c0 + (a.T - a.nq) + jr;
-  const bool dense = m.sparse_topk == 0;
-  const int n_all = dense ? max(0, min(position + 1, c.max_ctx)) : min(__ldcg(a.sel_cnt + r), a.sel_ld);
-  const int per = dense ? ceil_div(n_all, S) : kMkCrossSplit;
-  const int ks = s * per, ke = min(ks + per, n_all);
-  const int Lc = kMkSwaSplit;  // keys per sub-chunk
-  float* Ks = smem;                 // [Lc][hd + 1]
-  float* Vs = Ks + Lc * (hd + 1);   // [Lc][hd]
-  float* Qs = Vs + Lc * hd;         // [G][hd]
-  float* Sc = Qs + kMkMaxQ * hd;    // [G][Lc]
-  float* oacc = Sc + kMkMaxQ * Lc;  // [G][hd]
-  __shared__ float qm[kMkMaxQ], ql[kMkMaxQ], corr[kMkMaxQ];
-  __shared__ int kid[kMkSwaSplit];
-  const float* row = a.cproj + (int64_t)r * a.cr_ld;
-  for (int j = warp; j < G; j += kW)
-    norm_rope_warp(row + (g * G + j) * hd, L.q_norm, hd, m.rot_dim / 2, position, m.inv_freq, m.norm_eps, Qs + j * hd,
-                   false, nullptr);
-  for (int i = tid; i < G; i += kT) {
-    qm[i] = -INFINITY;
-    ql[i] = 0.0f;
-  }
-  for (int i = tid; i < G * hd; i += kT) oacc[i] = 0.0f;
-  const uint16_t* kb = c.kv_k + (int64_t)b * c.max_ctx * Hkv * hd;
-  const uint16_t* vb = c.kv_v + (int64_t)b * c.max_ctx * Hkv * hd;
-  for (int c0 = ks; c0 < ke; c0 += Lc) {
-    const int cn = min(Lc, ke - c0);
-    // (the previous chunk's attend_chunk ended with a barrier; kid is free)
-    // on the warps after the query ones, so the first chunk's ids load beside the q RoPE
-    for (int i = (tid + kT - 32 * (G % kW)) % kT; i < cn; i += kT)
-      kid[i] = dense ? c0 + i : __ldcg(a.sel_idx + (int64_t)r * a.sel_ld + c0 + i);
-    __syncthreads();
-    const int vpk = hd / 8;
-#pragma unroll 4
-    for (int i = tid; i < cn * vpk; i += kT) {
-      const int key = i / vpk, e8 = (i - key * vpk) * 8;
-      const int64_t off = ((int64_t)kid[key] * Hkv + g) * hd + e8;
-      const uint4 kq = __ldcg(reinterpret_cast<const uint4*>(kb + off));
-      const uint4 vq = __ldcg(reinterpret_cast<const uint4*>(vb + off));
-      const uint32_t kw[4] = {kq.x, kq.y, kq.z, kq.w}, vw[4] = {vq.x, vq.y, vq.z, vq.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        Ks[key * (hd + 1) + e8 + 2 * e] = bf16_to_f32(kw[e]);
-        Ks[key * (hd + 1) + e8 + 2 * e + 1] = bf16_to_f32(kw[e] >> 16);
-        Vs[key * hd + e8 + 2 * e] = bf16_to_f32(vw[e]);
-        Vs[key * hd + e8 + 2 * e + 1] = bf16_to_f32(vw[e] >> 16);
-      }
-    }
-    __syncthreads();
-    attend_chunk(Qs, Ks, Vs, Sc, Lc, G, cn, hd, rsqrtf((float)hd), qm, ql, corr, oacc, nullptr, nullptr, 0);
-  }
-  __syncthreads();
-  for (int i = tid; i < G * (hd + 2); i += kT) {
-    const int j = i / (hd + 2), e = i - j * (hd + 2);
-    float* pp = a.part2 + (((int64_t)r * Hq + g * G + j) * S + s) * (hd + 2);
-    pp[e] = e == 0 ? qm[j] : (e == 1 ? ql[j] : oacc[j * hd + e - 2]);
-  }
-  __syncthreads();
-  // the o projection merges the partials (PRE_COMBINE)
-}
-
-__device__ void cross_phase(const MkArgs& a, const CbCrossLayer& L, float* smem) {
-  const int Hkv = a.m.n_kv_heads, S = a.cross_splits, RQ = a.B * a.nq;
-  for (int it = blockIdx.x; it < RQ * Hkv * S; it += gridDim.x) {
-    const int s = it % S, g = (it / S) % Hkv, r = it / (S * Hkv);
-    cross_item(a, L, r, g, s, smem);
-  }
-}
-
 // ------------------------------------------------------ shared KV + indexer
 __device__ __forceinline__ void query_row(const MkArgs& a, int r, int& b, int& t, int& p, int& n) {
   b = r / a.nq;
@@ -1613,6 +1334,631 @@ __device__ void resolve_row(const MkArgs& a, int r, float* smem) {
   __syncthreads();
 }
 
+// ------------------------------------------------- attention (cluster per query head)
+// One cluster per query head h (KV head g = h / G) runs the whole attention
+// mixer of an SWA or cross layer:
+//   in-projection rows of the head (q; SWA also k and v of its KV head; the
+//   head gate), tiles rank, rank + 8, ... per CTA -> distributed shared memory
+//   -> q RMSNorm + RoPE (SWA: k too, and the first head of each KV group
+//   appends this step's k / v to the window ring) -> each CTA attends over its
+//   eighth of every query's keys (8-lane key groups, running softmax) -> the
+//   CTA partials (max, sum, o) are merged by every CTA of the cluster -> the
+//   gated head output times the head's column block of the o-projection for
+//   this CTA's d/8 output rows -> added to the residual stream.
+// Before the barrier that starts the phase (nothing there depends on the
+// step's earlier phases): the o-projection block, norms, RoPE frequencies, and
+// the K/V rows of this CTA's keys (SWA: the window's earlier positions; cross:
+// the selected keys, except in the first cross layer, whose selection is
+// resolved by the phase just before it) into shared memory.
+constexpr int kParHeadO = kParConv;                      // [d/8 rows][hd/2 code bytes + scale words]
+constexpr int kParHeadQn = kParHeadO + kMkMaxD / 8 * (128 / 2 + 8) / 4;  // q_norm [hd]
+constexpr int kParHeadKn = kParHeadQn + 128;             // k_norm [hd]
+constexpr int kParHeadInv = kParHeadKn + 128;            // RoPE inverse frequencies [rot/2]
+constexpr int kHeadOTs = 8;                              // small-block index of the o-projection tile scales
+
+struct HeadGeo {
+  int hd, G, g, qt, ntile, HP, RC, d, nsw, os, sb0, gate_row;
+  bool swa;
+};
+
+__device__ __forceinline__ HeadGeo head_geo(const CbModel& m, bool swa, int h) {
+  HeadGeo e;
+  e.swa = swa;
+  e.hd = m.head_dim;
+  e.G = m.n_q_heads / m.n_kv_heads;
+  e.g = h / e.G;
+  e.qt = e.hd / kTileRows;
+  e.ntile = (swa ? 3 : 1) * e.qt + 1;
+  e.HP = (swa ? 3 : 1) * e.hd + 1;
+  e.d = m.d_model;
+  e.RC = e.d / kCl;
+  e.nsw = e.hd >= 128 ? 2 : 1;   // scale words per o-projection row slice
+  e.os = e.hd / 2 + 4 * e.nsw;    // bytes per row slice
+  e.sb0 = h * e.hd / 16;          // first scale byte of the head's columns in an o-projection row
+  e.gate_row = (swa ? m.swa_off_gate : m.cr_off_gate) + h;
+  return e;
+}
+
+// Entry j of head h's in-projection tile list: q tiles, (SWA) k tiles, v tiles, then the gate tile.
+__device__ __forceinline__ int head_tile(const CbModel& m, const HeadGeo& e, int h, int j, int& hp_off) {
+  if (j < e.qt) {
+    hp_off = j * kTileRows;
+    return (h * e.hd) / kTileRows + j;
+  }
+  j -= e.qt;
+  if (e.swa) {
+    if (j < e.qt) {
+      hp_off = e.hd + j * kTileRows;
+      return (m.swa_off_kv + e.g * e.hd) / kTileRows + j;
+    }
+    j -= e.qt;
+    if (j < e.qt) {
+      hp_off = 2 * e.hd + j * kTileRows;
+      return (m.swa_off_kv + m.n_kv_heads * e.hd + e.g * e.hd) / kTileRows + j;
+    }
+  }
+  hp_off = e.HP - 1;
+  return e.gate_row / kTileRows;
+}
+
+template <typename F>
+__device__ __forceinline__ int head_chunks(const CbMatrix& W, const CbModel& m, bool swa, int h, int rank, F&& f) {
+  const HeadGeo e = head_geo(m, swa, h);
+  const int64_t tb = tile_bytes(W.k);
+  int n = 0, off = 0;
+  for (int j = rank; j < e.ntile; j += kCl) {
+    int hp_off;
+    const int t = head_tile(m, e, h, j, hp_off);
+    f(n++, W.tiles + t * tb, (unsigned)tb, off);
+    off += (int)tb;
+  }
+  return n;
+}
+
+// Shared-memory plan of a head phase inside the work area.  xs (the
+// in-projection input) is dead after the first cluster barrier and the
+// attention scratch overlays it; hp and part are read by the cluster; the
+// prefetched K/V rows take what is left below the parameter region.
+template <int M>
+struct HeadSmem {
+  static constexpr int QG = M <= 5 ? M : 4;  // queries per pass over the keys
+  float *xs, *qs, *og, *wpart, *hp, *part;
+  uint16_t *kc, *vc, *kvb;
+  int nbuf_max;
+};
+
+template <int M>
+__device__ __forceinline__ HeadSmem<M> head_smem(float* work, const HeadGeo& e) {
+  HeadSmem<M> s;
+  const int hd = e.hd;
+  s.xs = work;                                               // [M][d]
+  s.qs = work;                                               // [M][hd] scaled queries
+  s.kc = reinterpret_cast<uint16_t*>(s.qs + M * hd);         // [M][hd] this step's keys (bf16)
+  s.vc = s.kc + M * hd;                                      // [M][hd] this step's values (bf16)
+  s.og = s.qs + 2 * M * hd;                                  // [M][hd] gated head output
+  s.wpart = s.og + M * hd;                                   // [kW][QG][hd + 2] warp partials
+  const int over = pad4(3 * M * hd + kW * HeadSmem<M>::QG * (hd + 2));
+  s.hp = work + max(pad4(M * e.d), over);                    // [M][HP]
+  s.part = s.hp + pad4(M * e.HP);                            // [M][hd + 2] this CTA's partial per row
+  const int used = (int)(s.part - work) + pad4(M * (hd + 2));
+  s.nbuf_max = max(0, (kPreOff / 4 - used) / hd);            // a key row pair is hd floats
+  s.kvb = reinterpret_cast<uint16_t*>(work + kPreOff / 4 - s.nbuf_max * hd);  // [nbuf_max][K hd | V hd]
+  return s;
+}
+
+// The phase's rows and key segments (per CTA; kept from the preload to the phase).
+__shared__ int h_pos[kMkMaxRows], h_seq[kMkMaxRows], h_n[kMkMaxRows];
+__shared__ int g_lo[kMkMaxRows], g_n[kMkMaxRows], g_c0[kMkMaxRows], g_s0[kMkMaxRows], g_b[kMkMaxRows],
+    g_row[kMkMaxRows], g_p0[kMkMaxRows];
+__shared__ int g_nseg, g_tot, g_nbuf;
+
+// Row r < Mr (thread r): position, sequence and, for cross rows, the key count.
+__device__ __forceinline__ void head_rows(const MkArgs& a, bool swa, int Mr) {
+  const int r = threadIdx.x;
+  if (r < Mr) {
+    int b, t, p, n = 0;
+    if (swa) {
+      b = r / a.T;
+      p = a.c.pos[b] + a.c0 + (r - b * a.T);
+    } else {
+      query_row(a, r, b, t, p, n);
+      if (a.m.sparse_topk > 0) n = min(__ldcg(a.sel_cnt + r), a.sel_ld);
+    }
+    h_pos[r] = p;
+    h_seq[r] = b;
+    h_n[r] = n;
+  }
+}
+
+// Thread 0: the key segments of the pass over rows r0 .. r0 + nq - 1 (SWA: one per
+// sequence, the union of its queries' windows; cross: one per row, its
+// selection) and this rank's eighth of each, concatenated.
+__device__ __forceinline__ void head_segments(const MkArgs& a, bool swa, int r0, int nq, int rank) {
+  int ns = 0, tot = 0;
+  for (int j = 0; j < nq; ++j) {
+    const int r = r0 + j;
+    int lo, hi;
+    if (swa) {
+      lo = max(0, h_pos[r] - a.m.swa_window + 1);
+      hi = h_pos[r];
+      if (ns > 0 && g_b[ns - 1] == h_seq[r]) {  // a later token of the same sequence extends its segment
+        g_n[ns - 1] = hi - g_lo[ns - 1] + 1;
+        continue;
+      }
+    } else {
+      lo = 0;
+      hi = h_n[r] - 1;
+    }
+    g_lo[ns] = lo;
+    g_n[ns] = hi - lo + 1;
+    g_b[ns] = h_seq[r];
+    g_row[ns] = r;
+    g_p0[ns] = h_pos[r] - (r - h_seq[r] * a.T);  // position of the sequence's first token of this step
+    ++ns;
+  }
+  for (int s = 0; s < ns; ++s) {
+    const int n = max(0, g_n[s]);
+    const int a0 = n * rank / kCl, a1 = n * (rank + 1) / kCl;
+    g_s0[s] = a0;
+    g_c0[s] = tot;
+    tot += a1 - a0;
+  }
+  g_nseg = ns;
+  g_tot = tot;
+}
+
+// Key i of this rank's list: segment, position, and where its K/V rows are:
+// 0 = global memory (ks / vs), 1 = this step's SWA token (row of kc / vc).
+__device__ __forceinline__ int head_key(const MkArgs& a, const HeadGeo& e, bool swa, int layer, int i, bool need_src,
+                                        int& seg, int& kp, const uint16_t*& ks, const uint16_t*& vs, int& mr) {
+  int s = 0;
+  while (s + 1 < g_nseg && i >= g_c0[s + 1]) ++s;
+  seg = s;
+  const int li = g_s0[s] + (i - g_c0[s]), b = g_b[s];
+  const CbCache& c = a.c;
+  const int hd = e.hd, Hkv = a.m.n_kv_heads;
+  if (swa) {
+    kp = g_lo[s] + li;
+    if (kp >= g_p0[s]) {
+      mr = b * a.T + (kp - g_p0[s]);
+      return 1;
+    }
+    if (need_src) {
+      const int64_t off = (((int64_t)(b * c.n_swa + a.m.self_layers[layer].slot) * c.swa_slots + kp % c.swa_slots) *
+                               Hkv + e.g) * hd;
+      ks = c.swa_k + off;
+      vs = c.swa_v + off;
+    }
+    return 0;
+  }
+  kp = 0;
+  if (need_src) {
+    kp = a.m.sparse_topk > 0 ? __ldcg(a.sel_idx + (int64_t)g_row[s] * a.sel_ld + li) : li;
+    const int64_t off = (((int64_t)b * c.max_ctx + kp) * Hkv + e.g) * hd;
+    ks = c.kv_k + off;
+    vs = c.kv_v + off;
+  }
+  return 0;
+}
+
+// This rank's first nbuf keys (those in global memory) into kvb[i] = (K row, V row), 16 bytes per copy.
+__device__ void head_prefetch(const MkArgs& a, const HeadGeo& e, bool swa, int layer, uint16_t* kvb, int nbuf) {
+  const int hd = e.hd, per = hd / 8;
+  for (int x = threadIdx.x; x < nbuf * per; x += kT) {
+    const int i = x / per, q = x - i * per;
+    int seg, kp, mr;
+    const uint16_t *ks, *vs;
+    if (head_key(a, e, swa, layer, i, true, seg, kp, ks, vs, mr) == 0) {
+      cp_async16(kvb + (int64_t)i * 2 * hd + q * 8, ks + q * 8);
+      cp_async16(kvb + (int64_t)i * 2 * hd + hd + q * 8, vs + q * 8);
+    }
+  }
+}
+
+// The first pass's rows, segments and K/V prefetch (every thread of the CTA).
+template <int M>
+__device__ void head_plan(const MkArgs& a, const HeadGeo& e, bool swa, int layer, int rank, float* work) {
+  const int Mr = swa ? a.B * a.T : a.B * a.nq;
+  head_rows(a, swa, Mr);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    head_segments(a, swa, 0, min(HeadSmem<M>::QG, Mr), rank);
+    g_nbuf = min(g_tot, head_smem<M>(work, e).nbuf_max);
+  }
+  __syncthreads();
+  head_prefetch(a, e, swa, layer, head_smem<M>(work, e).kvb, g_nbuf);
+}
+
+// Before the barrier: norm vector, in-projection tile scales, q/k norms, RoPE
+// frequencies, this rank's o-projection rows restricted to the head's
+// columns, and (SWA, later cross layers) the plan and K/V prefetch.
+template <int M>
+__device__ void head_preload(const MkArgs& a, bool swa, int layer, int h, int rank, float* work) {
+  const CbModel& m = a.m;
+  const HeadGeo e = head_geo(m, swa, h);
+  const CbMatrix& W = swa ? m.self_layers[layer].in_proj : m.cross_layers[layer].q_gate;
+  const CbMatrix& O = swa ? m.self_layers[layer].o_proj : m.cross_layers[layer].o_proj;
+  const float* norm1 = swa ? m.self_layers[layer].norm1 : m.cross_layers[layer].norm1;
+  const float* qn = swa ? m.self_layers[layer].q_norm : m.cross_layers[layer].q_norm;
+  const int tid = threadIdx.x;
+  float* pn = par_norm(work);
+  float* ps = par_small(work);
+  for (int i = tid; i < e.d / 4; i += kT) cp_async16(pn + 4 * i, norm1 + 4 * i);
+  if (tid == 0) {
+    int q = 0;
+    for (int j = rank; j < e.ntile; j += kCl, ++q) {
+      int hp_off;
+      cp_async4(ps + q, W.tile_scale + head_tile(m, e, h, j, hp_off));
+    }
+  }
+  const int n0 = rank * e.RC, t0 = n0 / kTileRows, nt = (n0 + e.RC - 1) / kTileRows - t0 + 1;
+  for (int i = tid; i < nt; i += kT) cp_async4(ps + kHeadOTs + i, O.tile_scale + t0 + i);
+  float* pq = work + kPreOff / 4 + kParHeadQn;
+  float* pk = work + kPreOff / 4 + kParHeadKn;
+  float* pf = work + kPreOff / 4 + kParHeadInv;
+  for (int i = tid; i < e.hd; i += kT) {
+    cp_async4(pq + i, qn + i);
+    if (swa) cp_async4(pk + i, m.self_layers[layer].k_norm + i);
+  }
+  for (int i = tid; i < m.rot_dim / 2; i += kT) cp_async4(pf + i, m.inv_freq + i);
+  uint8_t* ob = reinterpret_cast<uint8_t*>(work + kPreOff / 4 + kParHeadO);
+  const int K = O.k, wpr = e.hd / 8 + e.nsw;  // words per row slice
+  const int64_t tb = tile_bytes(K);
+  for (int i = tid; i < e.RC * wpr; i += kT) {
+    const int row = i / wpr, wd = i - row * wpr, n = n0 + row, w = n & (kTileRows - 1);
+    const uint8_t* tile = O.tiles + (int64_t)(n / kTileRows) * tb;
+    const uint8_t* src = wd < e.hd / 8 ? tile + w * (K / 2) + h * (e.hd / 2) + wd * 4
+                                       : tile + kTileRows * (K / 2) + w * (K / 16) + (e.sb0 & ~3) + (wd - e.hd / 8) * 4;
+    cp_async4(ob + row * e.os + wd * 4, src);
+  }
+  if (swa || layer > 0) head_plan<M>(a, e, swa, layer, rank, work);
+}
+
+// RMSNorm over hd (weights w) + partial interleaved RoPE at position p of a
+// shared-memory vector, one warp; out = result * oscale.  When bits is set the
+// result is rounded to bfloat16 first and the bits are stored there too.
+__device__ __forceinline__ void head_norm_rope(const float* x, const float* w, int hd, int rot2, int p,
+                                               const float* inv_freq, float eps, float oscale, float* out,
+                                               uint16_t* bits) {
+  const int lane = threadIdx.x & 31;
+  float ss = 0.0f;
+  for (int i = lane; i < hd; i += 32) ss += x[i] * x[i];
+  ss = warp_sum(ss);
+  const float rn = rsqrtf(ss / (float)hd + eps);
+  for (int j = lane; j < hd / 2; j += 32) {
+    float x1 = x[2 * j] * rn * w[2 * j];
+    float x2 = x[2 * j + 1] * rn * w[2 * j + 1];
+    if (j < rot2) rope_pair(x1, x2, p, inv_freq[j]);
+    if (bits) {
+      const uint16_t b1 = f32_to_bf16(x1), b2 = f32_to_bf16(x2);
+      bits[2 * j] = b1;
+      bits[2 * j + 1] = b2;
+      x1 = bf16_to_f32(b1);
+      x2 = bf16_to_f32(b2);
+    }
+    out[2 * j] = x1 * oscale;
+    out[2 * j + 1] = x2 * oscale;
+  }
+}
+
+__device__ __forceinline__ float ld_dsmem(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// Running-softmax update of one query with one key score.
+__device__ __forceinline__ void soft_update(float sc, const float (&vf)[8], float& mq, float& lq, float (&o)[8]) {
+  const float mn = fmaxf(mq, sc);
+  const float c = mq == -INFINITY ? 0.0f : expf(mq - mn);
+  const float pe = expf(sc - mn);
+  lq = lq * c + pe;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) o[e] = fmaf(pe, vf[e], o[e] * c);
+  mq = mn;
+}
+
+template <int M>
+__device__ void head_phase(const MkArgs& a, bool swa, int layer, bool first, bool live, int h, int rank,
+                           const uint8_t* slot, float* work) {
+  constexpr int QG = HeadSmem<M>::QG;
+  constexpr int KU = QG == 1 ? 4 : 2;  // keys per key group in flight
+  const CbModel& m = a.m;
+  const CbCache& c = a.c;
+  const HeadGeo e = head_geo(m, swa, h);
+  const HeadSmem<M> sm = head_smem<M>(work, e);
+  const CbMatrix& W = swa ? m.self_layers[layer].in_proj : m.cross_layers[layer].q_gate;
+  long long* resid = swa ? a.hq : a.xq;
+  const int Mr = swa ? a.B * a.T : a.B * a.nq;
+  const int hd = e.hd, HP = e.HP, d = e.d, K = W.k;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t tb = tile_bytes(K);
+  float* xs = sm.xs;
+  float* qs = sm.qs;
+  uint16_t* kc = sm.kc;
+  uint16_t* vc = sm.vc;
+  float* og = sm.og;
+  float* wpart = sm.wpart;
+  float* hp = sm.hp;
+  float* part = sm.part;
+  const float* ps = par_small(work);
+  const float* qn = work + kPreOff / 4 + kParHeadQn;
+  const float* kn = work + kPreOff / 4 + kParHeadKn;
+  const float* inv = work + kPreOff / 4 + kParHeadInv;
+  const uint8_t* ob = reinterpret_cast<const uint8_t*>(work + kPreOff / 4 + kParHeadO);
+  const bool planned = swa || layer > 0;  // plan and K/V prefetch done before the barrier
+  if (live) {
+    if (!planned) head_plan<M>(a, e, swa, layer, rank, work);  // the first cross layer: selections are new
+    __shared__ int s_rows[kMkMaxRows];
+    if (tid < kMkMaxRows) s_rows[tid] = tid;
+    __syncthreads();
+    float rn[M];
+    stage_rows<M>(resid, nullptr, d, s_rows, Mr, K, par_norm(work), m.norm_eps, xs, rn, nullptr,
+                  (swa && first && h == 0 && rank == 0) ? a.hq : nullptr, (swa && first) ? &a : nullptr);
+    mark(a, 0);
+    int off = 0, q = 0;
+    for (int j = rank; j < e.ntile; j += kCl, ++q) {
+      int hp_off;
+      head_tile(m, e, h, j, hp_off);
+      const bool gate_tile = j == e.ntile - 1;
+      if (!gate_tile || warp == (e.gate_row & (kTileRows - 1))) {  // the gate tile: the head's row only
+        float acc[M];
+        row_dot<M>(slot + off, K, warp, true, false, xs, acc);
+        const float ts = ps[q];
+        const int col = gate_tile ? HP - 1 : hp_off + warp;
+        if (lane < kCl)
+#pragma unroll
+          for (int mr = 0; mr < M; ++mr)
+            if (mr < Mr) st_dsmem(dsmem(hp + mr * HP + col, lane), acc[mr] * ts * rn[mr]);
+      }
+      off += (int)tb;
+    }
+  }
+  cluster_sync();  // every rank's in-projection rows are in every rank's hp
+  mark(a, 1);
+  if (live) {
+    const int rot2 = m.rot_dim / 2;
+    const float scale = rsqrtf((float)hd);
+    const bool writer = swa && h % e.G == 0 && rank == 0;  // appends this step's k / v to the ring
+    const int nj = swa ? 3 : 1;                            // q; SWA also k and v, one warp each
+    for (int job = warp; job < Mr * nj; job += kW) {
+      const int mr = job / nj, kind = job - mr * nj, p = h_pos[mr];
+      int64_t roff = 0;
+      if (writer)
+        roff = (((int64_t)(h_seq[mr] * c.n_swa + m.self_layers[layer].slot) * c.swa_slots + p % c.swa_slots) *
+                    m.n_kv_heads + e.g) * hd;
+      if (kind == 0) {
+        head_norm_rope(hp + mr * HP, qn, hd, rot2, p, inv, m.norm_eps, scale, qs + mr * hd, nullptr);
+      } else if (kind == 1) {
+        head_norm_rope(hp + mr * HP + hd, kn, hd, rot2, p, inv, m.norm_eps, 1.0f, og + mr * hd, kc + mr * hd);
+        if (writer) {
+          __syncwarp();
+          for (int dd = lane; dd < hd; dd += 32) c.swa_k[roff + dd] = kc[mr * hd + dd];
+        }
+      } else {
+        for (int dd = lane; dd < hd; dd += 32) {
+          const uint16_t v = f32_to_bf16(hp[mr * HP + 2 * hd + dd]);
+          vc[mr * hd + dd] = v;
+          if (writer) c.swa_v[roff + dd] = v;
+        }
+      }
+    }
+    __syncthreads();
+    mark(a, 2);
+    // ---- attention: groups of LK lanes hold one key (8 dims per lane)
+    const int LK = hd / 8, KG = 32 / LK, NG = kW * KG;
+    const int grp = warp * KG + lane / LK, sub = lane % LK;
+    for (int r0 = 0; r0 < Mr; r0 += QG) {
+      const int nq = min(QG, Mr - r0);
+      int nbuf = 0;
+      if (r0 == 0) {
+        cp_async_wait_all();  // the prefetched keys
+        nbuf = g_nbuf;
+      } else if (tid == 0) {
+        head_segments(a, swa, r0, nq, rank);
+      }
+      __syncthreads();
+      const int tot = g_tot;
+      float o[QG][8], mq[QG], lq[QG];
+#pragma unroll
+      for (int j = 0; j < QG; ++j) {
+        mq[j] = -INFINITY;
+        lq[j] = 0.0f;
+#pragma unroll
+        for (int x = 0; x < 8; ++x) o[j][x] = 0.0f;
+      }
+      for (int base = 0; base < tot; base += NG * KU) {
+        uint4 kq[KU], vq[KU];
+        int kpos[KU], kseg[KU];
+#pragma unroll
+        for (int u = 0; u < KU; ++u) {
+          const int i = base + u * NG + grp;
+          kseg[u] = -1;
+          kpos[u] = 0;
+          kq[u] = make_uint4(0u, 0u, 0u, 0u);
+          vq[u] = kq[u];
+          if (i < tot) {
+            int seg, kp, mr;
+            const uint16_t *ks, *vs;
+            const int where = head_key(a, e, swa, layer, i, i >= nbuf, seg, kp, ks, vs, mr);
+            if (where == 1) {
+              kq[u] = *reinterpret_cast<const uint4*>(kc + mr * hd + sub * 8);
+              vq[u] = *reinterpret_cast<const uint4*>(vc + mr * hd + sub * 8);
+            } else if (i < nbuf) {
+              kq[u] = *reinterpret_cast<const uint4*>(sm.kvb + (int64_t)i * 2 * hd + sub * 8);
+              vq[u] = *reinterpret_cast<const uint4*>(sm.kvb + (int64_t)i * 2 * hd + hd + sub * 8);
+            } else {
+              kq[u] = __ldcg(reinterpret_cast<const uint4*>(ks + sub * 8));
+              vq[u] = __ldcg(reinterpret_cast<const uint4*>(vs + sub * 8));
+            }
+            kpos[u] = kp;
+            kseg[u] = seg;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < KU; ++u) {
+          const uint32_t kw[4] = {kq[u].x, kq[u].y, kq[u].z, kq[u].w}, vw[4] = {vq[u].x, vq[u].y, vq[u].z, vq[u].w};
+          float kf[8], vf[8];
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            kf[2 * x] = bf16_to_f32(kw[x]);
+            kf[2 * x + 1] = bf16_to_f32(kw[x] >> 16);
+            vf[2 * x] = bf16_to_f32(vw[x]);
+            vf[2 * x + 1] = bf16_to_f32(vw[x] >> 16);
+          }
+#pragma unroll
+          for (int j = 0; j < QG; ++j) {
+            if (j < nq) {
+              const float4 q0 = *reinterpret_cast<const float4*>(qs + (r0 + j) * hd + sub * 8);
+              const float4 q1 = *reinterpret_cast<const float4*>(qs + (r0 + j) * hd + sub * 8 + 4);
+              float sc = q0.x * kf[0];
+              sc = fmaf(q0.y, kf[1], sc);
+              sc = fmaf(q0.z, kf[2], sc);
+              sc = fmaf(q0.w, kf[3], sc);
+              sc = fmaf(q1.x, kf[4], sc);
+              sc = fmaf(q1.y, kf[5], sc);
+              sc = fmaf(q1.z, kf[6], sc);
+              sc = fmaf(q1.w, kf[7], sc);
+              for (int x = LK / 2; x > 0; x >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, x);
+              const int s = kseg[u];
+              bool ok = s >= 0;
+              if (ok) {
+                if (swa) {
+                  const int pj = h_pos[r0 + j];
+                  ok = g_b[s] == h_seq[r0 + j] && kpos[u] <= pj && kpos[u] > pj - m.swa_window;
+                } else {
+                  ok = g_row[s] == r0 + j;
+                }
+              }
+              if (ok) soft_update(sc, vf, mq[j], lq[j], o[j]);
+            }
+          }
+        }
+      }
+      if (r0 == 0) mark(a, 3);
+      // merge the key groups of the warp, then the warps
+      for (int x = LK; x < 32; x <<= 1) {
+#pragma unroll
+        for (int j = 0; j < QG; ++j) {
+          const float m2 = __shfl_xor_sync(0xffffffffu, mq[j], x), l2 = __shfl_xor_sync(0xffffffffu, lq[j], x);
+          const float mn = fmaxf(mq[j], m2);
+          const float c1 = mq[j] == -INFINITY ? 0.0f : expf(mq[j] - mn);
+          const float c2 = m2 == -INFINITY ? 0.0f : expf(m2 - mn);
+          lq[j] = lq[j] * c1 + l2 * c2;
+#pragma unroll
+          for (int y = 0; y < 8; ++y) {
+            const float o2 = __shfl_xor_sync(0xffffffffu, o[j][y], x);
+            o[j][y] = o[j][y] * c1 + o2 * c2;
+          }
+          mq[j] = mn;
+        }
+      }
+      if (lane < LK) {
+#pragma unroll
+        for (int j = 0; j < QG; ++j) {
+          float* wp = wpart + (warp * QG + j) * (hd + 2);
+          if (lane == 0) {
+            wp[0] = mq[j];
+            wp[1] = lq[j];
+          }
+#pragma unroll
+          for (int y = 0; y < 8; ++y) wp[2 + sub * 8 + y] = o[j][y];
+        }
+      }
+      __syncthreads();
+      for (int i = tid; i < nq * (hd + 2); i += kT) {
+        const int j = i / (hd + 2), x = i - j * (hd + 2);
+        float mx = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kW; ++w) mx = fmaxf(mx, wpart[(w * QG + j) * (hd + 2)]);
+        float v = mx;
+        if (x > 0) {
+          v = 0.0f;
+#pragma unroll
+          for (int w = 0; w < kW; ++w) {
+            const float* wp = wpart + (w * QG + j) * (hd + 2);
+            if (wp[0] != -INFINITY) v += wp[x] * expf(wp[0] - mx);
+          }
+        }
+        part[(r0 + j) * (hd + 2) + x] = v;
+      }
+      __syncthreads();
+    }
+  }
+  mark(a, 4);
+  cluster_sync();  // every rank's partials are complete
+  mark(a, 5);
+  if (live) {
+    // merge the cluster's partials (every rank, all rows) into the gated head output
+    for (int i = tid; i < Mr * hd; i += kT) {
+      const int mr = i / hd, dd = i - mr * hd;
+      float mr_[kCl], lr[kCl], orr[kCl];
+#pragma unroll
+      for (int r = 0; r < kCl; ++r) {
+        const float* pp = part + mr * (hd + 2);
+        mr_[r] = ld_dsmem(dsmem(pp, r));
+        lr[r] = ld_dsmem(dsmem(pp + 1, r));
+        orr[r] = ld_dsmem(dsmem(pp + 2 + dd, r));
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < kCl; ++r) mx = fmaxf(mx, mr_[r]);
+      float L = 0.0f, O = 0.0f;
+#pragma unroll
+      for (int r = 0; r < kCl; ++r) {
+        if (mr_[r] == -INFINITY) continue;
+        const float w = expf(mr_[r] - mx);
+        L = fmaf(lr[r], w, L);
+        O = fmaf(orr[r], w, O);
+      }
+      og[i] = L > 0.0f ? (O / L) * sigmoid(hp[mr * HP + HP - 1]) : 0.0f;
+    }
+    __syncthreads();
+    // o-projection: output rows rank * RC ... of the head's hd columns, hd / 16 lanes per row
+    const int LQ = hd / 16, total = e.RC * LQ, n0 = rank * e.RC, t0 = n0 / kTileRows;
+    for (int base = 0; base < total; base += kT) {
+      const int i = base + tid, row = i / LQ, qb = i - row * LQ;
+      const bool valid = i < total;
+      float acc[M];
+#pragma unroll
+      for (int mr = 0; mr < M; ++mr) acc[mr] = 0.0f;
+      if (valid) {
+        const uint8_t* rb = ob + row * e.os;
+        const uint32_t c0 = *reinterpret_cast<const uint32_t*>(rb + qb * 8);
+        const uint32_t c1 = *reinterpret_cast<const uint32_t*>(rb + qb * 8 + 4);
+        const int n = n0 + row;
+        const float sc = e4m3_to_f32(rb[e.hd / 2 + (e.sb0 & 3) + qb]) * ps[kHeadOTs + n / kTileRows - t0];
+        float w[16];
+#pragma unroll
+        for (int x = 0; x < 4; ++x) {
+          const float2 lo = e2m1x2_to_f32x2(c0 >> (8 * x)), hi = e2m1x2_to_f32x2(c1 >> (8 * x));
+          w[2 * x] = lo.x;
+          w[2 * x + 1] = lo.y;
+          w[8 + 2 * x] = hi.x;
+          w[8 + 2 * x + 1] = hi.y;
+        }
+#pragma unroll
+        for (int mr = 0; mr < M; ++mr) {
+          if (mr < Mr) {
+            const float* ov = og + mr * hd + qb * 16;
+            float p = 0.0f;
+#pragma unroll
+            for (int x = 0; x < 16; ++x) p = fmaf(w[x], ov[x], p);
+            acc[mr] = p * sc;
+          }
+        }
+      }
+#pragma unroll
+      for (int mr = 0; mr < M; ++mr)
+        for (int x = LQ / 2; x > 0; x >>= 1) acc[mr] += __shfl_xor_sync(0xffffffffu, acc[mr], x);
+      if (valid && qb == 0)
+#pragma unroll
+        for (int mr = 0; mr < M; ++mr)
+          if (mr < Mr) red_fix(resid + (int64_t)mr * d + n0 + row, acc[mr]);
+    }
+  }
+}
+
 // ------------------------------------------------------------------ phase plan
 __device__ int build_plan(const CbModel& m, uint16_t* plan) {
   int n = 0;
@@ -1621,19 +1967,18 @@ __device__ int build_plan(const CbModel& m, uint16_t* plan) {
     if (m.self_layers[i].kind == CB_LAYER_GDN) {
       push(PH_GDN, i);
     } else {
-      push(PH_SWA_IN, i);
-      push(PH_SWA_ATT, i);
-      push(PH_SWA_O, i);
+      push(PH_SWA_HEAD, i);
     }
     push(PH_FFN_SELF, i);
   }
   push(PH_SH_PROJ, 0);
   push(PH_SH_SCORE, 0);
-  if (m.sparse_topk > 0) push(PH_SH_COMPACT, 0);
+  if (m.sparse_topk > 0) {
+    push(PH_SH_COMPACT, 0);
+    push(PH_CR_RESOLVE, 0);
+  }
   for (int j = 0; j < m.n_cross_layers; ++j) {
-    push(PH_CR_Q, j);
-    push(PH_CR_ATT, j);
-    push(PH_CR_O, j);
+    push(PH_CR_HEAD, j);
     push(PH_FFN_CROSS, j);
   }
   push(PH_LM_HEAD, 0);
@@ -1643,40 +1988,13 @@ __device__ int build_plan(const CbModel& m, uint16_t* plan) {
 // The GEMV of a GEMV phase (input, output, this CTA's units).
 __device__ GemvJob gemv_job(const MkArgs& a, int kind, int layer) {
   const CbModel& m = a.m;
-  const int d = m.d_model, RQ = a.B * a.nq;
+  const int d = m.d_model;
   GemvJob g{};
   g.ucta = blockIdx.x;
   g.uncta = gridDim.x;
   g.ldx = d;
   g.epi = EPI_STORE_;
   switch (kind) {
-    case PH_SWA_IN: {
-      const CbSelfLayer& L = m.self_layers[layer];
-      g.W = L.in_proj;
-      g.xq = a.hq;
-      g.pre = layer == 0 ? PRE_EMBED_ : PRE_RMS_;
-      g.norm_w = L.norm1;
-      g.y = a.proj;
-      g.ldy = a.ldp;
-      g.rows_out = L.in_proj.rows;
-      break;
-    }
-    case PH_SWA_O: {
-      const CbSelfLayer& L = m.self_layers[layer];
-      g.W = L.o_proj;
-      g.pre = PRE_COMBINE_;
-      g.part = a.part;
-      g.S = a.swa_splits;
-      g.hd = m.head_dim;
-      g.gate_x = a.proj;
-      g.gate_ld = a.ldp;
-      g.gate_off = m.swa_off_gate;
-      g.yq = a.hq;
-      g.ldy = d;
-      g.rows_out = d;
-      g.epi = EPI_RED_;
-      break;
-    }
     case PH_SH_PROJ:
       g.W = m.shared_proj;
       g.xq = a.hq;
@@ -1686,43 +2004,6 @@ __device__ GemvJob gemv_job(const MkArgs& a, int kind, int layer) {
       g.ldy = a.ldp;
       g.rows_out = m.shared_proj.rows;
       break;
-    case PH_CR_Q: {
-      const CbCrossLayer& L = m.cross_layers[layer];
-      g.W = L.q_gate;
-      g.xq = layer == 0 ? a.hq : a.xq;
-      if (layer == 0) {  // the query rows of the self-decoder's output start the cross residual stream
-        g.xmap_nq = a.nq;
-        g.xmap_T = a.T;
-        g.xmap_off = a.T - a.nq;
-        g.copy_q = a.xq;
-        if (m.sparse_topk > 0) {  // the first RQ CTAs resolve the selections beside this GEMV
-          g.ucta = (int)blockIdx.x - RQ;
-          g.uncta = (int)gridDim.x - RQ;
-        }
-      }
-      g.pre = PRE_RMS_;
-      g.norm_w = L.norm1;
-      g.y = a.cproj;
-      g.ldy = a.cr_ld;
-      g.rows_out = L.q_gate.rows;
-      break;
-    }
-    case PH_CR_O: {
-      const CbCrossLayer& L = m.cross_layers[layer];
-      g.W = L.o_proj;
-      g.pre = PRE_COMBINE_;
-      g.part = a.part2;
-      g.S = a.cross_splits;
-      g.hd = m.head_dim;
-      g.gate_x = a.cproj;
-      g.gate_ld = a.cr_ld;
-      g.gate_off = m.cr_off_gate;
-      g.yq = a.xq;
-      g.ldy = d;
-      g.rows_out = d;
-      g.epi = EPI_RED_;
-      break;
-    }
     default:  // PH_LM_HEAD
       g.W = m.lm_head;
       g.xq = a.xq;
@@ -1738,8 +2019,7 @@ __device__ GemvJob gemv_job(const MkArgs& a, int kind, int layer) {
 }
 
 __device__ __forceinline__ bool is_gemv(int kind) {
-  return kind == PH_SWA_IN || kind == PH_SWA_O || kind == PH_SH_PROJ || kind == PH_CR_Q || kind == PH_CR_O ||
-         kind == PH_LM_HEAD;
+  return kind == PH_SH_PROJ || kind == PH_LM_HEAD;
 }
 
 // Weight chunks of phase (kind, layer) for this CTA, in slot order: f(i, src, bytes, slot offset).
@@ -1766,6 +2046,13 @@ __device__ int phase_chunks(const MkArgs& a, int kind, int layer, F&& f) {
     const CbCrossLayer& L = m.cross_layers[layer];
     return ffn_chunks(L.gate_up, L.down_ks, m.ffn_hidden, blockIdx.x, gridDim.x, f);
   }
+  if (kind == PH_SWA_HEAD || kind == PH_CR_HEAD) {
+    const int cid = (int)cluster_index();
+    if (cid >= m.n_q_heads) return 0;
+    const bool swa = kind == PH_SWA_HEAD;
+    return head_chunks(swa ? m.self_layers[layer].in_proj : m.cross_layers[layer].q_gate, m, swa, cid,
+                       (int)cluster_rank(), f);
+  }
   return 0;
 }
 
@@ -1773,6 +2060,7 @@ __device__ int phase_chunks(const MkArgs& a, int kind, int layer, F&& f) {
 // there: the phase's norm vector, tile scales and tensor scale into the
 // parameter region (cp.async; completed after the wait).  The GDN phase has
 // its own (gdn_preload).
+template <int M>
 __device__ void phase_params(const MkArgs& a, int kind, int layer, float* work) {
   const CbModel& m = a.m;
   const int tid = threadIdx.x;
@@ -1799,6 +2087,9 @@ __device__ void phase_params(const MkArgs& a, int kind, int layer, float* work) 
       cp_async4(ps + 16 + i, GU.tile_scale + m.ffn_hidden / kTileRows + j);
     }
     if (tid == 0) cp_async4(ps + PS_TSCALE, D.tensor_scale);
+  } else if (kind == PH_SWA_HEAD || kind == PH_CR_HEAD) {
+    const int cid = (int)cluster_index();
+    if (cid < m.n_q_heads) head_preload<M>(a, kind == PH_SWA_HEAD, layer, cid, (int)cluster_rank(), work);
   }
 }
 
@@ -1815,6 +2106,22 @@ __device__ void stage_issue(const MkArgs& a, int kind, int layer, uint8_t* slot,
   phase_chunks(a, kind, layer, [&](int i, const uint8_t* src, unsigned bytes, int off) {
     if ((i & 31) == lane) bulk_copy(slot + off, src, bytes, bar);
   });
+}
+
+// Warp 0, last phase only: the GEMV tiles after the staged ones into the other slot.
+__device__ void stage_issue_extra(const MkArgs& a, int kind, int layer, uint8_t* slot, unsigned long long* bar) {
+  const int lane = threadIdx.x & 31;
+  const GemvJob g = gemv_job(a, kind, layer);
+  const int nst = gemv_staged(g), nx = gemv_extra(g);
+  if (nx == 0) return;
+  const int64_t tb = tile_bytes(g.W.k);
+  if (lane == 0) {
+    fence_proxy_async();
+    mbar_expect_arrive(bar, (unsigned)(nx * tb));
+  }
+  __syncwarp();
+  for (int i = lane; i < nx; i += 32)
+    bulk_copy(slot + i * tb, g.W.tiles + (int64_t)(g.ucta + (nst + i) * g.uncta) * tb, (unsigned)tb, bar);
 }
 
 // ------------------------------------------------------------------ kernel
@@ -1865,17 +2172,25 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
 
   for (int p = 0; p < P; ++p) {
     const int kind = s_plan[p] >> 8, layer = s_plan[p] & 0xFF, sl = p & 1;
+    int nst2 = 0;  // tiles of this phase in the other slot (last phase only)
     if (live && p + 1 < P) {  // the next phase's weights, into the other slot
       if (warp == 0) stage_issue(a, s_plan[p + 1] >> 8, s_plan[p + 1] & 0xFF, smem + (sl ^ 1) * kSlot, &s_bar[sl ^ 1]);
       if (sl) issued0 += 1;
       else issued1 += 1;
+    } else if (live && is_gemv(kind)) {  // the last phase: its later tiles into the free slot
+      nst2 = gemv_extra(gemv_job(a, kind, layer));
+      if (nst2 > 0) {
+        if (warp == 0) stage_issue_extra(a, kind, layer, smem + (sl ^ 1) * kSlot, &s_bar[sl ^ 1]);
+        if (sl) issued0 += 1;
+        else issued1 += 1;
+      }
     }
     float st[M];  // the recurrent state of this thread's GDN columns, one value per sequence
     const bool gdn_here = kind == PH_GDN && cid < m.gdn_heads;
-    if (tid == 0) s_mark_base = kMarkBase + 4 * p;
+    if (tid == 0) s_mark_base = kMarkBase + 6 * p;
     if (live) {
       if (gdn_here) gdn_preload<M>(a, m.self_layers[layer], cid, rank, st, work);
-      else phase_params(a, kind, layer, work);
+      else phase_params<M>(a, kind, layer, work);
     }
     live = grid_wait(a, gen, &s_ok) && live;
     cp_async_wait_all();  // this phase's parameters
@@ -1907,11 +2222,19 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
         ffn_phase<M>(a, L.gate_up, L.down_ks, L.norm2, a.xq, RQ, live, rank, cid, slot, work);
         break;
       }
-      case PH_SWA_ATT:
-        if (live) swa_phase(a, m.self_layers[layer], work);
+      case PH_SWA_HEAD:
+        if (cid < m.n_q_heads) head_phase<M>(a, true, layer, layer == 0, live, cid, rank, slot, work);
+        break;
+      case PH_CR_HEAD:
+        if (cid < m.n_q_heads) head_phase<M>(a, false, layer, false, live, cid, rank, slot, work);
         break;
       case PH_SH_SCORE:
         if (live) {
+          // the query rows of the self-decoder's output start the cross residual stream
+          for (int i = cta * kT + tid; i < RQ * d; i += ncta * kT) {
+            const int r = i / d, k = i - r * d, b = r / a.nq;
+            a.xq[i] = __ldcg(a.hq + ((int64_t)b * a.T + (a.T - a.nq) + (r - b * a.nq)) * d + k);
+          }
           shared_append(a, work);
           if (m.sparse_topk > 0) score_phase(a, work);
         }
@@ -1919,15 +2242,31 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
       case PH_SH_COMPACT:
         if (live) compact_phase(a);
         break;
-      case PH_CR_ATT:
-        if (live) cross_phase(a, m.cross_layers[layer], work);
+      case PH_CR_RESOLVE:
+        if (live && cta < RQ) resolve_row(a, cta, work);
         break;
       default: {  // GEMV phases
         if (!live) break;
         const GemvJob g = gemv_job(a, kind, layer);
-        const int rows = (kind == PH_CR_Q || kind == PH_CR_O || kind == PH_LM_HEAD) ? RQ : Mrows;
-        if (kind == PH_CR_Q && layer == 0 && m.sparse_topk > 0 && cta < RQ) resolve_row(a, cta, work);
-        else gemv_phase<M>(a, g, rows, slot, work);
+        const int rows = kind == PH_LM_HEAD ? RQ : Mrows;
+        if (nst2 > 0) {  // the second slot's tiles (copies started before the barrier)
+          const unsigned iss2 = sl ? issued0 : issued1, wtd2 = sl ? waited0 : waited1;
+          if (iss2 > wtd2) {
+            const bool ok = mbar_wait(&s_bar[sl ^ 1], wtd2 & 1u);
+            if (sl) waited0 += 1;
+            else waited1 += 1;
+            if (!ok && tid == 0) {
+              raise_abort(a);
+              s_live = 0;
+            }
+            __syncthreads();
+            if (s_live == 0) {
+              live = false;
+              break;
+            }
+          }
+        }
+        gemv_phase<M>(a, g, rows, slot, smem + (sl ^ 1) * kSlot, nst2, work);
         if (kind == PH_LM_HEAD && a.hidden != nullptr && cta == ncta - 1)
           for (int i = tid; i < RQ * d; i += kT) a.hidden[i] = from_fix(__ldcg(a.xq + i));
         break;
@@ -1970,20 +2309,27 @@ bool mk_supported(const CbModel& m, const CbCache& c, int T, int nq) {
                             m.indexer_heads > 16 || (m.indexer_heads * m.indexer_dim + 16 + kMkHistBins) * 4 +
                             CB_MAX_T * m.indexer_dim > kWork))
     return false;
-  const size_t att = sizeof(float) * ((size_t)kMkSwaSplit * (2 * m.head_dim + 1) + (size_t)kMkMaxQ * m.head_dim * 2 +
-                                      (size_t)kMkMaxQ * kMkSwaSplit) +
-                     sizeof(uint16_t) * 2 * kMkSwaSplit * m.head_dim;
-  if (att > (size_t)kWork) return false;
-  if (mk_swa_splits(m) > 32) return false;
-  if (m.sparse_topk > 0 && ceil_div(m.sparse_topk + 1, kMkCrossSplit) > 32) return false;
-  // GEMV staging: [M][K] inputs (+ [M][H][32] split weights for the o projections)
-  if ((size_t)kMkMaxRows * (kMkMaxD + m.n_q_heads * 32) * sizeof(float) > (size_t)kPreOff) return false;
+  // attention phases (a cluster per query head): hd / 8 lanes per key, 16-row
+  // tiles of q / k / v, the o-projection's column block of each head on 4-byte words
+  const int hd = m.head_dim;
+  if (hd % 16 || 32 % (hd / 8) || d % kCl || (m.n_q_heads * hd) % 64 || m.rot_dim / 2 > 64) return false;
+  {
+    const int HP = 3 * hd + 1, QGm = 5;
+    const size_t w = sizeof(float) * ((size_t)std::max(pad4(kMkMaxRows * d),
+                                                       pad4(3 * kMkMaxRows * hd + kW * QGm * (hd + 2))) +
+                                      pad4(kMkMaxRows * HP) + (size_t)kMkMaxRows * (hd + 2));
+    if (w > (size_t)kPreOff) return false;
+    if ((int64_t)ceil_div(3 * hd / kTileRows + 1, kCl) * tile_bytes(d) > kSlot) return false;
+  }
+  // GEMV staging: [M][K] inputs
+  if ((size_t)kMkMaxRows * kMkMaxD * sizeof(float) > (size_t)kPreOff) return false;
   // FFN: [8][M][d/8] partials + [M][d] inputs + [M][16]
   if ((size_t)kMkMaxRows * (2 * d + 16) * sizeof(float) > (size_t)kPreOff) return false;
   const int64_t tb = tile_bytes(d);
   for (int i = 0; i < m.n_self_layers; ++i) {
     const CbSelfLayer& L = m.self_layers[i];
     if (L.in_proj.k != d || L.gate_up.k != d || L.o_proj.rows < d || L.down.rows < d) return false;
+    if (L.kind != CB_LAYER_GDN && L.o_proj.k != m.n_q_heads * hd) return false;
     if (!sliced_ok(L.down_ks, d, m.ffn_hidden, 16)) return false;
     if (L.kind == CB_LAYER_GDN) {
       const int Dk = m.gdn_dk, Dv = m.gdn_dv, vpr = Dv / kCl;
@@ -2003,7 +2349,7 @@ bool mk_supported(const CbModel& m, const CbCache& c, int T, int nq) {
   }
   for (int j = 0; j < m.n_cross_layers; ++j) {
     const CbCrossLayer& L = m.cross_layers[j];
-    if (L.q_gate.k != d || L.gate_up.k != d) return false;
+    if (L.q_gate.k != d || L.gate_up.k != d || L.o_proj.rows < d || L.o_proj.k != m.n_q_heads * hd) return false;
     if (!sliced_ok(L.down_ks, d, m.ffn_hidden, 16)) return false;
   }
   if (m.lm_head.k != d || m.shared_proj.k != d) return false;
@@ -2020,8 +2366,8 @@ int launch_mk(const MkArgs& a, cudaStream_t st) {
   else fn = decode_mk_kernel<8>;
   if (ensure_smem_attr((const void*)fn, kSmem) != CB_OK) return CB_ERR_CUDA;
   const int ncl = std::min(resident_clusters((const void*)fn, kMkThreads, kSmem, kCl), kMkMaxClusters);
-  // every GDN head needs a cluster, and the first cross layer needs CTAs beyond the query rows
-  if (ncl < a.m.gdn_heads || ncl * kCl <= a.B * a.nq) return CB_ERR_SHAPE;
+  // every GDN head and every query head needs a cluster; one CTA resolves each query row's selection
+  if (ncl < a.m.gdn_heads || ncl < a.m.n_q_heads || ncl * kCl < a.B * a.nq) return CB_ERR_SHAPE;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(ncl * kCl);
   cfg.blockDim = dim3(kMkThreads);
