@@ -243,10 +243,11 @@ struct RowW {
 // Row `w` of a 16-row tile (codes of the 16 rows, then their scales), in shared
 // or global memory.
 template <int NU>
-__device__ __forceinline__ void tile_row(const uint8_t* tile, int K, int w, bool valid, bool global, RowW<NU>& r) {
+__device__ __forceinline__ void tile_row(const uint8_t* tile, int K, int w, bool valid, bool global, RowW<NU>& r,
+                                         int trows = kTileRows) {
   const int lane = threadIdx.x & 31, kc = K >> 3;
   const uint32_t* cw = reinterpret_cast<const uint32_t*>(tile + w * (K / 2));
-  const uint8_t* sb = tile + kTileRows * (K / 2) + w * (K / 16);
+  const uint8_t* sb = tile + trows * (K / 2) + w * (K / 16);
 #pragma unroll
   for (int u = 0; u < NU; ++u) {
     const int c = u * 32 + lane;
@@ -291,19 +292,19 @@ __device__ __forceinline__ void dot_row(const RowW<NU>& r, int K, const float* x
 }
 
 // Dot products of one tile row with the M staged input rows: acc[m] holds the
-// warp-reduced sum on every lane.
+// warp-reduced sum on every lane.  A tile holds trows rows (codes, then scales).
 template <int M>
 __device__ __forceinline__ void row_dot(const uint8_t* tile, int K, int w, bool valid, bool global, const float* xs,
-                                        float (&acc)[M]) {
+                                        float (&acc)[M], int trows = kTileRows) {
 #pragma unroll
   for (int m = 0; m < M; ++m) acc[m] = 0.0f;
   if (K <= 768) {
     RowW<3> r;
-    tile_row<3>(tile, K, w, valid, global, r);
+    tile_row<3>(tile, K, w, valid, global, r, trows);
     dot_row<M, 3>(r, K, xs, acc);
   } else {
     RowW<8> r;
-    tile_row<8>(tile, K, w, valid, global, r);
+    tile_row<8>(tile, K, w, valid, global, r, trows);
     dot_row<M, 8>(r, K, xs, acc);
   }
 #pragma unroll
@@ -856,18 +857,36 @@ __device__ __forceinline__ void gdn_phase(const MkArgs& a, const CbSelfLayer& L,
 // ------------------------------------------------------------------ FFN (split K)
 // Slices of 16 hidden units: slice j = the gate tile j, the up tile F/16 + j and
 // the 16 columns j of the down projection.  CTA c owns slices c, c + ncta, ...
-__device__ __forceinline__ int ffn_mine(int F, int cta, int ncta) {
+// When the slices outnumber the CTAs by at most one per cluster, CTA c owns
+// slice c only and slice ncta + q is split over cluster q instead: its CTA r
+// takes hidden units 2r and 2r + 1 (gate and up rows 2r, 2r + 1 and down
+// columns 2r, 2r + 1), so that no CTA holds two slices.
+__device__ __forceinline__ bool ffn_split(int F, int K, int ncta) {
   const int nsl = F / kTileRows;
+  return nsl > ncta && nsl - ncta <= ncta / kCl && K % 128 == 0;
+}
+__device__ __forceinline__ int ffn_mine(int F, int K, int cta, int ncta) {
+  const int nsl = F / kTileRows;
+  if (ffn_split(F, K, ncta)) return 1;
   return cta < nsl ? (nsl - 1 - cta) / ncta + 1 : 0;
+}
+// The slice split over this CTA's cluster, or -1.
+__device__ __forceinline__ int ffn_extra(int F, int K, int cta, int ncta) {
+  if (!ffn_split(F, K, ncta)) return -1;
+  const int q = cta / kCl;
+  return q < F / kTileRows - ncta ? ncta + q : -1;
 }
 __device__ __forceinline__ int ffn_staged(const CbMatrix& GU, const CbSliced& D, int F, int cta, int ncta) {
   const int64_t per = 2 * tile_bytes(GU.k) + slice_bytes(D);
-  return min(ffn_mine(F, cta, ncta), (int)(kSlot / per));
+  return min(ffn_mine(F, GU.k, cta, ncta), (int)(kSlot / per));
 }
 
+// Slot layout: the staged slices (gate tile, up tile, down slice each), then for
+// a split slice: gate rows 2r, 2r + 1 (codes, then scales), the same up rows, the down slice.
 template <typename F>
 __device__ __forceinline__ int ffn_chunks(const CbMatrix& GU, const CbSliced& D, int Fh, int cta, int ncta, F&& f) {
-  const int64_t tb = tile_bytes(GU.k), dsb = slice_bytes(D);
+  const int K = GU.k;
+  const int64_t tb = tile_bytes(K), dsb = slice_bytes(D);
   const int nst = ffn_staged(GU, D, Fh, cta, ncta);
   int n = 0, off = 0;
   for (int i = 0; i < nst; ++i) {
@@ -879,25 +898,40 @@ __device__ __forceinline__ int ffn_chunks(const CbMatrix& GU, const CbSliced& D,
     f(n++, D.data + j * dsb, (unsigned)dsb, off);
     off += (int)dsb;
   }
+  const int x = ffn_extra(Fh, K, cta, ncta);
+  if (x >= 0) {
+    const int r = cta % kCl;
+    for (int t = 0; t < 2; ++t) {
+      const uint8_t* tile = GU.tiles + (t == 0 ? x : Fh / kTileRows + x) * tb;
+      f(n++, tile + 2 * r * (K / 2), (unsigned)K, off);
+      off += K;
+      f(n++, tile + kTileRows * (K / 2) + 2 * r * (K / 16), (unsigned)(K / 8), off);
+      off += K / 8;
+    }
+    f(n++, D.data + x * dsb, (unsigned)dsb, off);
+  }
   return n;
 }
 
 template <int M>
-__device__ void ffn_phase(const MkArgs& a, const CbMatrix& GU, const CbSliced& D, const float* norm2, long long* resid,
-                          int Mr, bool live, int rank, int cid, const uint8_t* slot, float* work) {
+__device__ __forceinline__ void ffn_phase(const MkArgs& a, const CbMatrix& GU, const CbSliced& D, const float* norm2,
+                                          long long* resid, int Mr, bool live, int rank, int cid, const uint8_t* slot,
+                                          float* work) {
   const CbModel& m = a.m;
   const int d = m.d_model, Fh = m.ffn_hidden, RC = d / kCl, K = GU.k;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, cta = blockIdx.x, ncta = gridDim.x;
   float* red = work;                   // [kCl][M][RC]  (written by the cluster's CTAs)
   float* xs = red + kCl * M * RC;      // [M][d]
   float* act = xs + M * d;             // [M][16]
+  float* gux = act + M * kTileRows;    // [4][M] split slice: gate 2r, gate 2r + 1, up 2r, up 2r + 1
   constexpr int kNE = (kMkMaxD + kT - 1) / kT;  // outputs per thread
   float acc[kNE][M];
 #pragma unroll
   for (int e = 0; e < kNE; ++e)
 #pragma unroll
     for (int mr = 0; mr < M; ++mr) acc[e][mr] = 0.0f;
-  const int n_mine = ffn_mine(Fh, cta, ncta);
+  const int n_mine = ffn_mine(Fh, K, cta, ncta);
+  const int xsl = ffn_extra(Fh, K, cta, ncta);
   // a cluster adds its sums only when one of its CTAs owns a slice (cluster-uniform)
   const bool cluster_has = cid * kCl < Fh / kTileRows;
   if (live && n_mine > 0) {
@@ -922,6 +956,20 @@ __device__ void ffn_phase(const MkArgs& a, const CbMatrix& GU, const CbSliced& D
       row_dot<M>(tu, K, warp, true, glob, xs, uv);
       const float tsg = i < 16 ? ps[i] : GU.tile_scale[j];
       const float tsu = i < 16 ? ps[16 + i] : GU.tile_scale[Fh / kTileRows + j];
+      if (i == 0 && xsl >= 0 && warp < 4) {  // the split slice's rows: warp w takes row w & 1 of gate (w < 2) or up
+        const uint8_t* xt = slot + nst * (2 * tb + dsb) + (warp >> 1) * (K + K / 8);
+        float xv[M];
+        row_dot<M>(xt, K, warp & 1, true, false, xs, xv, 2);
+        const float tsx = ps[32 + (warp >> 1)];
+        if (lane < M && lane < Mr) {
+          float v = 0.0f;
+#pragma unroll
+          for (int mr = 0; mr < M; ++mr)
+            if (mr == lane) v = xv[mr] * tsx * rn[mr];
+          gux[warp * M + lane] = v;
+        }
+      }
+      if (i == 0) mark(a, 1);
       if (lane < M && lane < Mr) {
         float g0 = 0.0f, u0 = 0.0f;
 #pragma unroll
@@ -933,9 +981,26 @@ __device__ void ffn_phase(const MkArgs& a, const CbMatrix& GU, const CbSliced& D
         act[lane * kTileRows + warp] = silu(g0) * u0;
       }
       __syncthreads();
+      const bool with_x = i == 0 && xsl >= 0;
+      float ax[M][2];  // the split slice's two activations per row
+#pragma unroll
+      for (int mr = 0; mr < M; ++mr) {
+        ax[mr][0] = ax[mr][1] = 0.0f;
+        if (with_x && mr < Mr) {
+          ax[mr][0] = silu(gux[mr]) * gux[2 * M + mr];
+          ax[mr][1] = silu(gux[M + mr]) * gux[3 * M + mr];
+        }
+      }
+      const uint8_t* dsx = slot + nst * (2 * tb + dsb) + 2 * (K + K / 8);
 #pragma unroll
       for (int e = 0; e < kNE; ++e) {
         const int n = tid + e * kT;
+        if (n < d && with_x) {
+          const float2 fx = e2m1x2_to_f32x2(dsx[(int64_t)n * 8 + rank]);
+          const float scx = e4m3_to_f32(dsx[(int64_t)d * 8 + n]) * ts_d;
+#pragma unroll
+          for (int mr = 0; mr < M; ++mr) acc[e][mr] = fmaf(fmaf(fx.x, ax[mr][0], fx.y * ax[mr][1]), scx, acc[e][mr]);
+        }
         if (n < d) {
           const uint2 cw = glob ? __ldg(reinterpret_cast<const uint2*>(ds + (int64_t)n * 8))
                                 : *reinterpret_cast<const uint2*>(ds + (int64_t)n * 8);
@@ -959,8 +1024,10 @@ __device__ void ffn_phase(const MkArgs& a, const CbMatrix& GU, const CbSliced& D
         }
       }
       __syncthreads();
+      if (i == 0) mark(a, 2);
     }
   }
+  mark(a, 3);
   if (live && cluster_has) {
 #pragma unroll
     for (int e = 0; e < kNE; ++e) {
@@ -973,9 +1040,9 @@ __device__ void ffn_phase(const MkArgs& a, const CbMatrix& GU, const CbSliced& D
       }
     }
   }
-  mark(a, 1);
+  mark(a, 4);
   cluster_sync();
-  mark(a, 2);
+  mark(a, 5);
   if (live && cluster_has) {
     for (int i = tid; i < Mr * RC; i += kT) {
       const int mr = i / RC, nl = i - mr * RC;
@@ -2078,8 +2145,10 @@ __device__ void phase_params(const MkArgs& a, int kind, int layer, float* work) 
     const CbMatrix& GU = self ? m.self_layers[layer].gate_up : m.cross_layers[layer].gate_up;
     const CbSliced& D = self ? m.self_layers[layer].down_ks : m.cross_layers[layer].down_ks;
     const float* norm2 = self ? m.self_layers[layer].norm2 : m.cross_layers[layer].norm2;
-    const int n = min(ffn_mine(m.ffn_hidden, blockIdx.x, gridDim.x), 16);
+    const int n = min(ffn_mine(m.ffn_hidden, GU.k, blockIdx.x, gridDim.x), 16);
     if (n == 0) return;
+    const int x = ffn_extra(m.ffn_hidden, GU.k, blockIdx.x, gridDim.x);
+    if (x >= 0 && tid < 2) cp_async4(ps + 32 + tid, GU.tile_scale + (tid == 0 ? x : m.ffn_hidden / kTileRows + x));
     for (int i = tid; i < m.d_model / 4; i += kT) cp_async16(pn + 4 * i, norm2 + 4 * i);
     for (int i = tid; i < n; i += kT) {
       const int j = blockIdx.x + i * gridDim.x;
@@ -2323,8 +2392,8 @@ bool mk_supported(const CbModel& m, const CbCache& c, int T, int nq) {
   }
   // GEMV staging: [M][K] inputs
   if ((size_t)kMkMaxRows * kMkMaxD * sizeof(float) > (size_t)kPreOff) return false;
-  // FFN: [8][M][d/8] partials + [M][d] inputs + [M][16]
-  if ((size_t)kMkMaxRows * (2 * d + 16) * sizeof(float) > (size_t)kPreOff) return false;
+  // FFN: [8][M][d/8] partials + [M][d] inputs + [M][16] + [4][M]
+  if ((size_t)kMkMaxRows * (2 * d + 20) * sizeof(float) > (size_t)kPreOff) return false;
   const int64_t tb = tile_bytes(d);
   for (int i = 0; i < m.n_self_layers; ++i) {
     const CbSelfLayer& L = m.self_layers[i];
