@@ -116,19 +116,25 @@ __device__ __forceinline__ void raise_abort(const MkArgs& a) {
 // Work that does not depend on the other CTAs' writes (the next phase's weight
 // copies, recurrent state) goes between the two.  The abort bit in the counter
 // ends every wait at once; grid_wait returns false when the launch is aborted.
+// The barrier is taken by lane 0 of the last warp, so that warp 0 can issue the
+// next phase's weight copies while the arrival drains this CTA's writes.
+constexpr int kBarThread = kT - 32;
+
 __device__ __forceinline__ void grid_arrive(const MkArgs& a, unsigned& gen) {
   __syncthreads();
   gen += 1;
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == kBarThread) {
     if (blockIdx.x == 0 && 2 * gen < (unsigned)kMkTrace) a.trace[2 * gen - 1] = gtimer();
-    __threadfence();
+    // a release add at GPU scope: the CTA's writes (ordered before it by the
+    // CTA barrier) are visible to every CTA that acquires the count
     // the test hook leaves this barrier one arrival short, so every wait on it runs out
-    if (!(blockIdx.x == 0 && gen == s_stall_barrier)) atomicAdd(a.sync, 1u);
+    if (!(blockIdx.x == 0 && gen == s_stall_barrier))
+      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.sync) : "memory");
   }
 }
 
 __device__ __forceinline__ bool grid_wait(const MkArgs& a, unsigned gen, int* s_ok) {
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == kBarThread) {
     const unsigned target = gen * gridDim.x;
     int ok = 1;
     const unsigned long long t0 = gtimer();
@@ -542,7 +548,7 @@ __device__ __forceinline__ int gdn_channel(const GdnGeo& g, int h, int c) {
 // are written by the cluster's CTAs; the preload region is written only by
 // this CTA, before the barrier that starts the phase).
 struct GdnSmem {
-  float *hp, *ssq, *red, *xs, *qk, *vv, *og, *rs, *pv, *gb, *pconv_w, *pconv_s;
+  float *hp, *ssq, *red, *xs, *qk, *vv, *og, *rs, *pv, *gb, *stb, *pconv_w, *pconv_s;
 };
 __host__ __device__ inline int pad4(int n) { return (n + 3) & ~3; }  // floats to a 16-byte multiple
 
@@ -559,13 +565,15 @@ __device__ __forceinline__ GdnSmem gdn_smem(float* work, const GdnGeo& g) {
   s.rs = s.og + pad4(M * g.vpr);        // [kT] reduction scratch
   s.pv = s.rs + kT;                     // [kW]
   s.gb = s.pv + kW;                     // [M][2] decay log, beta
+  s.stb = s.gb + pad4(M * 2);           // [M][kT] state columns copied before the barrier
   s.pconv_w = work + kPreOff / 4 + kParConv;  // [NC][4] conv taps (parameter region)
   s.pconv_s = s.pconv_w + g.NC * 4;     // [B][3][NC] conv window
   return s;
 }
 
-// Before the barrier: this rank's state columns into registers and its conv
-// taps / conv window into the preload region (they do not depend on the step).
+// Before the barrier: this rank's state columns into the work area (read into
+// registers once the phase starts) and its conv taps / conv window into the
+// preload region; all by cp.async (they do not depend on the step).
 template <int M>
 __device__ __forceinline__ void gdn_preload(const MkArgs& a, const CbSelfLayer& L, int h, int rank, float (&st)[M],
                             float* work) {
@@ -577,10 +585,9 @@ __device__ __forceinline__ void gdn_preload(const MkArgs& a, const CbSelfLayer& 
   const int k = tid / g.vpr, v = tid - k * g.vpr;
 #pragma unroll
   for (int b = 0; b < M; ++b) {
-    st[b] = 0.0f;
     if (b < a.B && holds) {
       const int64_t slot = (int64_t)b * a.c.n_gdn + L.slot;
-      st[b] = __ldcg(a.c.gdn_state + ((slot * g.H + h) * g.Dk + k) * g.Dv + g.v0 + v);
+      cp_async4(s.stb + b * kT + tid, a.c.gdn_state + ((slot * g.H + h) * g.Dk + k) * g.Dv + g.v0 + v);
     }
   }
   // norm vector, tile scales of this rank's tiles, gate constants, tensor scale, o_norm columns
@@ -653,6 +660,8 @@ __device__ __forceinline__ void gdn_phase(const MkArgs& a, const CbSelfLayer& L,
   const int B = a.B, T = a.T, Mr = B * T, d = g.d, K = L.in_proj.k, C = 2 * g.H * g.Dk + g.H * g.Dv;
   const int64_t tb = tile_bytes(K);
   const bool snap = a.c.snap_state != nullptr && a.c.snap_conv != nullptr && T > 1;
+#pragma unroll
+  for (int b = 0; b < M; ++b) st[b] = (b < B && tid < g.Dk * g.vpr) ? s.stb[b * kT + tid] : 0.0f;
   if (live) {
     __shared__ int s_rows[kMkMaxRows];
     if (tid < kMkMaxRows) s_rows[tid] = tid;
@@ -1514,7 +1523,12 @@ __device__ __forceinline__ HeadSmem<M> head_smem(float* work, const HeadGeo& e) 
 }
 
 // The phase's rows and key segments (per CTA; kept from the preload to the phase).
-__shared__ int h_pos[kMkMaxRows], h_seq[kMkMaxRows], h_n[kMkMaxRows];
+// The first cross layer's plan is kept for the later ones (same rows, same
+// selections): g_cross_ready marks it, g_keys holds this rank's selected key
+// indices.  s_self_pos: positions of the self-decoder rows, read at launch start.
+constexpr int kHeadKeys = 512;
+__shared__ int h_pos[kMkMaxRows], h_seq[kMkMaxRows], h_n[kMkMaxRows], s_self_pos[kMkMaxRows];
+__shared__ int g_keys[kHeadKeys], g_nkeys, g_cross_ready;
 __shared__ int g_lo[kMkMaxRows], g_n[kMkMaxRows], g_c0[kMkMaxRows], g_s0[kMkMaxRows], g_b[kMkMaxRows],
     g_row[kMkMaxRows], g_p0[kMkMaxRows];
 __shared__ int g_nseg, g_tot, g_nbuf;
@@ -1526,7 +1540,7 @@ __device__ __forceinline__ void head_rows(const MkArgs& a, bool swa, int Mr) {
     int b, t, p, n = 0;
     if (swa) {
       b = r / a.T;
-      p = a.c.pos[b] + a.c0 + (r - b * a.T);
+      p = s_self_pos[r];
     } else {
       query_row(a, r, b, t, p, n);
       if (a.m.sparse_topk > 0) n = min(__ldcg(a.sel_cnt + r), a.sel_ld);
@@ -1600,7 +1614,7 @@ __device__ __forceinline__ int head_key(const MkArgs& a, const HeadGeo& e, bool 
   }
   kp = 0;
   if (need_src) {
-    kp = a.m.sparse_topk > 0 ? __ldcg(a.sel_idx + (int64_t)g_row[s] * a.sel_ld + li) : li;
+    kp = a.m.sparse_topk == 0 ? li : i < g_nkeys ? g_keys[i] : __ldcg(a.sel_idx + (int64_t)g_row[s] * a.sel_ld + li);
     const int64_t off = (((int64_t)b * c.max_ctx + kp) * Hkv + e.g) * hd;
     ks = c.kv_k + off;
     vs = c.kv_v + off;
@@ -1626,13 +1640,29 @@ __device__ void head_prefetch(const MkArgs& a, const HeadGeo& e, bool swa, int l
 template <int M>
 __device__ void head_plan(const MkArgs& a, const HeadGeo& e, bool swa, int layer, int rank, float* work) {
   const int Mr = swa ? a.B * a.T : a.B * a.nq;
-  head_rows(a, swa, Mr);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    head_segments(a, swa, 0, min(HeadSmem<M>::QG, Mr), rank);
-    g_nbuf = min(g_tot, head_smem<M>(work, e).nbuf_max);
+  if (swa || !g_cross_ready) {
+    head_rows(a, swa, Mr);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      head_segments(a, swa, 0, min(HeadSmem<M>::QG, Mr), rank);
+      g_nbuf = min(g_tot, head_smem<M>(work, e).nbuf_max);
+    }
+    __syncthreads();
+    if (!swa && Mr <= HeadSmem<M>::QG) {  // one pass: keep the plan and this rank's keys for the later layers
+      const int nk = a.m.sparse_topk > 0 ? min(g_tot, kHeadKeys) : 0;
+      for (int i = threadIdx.x; i < nk; i += kT) {
+        int s = 0;
+        while (s + 1 < g_nseg && i >= g_c0[s + 1]) ++s;
+        g_keys[i] = __ldcg(a.sel_idx + (int64_t)g_row[s] * a.sel_ld + g_s0[s] + (i - g_c0[s]));
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        g_nkeys = nk;
+        g_cross_ready = 1;
+      }
+      __syncthreads();
+    }
   }
-  __syncthreads();
   head_prefetch(a, e, swa, layer, head_smem<M>(work, e).kvb, g_nbuf);
 }
 
@@ -2217,8 +2247,11 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     const int stall = __ldcg(&a.ctl->stall_barrier);
     s_stall_barrier = stall > 0 ? (unsigned)stall : 0u;
     s_live = 1;
+    g_nkeys = 0;
+    g_cross_ready = 0;
     if (cta == 0) a.trace[0] = gtimer();
   }
+  if (tid < Mrows) s_self_pos[tid] = a.c.pos[tid / a.T] + a.c0 + tid % a.T;
   if (cta == 0) {
     // the histogram exists only with a top-k (dense cross attention carves it empty)
     if (m.sparse_topk > 0)
@@ -2411,7 +2444,8 @@ bool mk_supported(const CbModel& m, const CbCache& c, int T, int nq) {
       // GDN working memory before the preload region; conv taps and windows after it
       const size_t w = sizeof(float) * ((size_t)kMkMaxRows * (2 * Dk + 2 * Dv + 2) + kCl * kMkMaxRows +
                                         (size_t)kMkMaxRows * 2 * d + (size_t)kMkMaxRows * (2 * Dk + 2 * vpr) +
-                                        kT + kW + 2 * kMkMaxRows + 32);  // + 16-byte padding of each array
+                                        kT + kW + 2 * kMkMaxRows + (size_t)kMkMaxRows * kT +
+                                        36);  // + 16-byte padding of each array
       const size_t pre = sizeof(float) * ((size_t)kParConv + (size_t)(2 * Dk + vpr) * (4 + 3 * c.batch));
       if (w > (size_t)kPreOff || pre > (size_t)(kWork - kPreOff) || vpr > 16) return false;
     }
