@@ -116,9 +116,11 @@ __device__ __forceinline__ void raise_abort(const MkArgs& a) {
 // Work that does not depend on the other CTAs' writes (the next phase's weight
 // copies, recurrent state) goes between the two.  The abort bit in the counter
 // ends every wait at once; grid_wait returns false when the launch is aborted.
-// The barrier is taken by lane 0 of the last warp, so that warp 0 can issue the
-// next phase's weight copies while the arrival drains this CTA's writes.
+// The barrier is taken by lane 0 of the last warp and the weight copies are
+// issued by another warp, so that neither waits for the arrival to drain this
+// CTA's writes.
 constexpr int kBarThread = kT - 32;
+constexpr int kCopyWarp = kW - 2;  // issues the weight copies (warp 0 carries the most preload work)
 
 __device__ __forceinline__ void grid_arrive(const MkArgs& a, unsigned& gen) {
   __syncthreads();
@@ -229,6 +231,9 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Every committed group but the most recent one complete.
+__device__ __forceinline__ void cp_async_wait_prior() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 // ------------------------------------------------------------------ fixed point
 __device__ __forceinline__ float from_fix(long long q) { return __ll2float_rn(q) * kFixInv; }
@@ -583,14 +588,7 @@ __device__ __forceinline__ void gdn_preload(const MkArgs& a, const CbSelfLayer& 
   const int tid = threadIdx.x, C = 2 * g.H * g.Dk + g.H * g.Dv;
   const bool holds = tid < g.Dk * g.vpr;
   const int k = tid / g.vpr, v = tid - k * g.vpr;
-#pragma unroll
-  for (int b = 0; b < M; ++b) {
-    if (b < a.B && holds) {
-      const int64_t slot = (int64_t)b * a.c.n_gdn + L.slot;
-      cp_async4(s.stb + b * kT + tid, a.c.gdn_state + ((slot * g.H + h) * g.Dk + k) * g.Dv + g.v0 + v);
-    }
-  }
-  // norm vector, tile scales of this rank's tiles, gate constants, tensor scale, o_norm columns
+  // first group (needed as the phase starts): norm vector, tile scales of this rank's tiles
   float* pn = par_norm(work);
   float* ps = par_small(work);
   for (int i = tid; i < m.d_model / 4; i += kT) cp_async16(pn + 4 * i, L.norm1 + 4 * i);
@@ -604,6 +602,18 @@ __device__ __forceinline__ void gdn_preload(const MkArgs& a, const CbSelfLayer& 
       cp_async4(ps + 16, L.in_proj.tile_scale + (m.gdn_off_a + h) / kTileRows);
       cp_async4(ps + 17, L.in_proj.tile_scale + (m.gdn_off_b + h) / kTileRows);
     }
+  }
+  cp_async_commit();
+  // second group (needed after the in-projection): state columns, gate constants,
+  // tensor scale, o_norm columns, conv taps and window
+#pragma unroll
+  for (int b = 0; b < M; ++b) {
+    if (b < a.B && holds) {
+      const int64_t slot = (int64_t)b * a.c.n_gdn + L.slot;
+      cp_async4(s.stb + b * kT + tid, a.c.gdn_state + ((slot * g.H + h) * g.Dk + k) * g.Dv + g.v0 + v);
+    }
+  }
+  if (tid == 0) {
     cp_async4(ps + PS_A_LOG, L.A_log + h);
     cp_async4(ps + PS_DT_BIAS, L.dt_bias + h);
     cp_async4(ps + PS_TSCALE, L.o_proj_ks.tensor_scale);
@@ -615,6 +625,7 @@ __device__ __forceinline__ void gdn_preload(const MkArgs& a, const CbSelfLayer& 
     const int64_t slot = (int64_t)b * a.c.n_gdn + L.slot;
     cp_async4(s.pconv_s + i, a.c.gdn_conv + (slot * 3 + j) * C + gdn_channel(g, h, c));
   }
+  cp_async_commit();
 }
 
 __device__ __forceinline__ int64_t slice_bytes(const CbSliced& S) {
@@ -660,8 +671,6 @@ __device__ __forceinline__ void gdn_phase(const MkArgs& a, const CbSelfLayer& L,
   const int B = a.B, T = a.T, Mr = B * T, d = g.d, K = L.in_proj.k, C = 2 * g.H * g.Dk + g.H * g.Dv;
   const int64_t tb = tile_bytes(K);
   const bool snap = a.c.snap_state != nullptr && a.c.snap_conv != nullptr && T > 1;
-#pragma unroll
-  for (int b = 0; b < M; ++b) st[b] = (b < B && tid < g.Dk * g.vpr) ? s.stb[b * kT + tid] : 0.0f;
   if (live) {
     __shared__ int s_rows[kMkMaxRows];
     if (tid < kMkMaxRows) s_rows[tid] = tid;
@@ -702,8 +711,11 @@ __device__ __forceinline__ void gdn_phase(const MkArgs& a, const CbSelfLayer& L,
       }
     }
   }
+  cp_async_wait_all();  // the preload's second group (state, conv, constants); the cluster barrier publishes it
   cluster_sync();  // every rank's in-projection rows are in every rank's hp
   mark(a, 1);
+#pragma unroll
+  for (int b = 0; b < M; ++b) st[b] = (b < B && tid < g.Dk * g.vpr) ? s.stb[b * kT + tid] : 0.0f;
   if (live) {
     const float* ps = par_small(work);
     // short conv (4 taps) on q, k and this rank's v channels; the new window goes back to the cache
@@ -1688,6 +1700,7 @@ __device__ void head_preload(const MkArgs& a, bool swa, int layer, int h, int ra
       cp_async4(ps + q, W.tile_scale + head_tile(m, e, h, j, hp_off));
     }
   }
+  cp_async_commit();  // the first group: what the in-projection needs; the rest is waited after it
   const int n0 = rank * e.RC, t0 = n0 / kTileRows, nt = (n0 + e.RC - 1) / kTileRows - t0 + 1;
   for (int i = tid; i < nt; i += kT) cp_async4(ps + kHeadOTs + i, O.tile_scale + t0 + i);
   float* pq = work + kPreOff / 4 + kParHeadQn;
@@ -1709,6 +1722,7 @@ __device__ void head_preload(const MkArgs& a, bool swa, int layer, int h, int ra
     cp_async4(ob + row * e.os + wd * 4, src);
   }
   if (swa || layer > 0) head_plan<M>(a, e, swa, layer, rank, work);
+  cp_async_commit();
 }
 
 // RMSNorm over hd (weights w) + partial interleaved RoPE at position p of a
@@ -1811,6 +1825,7 @@ __device__ void head_phase(const MkArgs& a, bool swa, int layer, bool first, boo
       off += (int)tb;
     }
   }
+  cp_async_wait_all();  // the preload's second group; the cluster barrier publishes it
   cluster_sync();  // every rank's in-projection rows are in every rank's hp
   mark(a, 1);
   if (live) {
@@ -2192,7 +2207,7 @@ __device__ void phase_params(const MkArgs& a, int kind, int layer, float* work) 
   }
 }
 
-// Warp 0: arm the slot's mbarrier with the phase's byte count and start its copies.
+// The copy warp: arm the slot's mbarrier with the phase's byte count and start its copies.
 __device__ void stage_issue(const MkArgs& a, int kind, int layer, uint8_t* slot, unsigned long long* bar) {
   const int lane = threadIdx.x & 31;
   unsigned total = 0;
@@ -2207,7 +2222,7 @@ __device__ void stage_issue(const MkArgs& a, int kind, int layer, uint8_t* slot,
   });
 }
 
-// Warp 0, last phase only: the GEMV tiles after the staged ones into the other slot.
+// The copy warp, last phase only: the GEMV tiles after the staged ones into the other slot.
 __device__ void stage_issue_extra(const MkArgs& a, int kind, int layer, uint8_t* slot, unsigned long long* bar) {
   const int lane = threadIdx.x & 31;
   const GemvJob g = gemv_job(a, kind, layer);
@@ -2267,7 +2282,7 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
   // bulk-copy phases issued and waited per slot (uniform in the CTA)
   unsigned issued0 = 0u, issued1 = 0u, waited0 = 0u, waited1 = 0u;
   const int P = s_np;
-  if (warp == 0) stage_issue(a, s_plan[0] >> 8, s_plan[0] & 0xFF, smem, &s_bar[0]);
+  if (warp == kCopyWarp) stage_issue(a, s_plan[0] >> 8, s_plan[0] & 0xFF, smem, &s_bar[0]);
   issued0 = 1;
   grid_arrive(a, gen);
   bool live = true;
@@ -2276,13 +2291,14 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
     const int kind = s_plan[p] >> 8, layer = s_plan[p] & 0xFF, sl = p & 1;
     int nst2 = 0;  // tiles of this phase in the other slot (last phase only)
     if (live && p + 1 < P) {  // the next phase's weights, into the other slot
-      if (warp == 0) stage_issue(a, s_plan[p + 1] >> 8, s_plan[p + 1] & 0xFF, smem + (sl ^ 1) * kSlot, &s_bar[sl ^ 1]);
+      if (warp == kCopyWarp)
+        stage_issue(a, s_plan[p + 1] >> 8, s_plan[p + 1] & 0xFF, smem + (sl ^ 1) * kSlot, &s_bar[sl ^ 1]);
       if (sl) issued0 += 1;
       else issued1 += 1;
     } else if (live && is_gemv(kind)) {  // the last phase: its later tiles into the free slot
       nst2 = gemv_extra(gemv_job(a, kind, layer));
       if (nst2 > 0) {
-        if (warp == 0) stage_issue_extra(a, kind, layer, smem + (sl ^ 1) * kSlot, &s_bar[sl ^ 1]);
+        if (warp == kCopyWarp) stage_issue_extra(a, kind, layer, smem + (sl ^ 1) * kSlot, &s_bar[sl ^ 1]);
         if (sl) issued0 += 1;
         else issued1 += 1;
       }
@@ -2295,7 +2311,9 @@ __global__ void __launch_bounds__(kMkThreads, 1) decode_mk_kernel(const __grid_c
       else phase_params<M>(a, kind, layer, work);
     }
     live = grid_wait(a, gen, &s_ok) && live;
-    cp_async_wait_all();  // this phase's parameters
+    // this phase's parameters (GDN and attention phases: the first of their two groups)
+    if (gdn_here || ((kind == PH_SWA_HEAD || kind == PH_CR_HEAD) && cid < m.n_q_heads)) cp_async_wait_prior();
+    else cp_async_wait_all();
     __syncthreads();
     const unsigned iss = sl ? issued1 : issued0, wtd = sl ? waited1 : waited0;
     if (live && iss > wtd) {
