@@ -1325,7 +1325,7 @@ __device__ void resolve_row(const MkArgs& a, int r, float* smem) {
   }
   __shared__ unsigned hist256[256];
   __shared__ unsigned wsum[32], s_total;
-  __shared__ int s_digit, s_rem;
+  __shared__ int s_digit, s_rem, s_done;
   unsigned* bits = reinterpret_cast<unsigned*>(smem);  // [kMkBitmapWords]
   unsigned long long* cs = reinterpret_cast<unsigned long long*>(smem) + kMkBitmapWords / 2;
   const int cap = (kPreOff - kMkBitmapWords * (int)sizeof(unsigned)) / (int)sizeof(unsigned long long);
@@ -1342,6 +1342,7 @@ __device__ void resolve_row(const MkArgs& a, int r, float* smem) {
     cand = cs;
   }
   __syncthreads();
+  mark(a, 0);
 #pragma unroll 2
   for (int i = tid; i < above; i += kT) {
     const int j = __ldcg(a.hi_list + (int64_t)r * k + i);
@@ -1349,8 +1350,11 @@ __device__ void resolve_row(const MkArgs& a, int r, float* smem) {
   }
   unsigned long long prefix = 0ull, pmask = 0ull;
   int remaining = need;
+  // radix select of the need-th largest candidate; it stops as soon as the chosen
+  // digit's bucket holds exactly the remaining count (then every candidate with
+  // the prefix so far is selected: the threshold is the prefix with zero low bits)
 #pragma unroll 1
-  for (int ps = 0; ps < 7; ++ps) {  // digits of 8 bits from bit 45 down, then the low 5 bits
+  for (int ps = 0; ps < 7 && nc > need; ++ps) {  // digits of 8 bits from bit 45 down, then the low 5 bits
     const int shift = ps < 6 ? 45 - 8 * ps : 0;
     const unsigned dm = ps < 6 ? 0xFFu : 0x1Fu;
     for (int i = tid; i < 256; i += kT) hist256[i] = 0u;
@@ -1380,6 +1384,7 @@ __device__ void resolve_row(const MkArgs& a, int r, float* smem) {
           if (cum + c8[i] >= (unsigned)remaining) {
             s_digit = 255 - 8 * lane - i;
             s_rem = remaining - (int)cum;
+            s_done = c8[i] == (unsigned)(remaining - (int)cum);
             break;
           }
           cum += c8[i];
@@ -1390,8 +1395,11 @@ __device__ void resolve_row(const MkArgs& a, int r, float* smem) {
     prefix |= (unsigned long long)s_digit << shift;
     pmask |= (unsigned long long)dm << shift;
     remaining = s_rem;
+    const bool done = s_done != 0;
     __syncthreads();
+    if (done) break;
   }
+  mark(a, 1);
   // candidates at or above the need-th largest (low 53 bits; the top 11 are equal)
   const unsigned long long thr = prefix;
   const unsigned long long low = (1ull << 53) - 1;
@@ -1404,6 +1412,7 @@ __device__ void resolve_row(const MkArgs& a, int r, float* smem) {
   }
   if (tid == 0) atomicOr(&bits[p >> 5], 1u << (p & 31));  // the diagonal
   __syncthreads();
+  mark(a, 2);
   // ascending output: thread tid owns words [tid * wpt, (tid + 1) * wpt)
   const int wpt = (nw + kT - 1) / kT;
   unsigned cnt = 0;
