@@ -242,6 +242,13 @@ __device__ __forceinline__ void red_fix(long long* p, float v) {
   asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(q) : "memory");
 }
 
+// ------------------------------------------------------------------ staged inputs
+// A staged input row of K floats keeps 16 bytes of padding after every 32
+// floats: the 8-float chunks that lanes 0-7 of a warp read with 128-bit loads
+// (chunks 32 bytes apart) then fall on 32 distinct banks.
+__host__ __device__ inline int xpad(int K) { return K + K / 8; }           // floats per staged row
+__host__ __device__ inline int xoff(int k) { return k + (k >> 5) * 4; }    // position of element k in its row
+
 // ------------------------------------------------------------------ weight rows
 // One weight row as seen by one lane: the 8-code chunks lane, lane+32, ...
 // (K <= 2048, so at most 8 chunks), code words and scale bytes.
@@ -286,8 +293,9 @@ __device__ __forceinline__ void dot_row(const RowW<NU>& r, int K, const float* x
       for (int j = 0; j < 4; ++j) f[j] = e2m1x2_to_f32x2(r.w[u] >> (8 * j));
 #pragma unroll
       for (int m = 0; m < M; ++m) {
-        const float4 x0 = *reinterpret_cast<const float4*>(xs + m * K + c * 8);
-        const float4 x1 = *reinterpret_cast<const float4*>(xs + m * K + c * 8 + 4);
+        const float* xc = xs + m * xpad(K) + xoff(c * 8);
+        const float4 x0 = *reinterpret_cast<const float4*>(xc);
+        const float4 x1 = *reinterpret_cast<const float4*>(xc + 4);
         float p = f[0].x * x0.x;
         p = fmaf(f[0].y, x0.y, p);
         p = fmaf(f[1].x, x0.z, p);
@@ -327,10 +335,11 @@ __device__ __forceinline__ unsigned long long pack_argmax(float v, int idx) {
 }
 
 // ------------------------------------------------------------------ RMSNorm staging
-// xs[m][k] = x[m][k] * norm_w[k] for m < m_rows (zeros above); rn[m] receives
-// the RMSNorm factor of each row (1 when norm_w is null).  x comes from a
-// fixed-point residual row (xq, row rowmap[m]), float rows (x) or the token
-// embeddings (embed_from).  The sums of squares are reduced in a fixed order.
+// xs[m][xoff(k)] = x[m][k] * norm_w[k] (rows xpad(K) floats apart) for m < m_rows
+// (zeros above); rn[m] receives the RMSNorm factor of each row (1 when norm_w is
+// null).  x comes from a fixed-point residual row (xq, row rowmap[m]), float rows
+// (x) or the token embeddings (embed_from).  The sums of squares are reduced in a
+// fixed order.
 template <int M>
 __device__ void stage_rows(const long long* xq, const float* x, int ldx, const int* rowmap, int m_rows, int K,
                            const float* norm_w, float eps, float* xs, float (&rn)[M], long long* copy_q,
@@ -377,7 +386,7 @@ __device__ void stage_rows(const long long* xq, const float* x, int ldx, const i
         if (q == mr) sq[q] += v * v;
       v *= norm_w[k];
     }
-    xs[i] = v;
+    xs[mr * xpad(K) + xoff(k)] = v;
   }
   if (norm) {
 #pragma unroll
@@ -439,7 +448,7 @@ __device__ void gemv_phase(const MkArgs& a, const GemvJob& g, int m_rows, const 
   const int K = g.W.k, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t tb = tile_bytes(K);
   const int nst = gemv_staged(g);
-  float* xs = work;  // [M][K]
+  float* xs = work;  // [M][xpad(K)]
   __shared__ unsigned long long s_best[kMkMaxRows];
   __shared__ int s_rowmap[kMkMaxRows];
   if (g.argmax && tid < kMkMaxRows) s_best[tid] = 0ull;
@@ -560,8 +569,8 @@ __host__ __device__ inline int pad4(int n) { return (n + 3) & ~3; }  // floats t
 template <int M>
 __device__ __forceinline__ GdnSmem gdn_smem(float* work, const GdnGeo& g) {
   GdnSmem s;  // every array starts on a 16-byte boundary (xs is read as float4)
-  s.xs = work;                          // [M][d]
-  s.hp = s.xs + pad4(M * g.d);          // [M][HP]
+  s.xs = work;                          // [M][xpad(d)]
+  s.hp = s.xs + pad4(M * xpad(g.d));    // [M][HP]
   s.ssq = s.hp + pad4(M * g.HP);        // [kCl][M]
   s.red = s.ssq + pad4(kCl * M);        // [kCl][M][RC]
   s.qk = s.red + pad4(kCl * M * g.RC);  // [M][2 Dk]
@@ -942,8 +951,8 @@ __device__ __forceinline__ void ffn_phase(const MkArgs& a, const CbMatrix& GU, c
   const int d = m.d_model, Fh = m.ffn_hidden, RC = d / kCl, K = GU.k;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, cta = blockIdx.x, ncta = gridDim.x;
   float* red = work;                   // [kCl][M][RC]  (written by the cluster's CTAs)
-  float* xs = red + kCl * M * RC;      // [M][d]
-  float* act = xs + M * d;             // [M][16]
+  float* xs = red + kCl * M * RC;      // [M][xpad(d)]
+  float* act = xs + M * xpad(d);       // [M][16]
   float* gux = act + M * kTileRows;    // [4][M] split slice: gate 2r, gate 2r + 1, up 2r, up 2r + 1
   constexpr int kNE = (kMkMaxD + kT - 1) / kT;  // outputs per thread
   float acc[kNE][M];
@@ -1528,14 +1537,14 @@ template <int M>
 __device__ __forceinline__ HeadSmem<M> head_smem(float* work, const HeadGeo& e) {
   HeadSmem<M> s;
   const int hd = e.hd;
-  s.xs = work;                                               // [M][d]
+  s.xs = work;                                               // [M][xpad(d)]
   s.qs = work;                                               // [M][hd] scaled queries
   s.kc = reinterpret_cast<uint16_t*>(s.qs + M * hd);         // [M][hd] this step's keys (bf16)
   s.vc = s.kc + M * hd;                                      // [M][hd] this step's values (bf16)
   s.og = s.qs + 2 * M * hd;                                  // [M][hd] gated head output
   s.wpart = s.og + M * hd;                                   // [kW][QG][hd + 2] warp partials
   const int over = pad4(3 * M * hd + kW * HeadSmem<M>::QG * (hd + 2));
-  s.hp = work + max(pad4(M * e.d), over);                    // [M][HP]
+  s.hp = work + max(pad4(M * xpad(e.d)), over);             // [M][HP]
   s.part = s.hp + pad4(M * e.HP);                            // [M][hd + 2] this CTA's partial per row
   const int used = (int)(s.part - work) + pad4(M * (hd + 2));
   s.nbuf_max = max(0, (kPreOff / 4 - used) / hd);            // a key row pair is hd floats
@@ -2444,16 +2453,16 @@ bool mk_supported(const CbModel& m, const CbCache& c, int T, int nq) {
   if (hd % 16 || 32 % (hd / 8) || d % kCl || (m.n_q_heads * hd) % 64 || m.rot_dim / 2 > 64) return false;
   {
     const int HP = 3 * hd + 1, QGm = 5;
-    const size_t w = sizeof(float) * ((size_t)std::max(pad4(kMkMaxRows * d),
+    const size_t w = sizeof(float) * ((size_t)std::max(pad4(kMkMaxRows * xpad(d)),
                                                        pad4(3 * kMkMaxRows * hd + kW * QGm * (hd + 2))) +
                                       pad4(kMkMaxRows * HP) + (size_t)kMkMaxRows * (hd + 2));
     if (w > (size_t)kPreOff) return false;
     if ((int64_t)ceil_div(3 * hd / kTileRows + 1, kCl) * tile_bytes(d) > kSlot) return false;
   }
-  // GEMV staging: [M][K] inputs
-  if ((size_t)kMkMaxRows * kMkMaxD * sizeof(float) > (size_t)kPreOff) return false;
-  // FFN: [8][M][d/8] partials + [M][d] inputs + [M][16] + [4][M]
-  if ((size_t)kMkMaxRows * (2 * d + 20) * sizeof(float) > (size_t)kPreOff) return false;
+  // GEMV staging: [M][xpad(K)] inputs
+  if ((size_t)kMkMaxRows * xpad(kMkMaxD) * sizeof(float) > (size_t)kPreOff) return false;
+  // FFN: [8][M][d/8] partials + [M][xpad(d)] inputs + [M][16] + [4][M]
+  if ((size_t)kMkMaxRows * (d + xpad(d) + 20) * sizeof(float) > (size_t)kPreOff) return false;
   const int64_t tb = tile_bytes(d);
   for (int i = 0; i < m.n_self_layers; ++i) {
     const CbSelfLayer& L = m.self_layers[i];
@@ -2470,7 +2479,7 @@ bool mk_supported(const CbModel& m, const CbCache& c, int T, int nq) {
       if ((int64_t)(ceil_div(ntile, kCl) + 2) * tb + slice > kSlot) return false;
       // GDN working memory before the preload region; conv taps and windows after it
       const size_t w = sizeof(float) * ((size_t)kMkMaxRows * (2 * Dk + 2 * Dv + 2) + kCl * kMkMaxRows +
-                                        (size_t)kMkMaxRows * 2 * d + (size_t)kMkMaxRows * (2 * Dk + 2 * vpr) +
+                                        (size_t)kMkMaxRows * (d + xpad(d)) + (size_t)kMkMaxRows * (2 * Dk + 2 * vpr) +
                                         kT + kW + 2 * kMkMaxRows + (size_t)kMkMaxRows * kT +
                                         36);  // + 16-byte padding of each array
       const size_t pre = sizeof(float) * ((size_t)kParConv + (size_t)(2 * Dk + vpr) * (4 + 3 * c.batch));
