@@ -1186,46 +1186,59 @@ __device__ __forceinline__ void key_range(int n, int cta, int ncta, int& js, int
   je = min(n, js + per);
 }
 
-// Scores of this CTA's key range for every query row + histogram of the top 11 key bits.
+// Scores of this CTA's key range for every query row + histogram of the top 11
+// key bits.  All rows at once: their queries, the chunk's new keys and the
+// histograms are staged together, and the rows' score loops run back to back
+// (a key read for one row is in L1 for the next rows of its sequence).
 __device__ void score_phase(const MkArgs& a, float* smem) {
   const CbModel& m = a.m;
   const CbCache& c = a.c;
-  const int RQ = a.B * a.nq, Hi = m.indexer_heads, Di = m.indexer_dim, k = m.sparse_topk;
+  const int RQ = a.B * a.nq, Hi = m.indexer_heads, Di = m.indexer_dim, k = m.sparse_topk, HD = Hi * Di;
+  const int Mrows = a.B * a.T;
   const int tid = threadIdx.x, cta = blockIdx.x, ncta = gridDim.x;
-  unsigned* hist = reinterpret_cast<unsigned*>(smem);             // [2048]
-  float* q = smem + kMkHistBins;                                   // [Hi*Di]
-  float* w = q + Hi * Di;                                          // [Hi]
-  uint8_t* newk = reinterpret_cast<uint8_t*>(w + 16);              // [8][Di] keys of this chunk's tokens
-  for (int r = 0; r < RQ; ++r) {
+  unsigned* hist = reinterpret_cast<unsigned*>(smem);        // [RQ][2048]
+  float* q = smem + RQ * kMkHistBins;                         // [RQ][Hi * Di]
+  float* w = q + RQ * HD;                                     // [RQ][16]
+  uint8_t* newk = reinterpret_cast<uint8_t*>(w + RQ * 16);    // [Mrows][Di] keys of this chunk's tokens
+  __shared__ int r_b[kMkMaxRows], r_p0[kMkMaxRows], r_js[kMkMaxRows], r_je[kMkMaxRows];
+  if (tid < RQ) {
     int b, t, p, n;
-    query_row(a, r, b, t, p, n);
-    if (n <= k) continue;
-    int js, je;
-    key_range(n, cta, ncta, js, je);
-    if (js >= je) continue;
-    const float* qrow = a.proj + ((int64_t)b * a.T + t) * a.ldp;
-    const int p0 = c.pos[b] + a.c0;
-    for (int i = tid; i < Hi * Di; i += kT) q[i] = __ldcg(qrow + m.sh_off_iq + i);
-    for (int i = tid; i < Hi; i += kT) w[i] = __ldcg(qrow + m.sh_off_iw + i);
-    for (int i = tid; i < a.T * Di; i += kT) {
-      const int t2 = i / Di, dd = i - t2 * Di;
-      newk[i] = f32_to_e4m3(__ldcg(a.proj + ((int64_t)b * a.T + t2) * a.ldp + m.sh_off_ik + dd));
-    }
-    for (int i = tid; i < kMkHistBins; i += kT) hist[i] = 0u;
-    __syncthreads();
+    query_row(a, tid, b, t, p, n);
+    int js = 0, je = 0;
+    if (n > k) key_range(n, cta, ncta, js, je);
+    r_b[tid] = b;
+    r_p0[tid] = c.pos[b] + a.c0;
+    r_js[tid] = js;
+    r_je[tid] = je;
+  }
+  for (int i = tid; i < RQ * HD; i += kT) {
+    const int r = i / HD, e = i - r * HD, b = r / a.nq, t = a.T - a.nq + (r - b * a.nq);
+    q[i] = __ldcg(a.proj + ((int64_t)b * a.T + t) * a.ldp + m.sh_off_iq + e);
+  }
+  for (int i = tid; i < RQ * Hi; i += kT) {
+    const int r = i / Hi, h = i - r * Hi, b = r / a.nq, t = a.T - a.nq + (r - b * a.nq);
+    w[r * 16 + h] = __ldcg(a.proj + ((int64_t)b * a.T + t) * a.ldp + m.sh_off_iw + h);
+  }
+  for (int i = tid; i < Mrows * Di; i += kT) {
+    const int mr = i / Di, dd = i - mr * Di;
+    newk[i] = f32_to_e4m3(__ldcg(a.proj + (int64_t)mr * a.ldp + m.sh_off_ik + dd));
+  }
+  for (int i = tid; i < RQ * kMkHistBins; i += kT) hist[i] = 0u;
+  __syncthreads();
+  for (int r = 0; r < RQ; ++r) {
+    const int js = r_js[r], je = r_je[r], b = r_b[r], p0 = r_p0[r];
     const uint8_t* ikb = c.kv_ik + (int64_t)b * c.max_ctx * Di;
     float* out = a.scores + (int64_t)r * c.max_ctx;
     for (int j = js + tid; j < je; j += kT) {
-      const uint8_t* kr = j < p0 ? ikb + (int64_t)j * Di : newk + (j - p0) * Di;
-      const float sc = indexer_score_bytes(kr, q, w, Hi, Di);
+      const uint8_t* kr = j < p0 ? ikb + (int64_t)j * Di : newk + (b * a.T + (j - p0)) * Di;
+      const float sc = indexer_score_bytes(kr, q + r * HD, w + r * 16, Hi, Di);
       out[j] = sc;
-      atomicAdd(&hist[score_key(sc) >> 21], 1u);
+      atomicAdd(&hist[r * kMkHistBins + (score_key(sc) >> 21)], 1u);
     }
-    __syncthreads();
-    for (int i = tid; i < kMkHistBins; i += kT)
-      if (hist[i]) atomicAdd(&a.hist[(int64_t)r * kMkHistBins + i], hist[i]);
-    __syncthreads();
   }
+  __syncthreads();
+  for (int i = tid; i < RQ * kMkHistBins; i += kT)
+    if (hist[i]) atomicAdd(&a.hist[i], hist[i]);
 }
 
 // Block-wide exclusive prefix sum of one unsigned per thread (kT threads).
@@ -1936,9 +1949,36 @@ __device__ void head_phase(const MkArgs& a, bool swa, int layer, bool first, boo
             vf[2 * x] = bf16_to_f32(vw[x]);
             vf[2 * x + 1] = bf16_to_f32(vw[x] >> 16);
           }
+          if constexpr (QG == 1) {  // one query row
 #pragma unroll
-          for (int j = 0; j < QG; ++j) {
-            if (j < nq) {
+            for (int j = 0; j < QG; ++j) {
+              if (j < nq) {
+                const float4 q0 = *reinterpret_cast<const float4*>(qs + (r0 + j) * hd + sub * 8);
+                const float4 q1 = *reinterpret_cast<const float4*>(qs + (r0 + j) * hd + sub * 8 + 4);
+                float sc = q0.x * kf[0];
+                sc = fmaf(q0.y, kf[1], sc);
+                sc = fmaf(q0.z, kf[2], sc);
+                sc = fmaf(q0.w, kf[3], sc);
+                sc = fmaf(q1.x, kf[4], sc);
+                sc = fmaf(q1.y, kf[5], sc);
+                sc = fmaf(q1.z, kf[6], sc);
+                sc = fmaf(q1.w, kf[7], sc);
+                for (int x = LK / 2; x > 0; x >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, x);
+                const int s = kseg[u];
+                bool ok = s >= 0;
+                if (ok) {
+                  if (swa) {
+                    const int pj = h_pos[r0 + j];
+                    ok = g_b[s] == h_seq[r0 + j] && kpos[u] <= pj && kpos[u] > pj - m.swa_window;
+                  } else {
+                    ok = g_row[s] == r0 + j;
+                  }
+                }
+                if (ok) soft_update(sc, vf, mq[j], lq[j], o[j]);
+              }
+            }
+          } else {
+            auto score = [&](int j) {  // this lane's part of q_j . k, reduced over the key group
               const float4 q0 = *reinterpret_cast<const float4*>(qs + (r0 + j) * hd + sub * 8);
               const float4 q1 = *reinterpret_cast<const float4*>(qs + (r0 + j) * hd + sub * 8 + 4);
               float sc = q0.x * kf[0];
@@ -1950,17 +1990,25 @@ __device__ void head_phase(const MkArgs& a, bool swa, int layer, bool first, boo
               sc = fmaf(q1.z, kf[6], sc);
               sc = fmaf(q1.w, kf[7], sc);
               for (int x = LK / 2; x > 0; x >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, x);
-              const int s = kseg[u];
-              bool ok = s >= 0;
-              if (ok) {
-                if (swa) {
+              return sc;
+            };
+            const int s = kseg[u];
+            if (swa) {  // every query of the pass may see the key (window and causal masks)
+#pragma unroll
+              for (int j = 0; j < QG; ++j) {
+                if (j < nq) {
+                  const float sc = score(j);
                   const int pj = h_pos[r0 + j];
-                  ok = g_b[s] == h_seq[r0 + j] && kpos[u] <= pj && kpos[u] > pj - m.swa_window;
-                } else {
-                  ok = g_row[s] == r0 + j;
+                  if (s >= 0 && g_b[s] == h_seq[r0 + j] && kpos[u] <= pj && kpos[u] > pj - m.swa_window)
+                    soft_update(sc, vf, mq[j], lq[j], o[j]);
                 }
               }
-              if (ok) soft_update(sc, vf, mq[j], lq[j], o[j]);
+            } else {  // a selected key belongs to one query row: score it against that row only
+              const int jr = s >= 0 ? g_row[s] - r0 : 0;
+              const float sc = score(jr);
+#pragma unroll
+              for (int j = 0; j < QG; ++j)
+                if (s >= 0 && j == jr) soft_update(sc, vf, mq[j], lq[j], o[j]);
             }
           }
         }
@@ -2444,8 +2492,9 @@ bool mk_supported(const CbModel& m, const CbCache& c, int T, int nq) {
   if (m.conv_size != 4) return false;
   if (m.sparse_topk > 0 && c.max_ctx > kMkBitmapWords * 32) return false;
   if (m.sparse_topk > 0 && (m.sparse_topk + 1 > kMaxSort || m.indexer_dim % 8 || m.indexer_dim > 256 ||
-                            m.indexer_heads > 16 || (m.indexer_heads * m.indexer_dim + 16 + kMkHistBins) * 4 +
-                            CB_MAX_T * m.indexer_dim > kWork))
+                            m.indexer_heads > 16 ||
+                            kMkMaxRows * (m.indexer_heads * m.indexer_dim + 16 + kMkHistBins) * 4 +
+                                    kMkMaxRows * m.indexer_dim > kPreOff))
     return false;
   // attention phases (a cluster per query head): hd / 8 lanes per key, 16-row
   // tiles of q / k / v, the o-projection's column block of each head on 4-byte words
