@@ -61,8 +61,8 @@ METRIC = "decode tok/s (batch 1, τ=1, 32K ctx) per B200 + HBM GB/s vs 8 TB/s; b
 # from an ncu capture (dram__bytes_read.sum + dram__bytes_write.sum), and the
 # SHA-256 prefix of the kernel source it was captured from: a changed source
 # reports traffic null until it is captured again.
-STEP_TRAFFIC = {"bytes": 95_876_864 + 4_303_872, "source": "cirrus_s_1a_b200/csrc/decode_mk.cu",
-                "sha256_16": "121c5fa1348d0c06"}
+STEP_TRAFFIC = {"bytes": 95_820_800 + 3_996_416, "source": "cirrus_s_1a_b200/csrc/decode_mk.cu",
+                "sha256_16": "e152670d4e85d71d"}
 CPU_ARM_WHY = ("the reference is a Python package that cannot travel to the GPU box, so the CPU arm runs the "
                "oracle: the reference forward restated operation by operation (oracle/model.py), checked against "
                "fixtures generated from the reference itself (tests/golden), with the B200 storage casts")

@@ -1804,7 +1804,7 @@ template <int M>
 __device__ void head_phase(const MkArgs& a, bool swa, int layer, bool first, bool live, int h, int rank,
                            const uint8_t* slot, float* work) {
   constexpr int QG = HeadSmem<M>::QG;
-  constexpr int KU = QG == 1 ? 4 : 2;  // keys per key group in flight
+  constexpr int KU = QG == 1 ? 1 : 2;  // keys per key group in flight (one row: a compact loop)
   const CbModel& m = a.m;
   const CbCache& c = a.c;
   const HeadGeo e = head_geo(m, swa, h);
