@@ -426,6 +426,27 @@ def prefill_bench(eng, dev, stream) -> dict:
             "runs": out}
 
 
+def profile_stream(M: int) -> None:
+    """The one-launch weight stream (cb_weight_stream_nvfp4) over the model's 78
+    projections with M input rows, two graph replays with L2 flushed before each
+    (for a profiler: the second launch is the one to capture)."""
+    import torch
+
+    from cirrus_s_1a_b200 import synthetic
+    from cirrus_s_1a_b200.config import baseline_config
+    from cirrus_s_1a_b200.engine import CirrusB200
+
+    cfg = baseline_config()
+    eng = CirrusB200(cfg, synthetic.random_state_dict(cfg, seed=0), device="cuda:0", max_ctx=256)
+    g, n_mats, nbytes = weight_stream_kernel_graph(eng, M)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda:0")
+    for _ in range(2):
+        flush.random_(0, 255)
+        g.replay()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_stream": {"M": M, "matrices": n_mats, "bytes": nbytes}}), flush=True)
+
+
 def profile_step(B: int, T: int) -> None:
     """Two eager steps of B sequences x T tokens at ctx 32K (the batched
     workload), each inside an NVTX range 'step' (`ncu --nvtx --nvtx-include
@@ -545,6 +566,8 @@ def main() -> None:
                          "for a profiler's launch list, then exit")
     ap.add_argument("--trace-step", metavar="BxT", default=None,
                     help="print the persistent kernel's per-phase timing for B sequences x T tokens, then exit")
+    ap.add_argument("--profile-stream", metavar="M", type=int, default=None,
+                    help="run the one-launch weight stream twice with M input rows (for a profiler), then exit")
     ap.add_argument("--profile-prefill", metavar="BxP", default=None,
                     help="run a warm-up prefill and one prefill (B prompts of P tokens) inside an NVTX range "
                          "named 'prefill', then exit")
@@ -556,6 +579,9 @@ def main() -> None:
         return
     if args.trace_step:
         trace_step(*(int(v) for v in args.trace_step.lower().split("x")))
+        return
+    if args.profile_stream:
+        profile_stream(args.profile_stream)
         return
     if args.profile_prefill:
         profile_prefill(*(int(v) for v in args.profile_prefill.lower().split("x")))

@@ -24,6 +24,10 @@ constexpr int kStRing = 8;                       // tiles in flight per CTA
 constexpr int kStMaxK = 2048;
 constexpr int kStSlot = kTileRows * kStMaxK * 9 / 16;  // 18 KB: one tile of K = 2048
 constexpr int kStMaxMats = 128;
+// Staged input rows keep 16 bytes of padding after every 32 floats, so the
+// 128-bit loads of lanes 0-7 (8-float chunks 32 bytes apart) hit 32 distinct banks.
+__host__ __device__ inline int st_xpad(int K) { return K + K / 8; }
+__device__ __forceinline__ int st_xoff(int k) { return k + (k >> 5) * 4; }
 constexpr unsigned long long kStTimeoutNs = 200ull * 1000 * 1000;
 
 struct StreamMat {
@@ -82,7 +86,7 @@ template <int M>
 __global__ void __launch_bounds__(kStThreads, 1) weight_stream_kernel(const __grid_constant__ StreamParams p) {
   extern __shared__ __align__(128) uint8_t ssm[];
   uint8_t* ring = ssm;                                           // [kStRing][kStSlot]
-  float* xs = reinterpret_cast<float*>(ssm + kStRing * kStSlot);  // [M][kmax]
+  float* xs = reinterpret_cast<float*>(ssm + kStRing * kStSlot);  // [M][st_xpad(kmax)]
   __shared__ __align__(8) unsigned long long full[kStRing], empty[kStRing];
   __shared__ StreamMat mats[kStMaxMats];
   __shared__ int s_abort;
@@ -98,7 +102,7 @@ __global__ void __launch_bounds__(kStThreads, 1) weight_stream_kernel(const __gr
   }
   for (int i = tid; i < M * p.kmax; i += kStThreads) {
     const int m = i / p.kmax, k = i - m * p.kmax;
-    xs[i] = m < p.m_rows ? p.x[(int64_t)m * p.ldx + k] : 0.0f;
+    xs[m * st_xpad(p.kmax) + st_xoff(k)] = m < p.m_rows ? p.x[(int64_t)m * p.ldx + k] : 0.0f;
   }
   __syncthreads();
   const int n_mine = p.total_tiles > (int)blockIdx.x ? (p.total_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
@@ -154,8 +158,9 @@ __global__ void __launch_bounds__(kStThreads, 1) weight_stream_kernel(const __gr
         for (int j = 0; j < 4; ++j) f[j] = e2m1x2_to_f32x2(w >> (8 * j));
 #pragma unroll
         for (int m = 0; m < M; ++m) {
-          const float4 xa = *reinterpret_cast<const float4*>(xs + m * p.kmax + c * 8);
-          const float4 xb = *reinterpret_cast<const float4*>(xs + m * p.kmax + c * 8 + 4);
+          const float* xc = xs + m * st_xpad(p.kmax) + st_xoff(c * 8);
+          const float4 xa = *reinterpret_cast<const float4*>(xc);
+          const float4 xb = *reinterpret_cast<const float4*>(xc + 4);
           float d = f[0].x * xa.x;
           d = fmaf(f[0].y, xa.y, d);
           d = fmaf(f[1].x, xa.z, d);
@@ -227,12 +232,13 @@ extern "C" int cb_weight_stream_nvfp4(const void* plan, int32_t n_mats, int32_t 
     return CB_ERR_ARG;
   StreamParams p{static_cast<const StreamMat*>(plan), n_mats, total_tiles, x, ldx, m_rows, kmax, y, ldy, status};
   const int M = m_rows <= 1 ? 1 : m_rows <= 2 ? 2 : m_rows <= 4 ? 4 : 8;
-  const size_t smem = (size_t)kStRing * kStSlot + sizeof(float) * (size_t)M * kmax;
+  const size_t smem = (size_t)kStRing * kStSlot + sizeof(float) * (size_t)M * st_xpad(kmax);
   const void* fn = M == 1 ? (const void*)weight_stream_kernel<1>
                  : M == 2 ? (const void*)weight_stream_kernel<2>
                  : M == 4 ? (const void*)weight_stream_kernel<4>
                           : (const void*)weight_stream_kernel<8>;
-  if (ensure_smem_attr(fn, (int)((size_t)kStRing * kStSlot + sizeof(float) * 8 * kStMaxK)) != CB_OK) return CB_ERR_CUDA;
+  if (ensure_smem_attr(fn, (int)((size_t)kStRing * kStSlot + sizeof(float) * 8 * st_xpad(kStMaxK))) != CB_OK)
+    return CB_ERR_CUDA;
   void* args[] = {&p};
   const cudaError_t e = cudaLaunchKernel(fn, dim3(num_sms()), dim3(kStThreads), args, smem, (cudaStream_t)stream);
   count_launch();
